@@ -1,0 +1,102 @@
+// Shared helpers for the tesm_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string>
+
+#include "../../include/tesm_b200.h"
+
+namespace tesm {
+
+// ------------------------------------------------------------ host-side errors
+void set_error(const std::string &msg);
+int fail(int code, const std::string &msg);
+int check_launch(const char *what);
+
+#define TESM_REQUIRE(cond, msg)                                   \
+  do {                                                            \
+    if (!(cond)) return ::tesm::fail(TESM_EINVAL, (msg));         \
+  } while (0)
+
+inline int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+inline int64_t ceil_div(int64_t x, int64_t m) { return (x + m - 1) / m; }
+
+// ------------------------------------------------------------ device status
+// Sticky word set by device code when a bounded wait gives up (TESM_ETIMEOUT).
+// The library is built as one translation unit (tesm_b200.cu includes every .cu).
+__device__ int g_device_status = 0;
+
+__device__ __forceinline__ void flag_timeout() { atomicExch(&g_device_status, TESM_ETIMEOUT); }
+
+// ------------------------------------------------------------ element access
+__device__ __forceinline__ float load_f(const void *p, int dtype, int64_t i) {
+  return dtype == TESM_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i])
+                            : reinterpret_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ void store_f(void *p, int dtype, int64_t i, float v) {
+  if (dtype == TESM_BF16)
+    reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float *>(p)[i] = v;
+}
+
+// Round a float to the nearest bfloat16 value (ties to even) and return it as float.
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Round to the arithmetic precision of `dtype` (identity for fp32).
+__device__ __forceinline__ float round_to(int dtype, float v) { return dtype == TESM_BF16 ? round_bf16(v) : v; }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reductions for blockDim.x a multiple of 32 (<= 1024). `red` holds 32 slots.
+template <class T, class Op>
+__device__ __forceinline__ T block_reduce(T v, T *red, Op op, T init) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  T r = lane < nw ? red[lane] : init;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) r = op(r, __shfl_xor_sync(0xffffffffu, r, o));
+  return r;
+}
+
+// Bounded spin limit for device waits (~seconds at B200 clocks with backoff).
+constexpr long long kSpinLimit = 1ll << 26;
+
+}  // namespace tesm

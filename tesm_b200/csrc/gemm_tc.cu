@@ -1,0 +1,382 @@
+// Prefill-shaped int8 GEMM on the sm_100a tensor cores:
+//   D[m,n] = sum_k A[m,k] * B[n,k]      (A: activation codes, B: ternary weights, int32 exact)
+//   out[m,n] = D * inv_scale[m] * w_deq[n|0]
+//
+// Persistent, warp-specialised CTA (one per SM):
+//   warp 0     : TMA producer (one elected thread), 128-byte swizzled K-major tiles,
+//                STAGES-deep smem ring guarded by full/empty mbarriers;
+//   warp 1     : TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::i8,
+//                M=128 x N=BN x K=32 per instruction, accumulator in TMEM, double-buffered
+//                across output tiles so the epilogue of tile i overlaps the MMAs of tile i+1;
+//   warps 2..5 : epilogue: tcgen05.ld 32 lanes x 32 columns, scale, convert, store.
+// Every mbarrier wait is bounded; a wait that gives up sets the sticky device status
+// (TESM_ETIMEOUT) and the CTA drains and exits instead of hanging.
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+namespace tesm {
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // bytes (= int8 elements) per k-block: one 128B swizzle atom
+constexpr int STAGES = 4;
+constexpr int NUM_THREADS = 192;
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at B200 clocks
+
+struct Params {
+  const float *inv_scale;
+  const float *w_deq;
+  int per_row;
+  int M, N, K;
+  void *out;
+  int out_dtype;
+  int64_t ldo;
+  int32_t *acc_out;
+  int64_t ld_acc;
+  int num_m_tiles, num_n_tiles, num_k_blocks, group_m;
+  int vec_store;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)));
+}
+
+// Bounded parity wait. Returns false (after flagging the device status) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kWaitCycles) {
+      flag_timeout();
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major operand tile with 128-byte swizzle: 8-row atoms 1024 B apart (SBO), version 1.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void *p) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::i8 instruction descriptor: D s32, A/B signed int8, both K-major, M=128, N=BN.
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
+  const int per_group = p.group_m * p.num_n_tiles;
+  const int grp = t / per_group;
+  const int first_m = grp * p.group_m;
+  const int gm = min(p.num_m_tiles - first_m, p.group_m);
+  const int r = t - grp * per_group;
+  nt = r / gm;
+  mt = first_m + (r - nt * gm);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  constexpr int A_BYTES = BM * BK;
+  constexpr int B_BYTES = BN * BK;
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+  uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = bars + 2 * STAGES + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = p.num_m_tiles * p.num_n_tiles;
+  const int nk = p.num_k_blocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(BN);
+      uint32_t it = 0, tile_i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tile_i) {
+        const uint32_t buf = tile_i & 1, use = tile_i >> 1;
+        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1)) break;
+        fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
+          if (!mbar_wait(&full[stage], phase)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint64_t adesc = smem_desc_sw128(sA + stage * A_BYTES);
+          const uint64_t bdesc = smem_desc_sw128(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            // advance 32 bytes along K inside the swizzle atom: +2 in 16-byte units
+            mma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          }
+          mma_commit(&empty[stage]);
+        }
+        if (ok) mma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quarter q = warp % 4
+    const int q = warp & 3;
+    uint32_t tile_i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++tile_i) {
+      int mt, nt;
+      tile_coords(p, t, mt, nt);
+      const uint32_t buf = tile_i & 1, use = tile_i >> 1;
+      if (!mbar_wait(&tfull[buf], use & 1)) break;
+      fence_after();
+      const int row = mt * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const float xs = row_ok ? p.inv_scale[row] : 0.f;
+      const float wd0 = p.w_deq[0];
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32;
+        tmem_ld32(taddr, r);
+        const int n0 = nt * BN + c * 32;
+        if (!row_ok || n0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float wd = p.per_row ? (n0 + j < p.N ? p.w_deq[n0 + j] : 0.f) : wd0;
+          v[j] = (float)(int32_t)r[j] * xs * wd;
+        }
+        if (p.acc_out) {
+          int32_t *arow = p.acc_out + (int64_t)row * p.ld_acc;
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) arow[n0 + j] = (int32_t)r[j];
+        }
+        if (p.vec_store && n0 + 32 <= p.N) {
+          if (p.out_dtype == TESM_BF16) {
+            uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + (int64_t)row * p.ldo + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              __nv_bfloat162 h[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+              dst[j] = *reinterpret_cast<uint4 *>(h);
+            }
+          } else {
+            float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + (int64_t)row * p.ldo + n0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) store_f(p.out, p.out_dtype, (int64_t)row * p.ldo + n0 + j, v[j]);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor map: inner dim `inner` bytes, `outer` rows, row pitch `ld` bytes.
+static int make_map(CUtensorMap *map, const void *ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return fail(TESM_ELAUNCH, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TESM_EINVAL, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return TESM_OK;
+}
+
+template <int BN>
+static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, A, p.K, p.M, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, p.K, p.N, ldb, BN);
+  if (rc) return rc;
+  const size_t smem = 1024 + (size_t)STAGES * (BM * BK + BN * BK) + 256;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_i8<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  p.num_m_tiles = (int)ceil_div(p.M, BM);
+  p.num_n_tiles = (int)ceil_div(p.N, BN);
+  p.num_k_blocks = (int)ceil_div(p.K, BK);
+  p.group_m = 16;
+  const int total = p.num_m_tiles * p.num_n_tiles;
+  const int grid = total < sm_count() ? total : sm_count();
+  k_gemm_i8<BN><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
+  return check_launch("gemm_i8");
+}
+
+}  // namespace tc
+}  // namespace tesm
+
+using namespace tesm;
+
+extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
+                                 int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K,
+                                 void *out, int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc,
+                                 tesm_stream_t stream) {
+  TESM_REQUIRE(codes && inv_scale && tern && w_deq && out, "gemm_i8: null pointer");
+  TESM_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31), "gemm_i8: bad shape");
+  if (M == 0) return TESM_OK;
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8: out dtype");
+  TESM_REQUIRE(ld_codes >= K && ld_codes % 16 == 0 && ((uintptr_t)codes & 15) == 0,
+               "gemm_i8: codes rows must be 16-byte aligned with ld_codes >= K");
+  TESM_REQUIRE(ld_tern >= K && ld_tern % 16 == 0 && ((uintptr_t)tern & 15) == 0,
+               "gemm_i8: tern rows must be 16-byte aligned with ld_tern >= K");
+  TESM_REQUIRE(ldo >= N, "gemm_i8: ldo < N");
+  tc::Params p = {};
+  p.inv_scale = inv_scale;
+  p.w_deq = w_deq;
+  p.per_row = per_row;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.ldo = ldo;
+  p.acc_out = acc_out;
+  p.ld_acc = ld_acc;
+  const int esz = out_dtype == TESM_BF16 ? 2 : 4;
+  p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (N <= 128) return tc::launch<128>(codes, ld_codes, tern, ld_tern, p, st);
+  return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, st);
+}

@@ -1,0 +1,219 @@
+// Ternary weight quantisation + INT2 packing, and per-token int8 activation quantisation.
+//
+// Bit-exactness notes (reference: tesm_ssm/modules/tesm.py:206-215,
+// tesm_ssm/utils/int2_quantization.py:21-60):
+//  * torch evaluates `c / t` for a python scalar c as `t.reciprocal() * c`, i.e. two
+//    roundings in the tensor dtype; we use __frcp_rn then __fmul_rn (then bf16 RNE for
+//    bf16 tensors).
+//  * the product of two bf16 values is exact in fp32, so fp32 multiply followed by bf16
+//    RNE reproduces torch's bf16 multiply.
+//  * torch.round is round-half-to-even == rintf.
+// This file is compiled without fast-math; explicit _rn intrinsics keep it that way.
+#include "common.cuh"
+
+namespace tesm {
+
+// ---------------------------------------------------------------- weight scale
+// One warp per row: fp64 sum of |w| in a fixed order (deterministic).
+__global__ void k_row_abs_sum(const void *__restrict__ w, int dtype, int64_t N, int64_t K, int64_t ldw,
+                              double *__restrict__ row_sum) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= N) return;
+  double s = 0.0;
+  const int64_t base = row * ldw;
+  for (int64_t k = lane; k < K; k += 32) s += (double)fabsf(load_f(w, dtype, base + k));
+  s = warp_sum_d(s);
+  if (lane == 0) row_sum[row] = s;
+}
+
+__device__ __forceinline__ void scale_from_sum(double sum, double count, int dtype, float eps, float *scale,
+                                               float *deq) {
+  float m = (float)(sum / count);
+  m = round_to(dtype, fmaxf(m, eps));
+  float sc = round_to(dtype, __frcp_rn(m));  // 1.0 / t -> reciprocal * 1.0
+  *scale = sc;
+  *deq = round_to(dtype, __frcp_rn(sc));    // q / scale for q = +-1
+}
+
+// Per-tensor: one block sums the per-row partials in a fixed order.
+__global__ void k_tensor_scale(const double *__restrict__ row_sum, int64_t N, int64_t K, int dtype, float eps,
+                               float *scale, float *deq) {
+  __shared__ double red[32];
+  double s = 0.0;
+  for (int64_t r = threadIdx.x; r < N; r += blockDim.x) s += row_sum[r];
+  s = block_reduce(s, red, [](double a, double b) { return a + b; }, 0.0);
+  if (threadIdx.x == 0) scale_from_sum(s, (double)N * (double)K, dtype, eps, scale, deq);
+}
+
+__global__ void k_row_scale(const double *__restrict__ row_sum, int64_t N, int64_t K, int dtype, float eps,
+                            float *scale, float *deq) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < N) scale_from_sum(row_sum[r], (double)K, dtype, eps, scale + r, deq + r);
+}
+
+// ---------------------------------------------------------------- pack
+// One thread per 16-column group of a row: 16 ternary codes -> one 32-bit word of the
+// reference byte format (4 bytes, lowest column in the low bits) + 16 int8 values.
+__global__ void k_pack(const void *__restrict__ w, int dtype, int64_t N, int64_t K, int64_t ldw, int per_row,
+                       const float *__restrict__ scale, uint8_t *__restrict__ packed, int64_t ld_packed,
+                       int8_t *__restrict__ tern, int64_t ld_tern, int64_t groups_per_row) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= N * groups_per_row) return;
+  const int64_t row = gid / groups_per_row;
+  const int64_t grp = gid - row * groups_per_row;
+  const float sc = per_row ? scale[row] : scale[0];
+  uint32_t word = 0;
+  uint32_t tw[4] = {0, 0, 0, 0};
+  const int64_t k0 = grp * 16;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int64_t k = k0 + e;
+    int t = 0;
+    if (k < K) {
+      float v = round_to(dtype, __fmul_rn(load_f(w, dtype, row * ldw + k), sc));
+      v = rintf(v);
+      t = (int)fminf(fmaxf(v, -1.f), 1.f);
+    }
+    word |= (uint32_t)(t + 1) << (2 * e);
+    tw[e >> 2] |= ((uint32_t)(uint8_t)(int8_t)t) << (8 * (e & 3));
+  }
+  reinterpret_cast<uint32_t *>(packed + row * ld_packed)[grp] = word;
+  if (tern) {
+    uint4 v = make_uint4(tw[0], tw[1], tw[2], tw[3]);
+    reinterpret_cast<uint4 *>(tern + row * ld_tern)[grp] = v;
+  }
+}
+
+// ---------------------------------------------------------------- activation quant
+// One block per row; each thread owns up to GPT 16-element groups (kept in registers).
+// GEMV layout: natural column k = s*256 + tig*64 + u*16 + 4*i + sw is stored at
+// s*256 + u*64 + tig*16 + sw*4 + i (see gemv.cu for the consumer side).
+constexpr int kQuantGPT = 4;
+
+template <int GPT>
+__global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, int64_t ldx, float eps,
+                            int8_t *__restrict__ codes, int64_t ld_codes, int layout, int64_t groups_out,
+                            float *__restrict__ inv_scale, int32_t *__restrict__ rowsum) {
+  __shared__ float redf[32];
+  __shared__ int redi[32];
+  const int64_t row = blockIdx.x;
+  const int64_t groups_in = (K + 15) / 16;
+  float v[GPT][16];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int64_t k = g * 16 + e;
+      float xv = 0.f;
+      if (g < groups_in && k < K) xv = load_f(x, dtype, row * ldx + k);
+      v[j][e] = xv;
+      amax = fmaxf(amax, fabsf(xv));
+    }
+  }
+  amax = block_reduce(amax, redf, [](float a, float b) { return fmaxf(a, b); }, 0.f);
+  const float mx = round_to(dtype, fmaxf(amax, eps));
+  const float s = round_to(dtype, __fmul_rn(round_to(dtype, __frcp_rn(mx)), 127.f));
+  if (threadIdx.x == 0) inv_scale[row] = __frcp_rn(s);
+  int csum = 0;
+  int8_t *crow = codes + row * ld_codes;
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+    if (g >= groups_out) continue;
+    int c[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float p = rintf(round_to(dtype, __fmul_rn(v[j][e], s)));
+      c[e] = (int)fminf(fmaxf(p, -128.f), 127.f);
+      csum += c[e];
+    }
+    uint32_t wv[4];
+    if (layout == TESM_LAYOUT_GEMV) {
+      // word sw holds elements e = 4*i + sw in byte i
+#pragma unroll
+      for (int sw = 0; sw < 4; ++sw)
+        wv[sw] = (uint32_t)(uint8_t)c[sw] | ((uint32_t)(uint8_t)c[4 + sw] << 8) |
+                 ((uint32_t)(uint8_t)c[8 + sw] << 16) | ((uint32_t)(uint8_t)c[12 + sw] << 24);
+      const int64_t s256 = g >> 4, tig = (g >> 2) & 3, u = g & 3;
+      const int64_t slot = s256 * 16 + u * 4 + tig;
+      reinterpret_cast<uint4 *>(crow)[slot] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        wv[q] = (uint32_t)(uint8_t)c[4 * q] | ((uint32_t)(uint8_t)c[4 * q + 1] << 8) |
+                ((uint32_t)(uint8_t)c[4 * q + 2] << 16) | ((uint32_t)(uint8_t)c[4 * q + 3] << 24);
+      reinterpret_cast<uint4 *>(crow)[g] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  }
+  if (rowsum) {
+    csum = block_reduce(csum, redi, [](int a, int b) { return a + b; }, 0);
+    if (threadIdx.x == 0) rowsum[row] = csum;
+  }
+}
+
+}  // namespace tesm
+
+using namespace tesm;
+
+extern "C" int tesm_b200_weight_scale(const void *w, int dtype, int64_t N, int64_t K, int64_t ldw, int per_row,
+                                      float eps, float *scale, float *deq, double *work, tesm_stream_t stream) {
+  TESM_REQUIRE(w && scale && deq && work, "weight_scale: null pointer");
+  TESM_REQUIRE(N > 0 && K > 0 && ldw >= K, "weight_scale: bad shape");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "weight_scale: dtype must be f32 or bf16");
+  cudaStream_t st = (cudaStream_t)stream;
+  k_row_abs_sum<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(w, dtype, N, K, ldw, work);
+  if (per_row)
+    k_row_scale<<<(unsigned)ceil_div(N, 256), 256, 0, st>>>(work, N, K, dtype, eps, scale, deq);
+  else
+    k_tensor_scale<<<1, 1024, 0, st>>>(work, N, K, dtype, eps, scale, deq);
+  return check_launch("weight_scale");
+}
+
+extern "C" int tesm_b200_pack_ternary(const void *w, int dtype, int64_t N, int64_t K, int64_t ldw, int per_row,
+                                      const float *scale, uint8_t *packed, int64_t ld_packed, int8_t *tern,
+                                      int64_t ld_tern, tesm_stream_t stream) {
+  TESM_REQUIRE(w && scale && packed, "pack_ternary: null pointer");
+  TESM_REQUIRE(N > 0 && K > 0 && ldw >= K, "pack_ternary: bad shape");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "pack_ternary: dtype must be f32 or bf16");
+  const int64_t Kp = round_up(K, 256);
+  TESM_REQUIRE(ld_packed >= Kp / 4 && ld_packed % 4 == 0 && ((uintptr_t)packed & 3) == 0,
+               "pack_ternary: ld_packed must be >= ceil(K/256)*64 bytes, a multiple of 4, pointer 4-aligned");
+  if (tern)
+    TESM_REQUIRE(ld_tern >= Kp && ld_tern % 16 == 0 && ((uintptr_t)tern & 15) == 0,
+                 "pack_ternary: ld_tern must be >= K rounded up to 256, a multiple of 16, pointer 16-aligned");
+  const int64_t gpr = Kp / 16;
+  const int64_t total = N * gpr;
+  k_pack<<<(unsigned)ceil_div(total, 256), 256, 0, (cudaStream_t)stream>>>(w, dtype, N, K, ldw, per_row, scale,
+                                                                            packed, ld_packed, tern, ld_tern, gpr);
+  return check_launch("pack_ternary");
+}
+
+extern "C" int tesm_b200_quant_act(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
+                                   int8_t *codes, int64_t ld_codes, int layout, float *inv_scale, int32_t *rowsum,
+                                   tesm_stream_t stream) {
+  TESM_REQUIRE(x && codes && inv_scale, "quant_act: null pointer");
+  TESM_REQUIRE(M >= 0 && K > 0 && ldx >= K, "quant_act: bad shape");
+  if (M == 0) return TESM_OK;
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "quant_act: dtype must be f32 or bf16");
+  TESM_REQUIRE(((uintptr_t)codes & 15) == 0 && ld_codes % 16 == 0, "quant_act: codes must be 16-byte aligned rows");
+  int64_t groups_out;
+  if (layout == TESM_LAYOUT_GEMV) {
+    TESM_REQUIRE(rowsum != nullptr, "quant_act: GEMV layout needs rowsum");
+    groups_out = round_up(K, 256) / 16;
+    TESM_REQUIRE(ld_codes >= groups_out * 16, "quant_act: ld_codes < K rounded up to 256 for GEMV layout");
+  } else if (layout == TESM_LAYOUT_ROWMAJOR) {
+    groups_out = ceil_div(K, 16);
+    TESM_REQUIRE(ld_codes >= groups_out * 16, "quant_act: ld_codes < K rounded up to 16");
+  } else {
+    return fail(TESM_EINVAL, "quant_act: unknown layout");
+  }
+  int64_t threads = round_up(ceil_div(groups_out, kQuantGPT), 32);
+  if (threads < 32) threads = 32;
+  TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
+  k_quant_act<kQuantGPT><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
+      x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum);
+  return check_launch("quant_act");
+}

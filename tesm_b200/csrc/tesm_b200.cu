@@ -1,0 +1,6 @@
+// Unity build of libtesm_b200.so: one translation unit so that device globals shared
+// between kernels need no relocatable device code.
+#include "capi.cu"
+#include "quant.cu"
+#include "gemv.cu"
+#include "gemm_tc.cu"

@@ -1,0 +1,145 @@
+"""Torch-tensor wrappers over the C ABI (device memory, streams and shapes only).
+
+Every function here launches kernels from libtesm_b200.so on the current torch
+stream; none computes anything with torch ops.  Tensors must live on the CUDA
+device; ownership stays with torch.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+F32, BF16 = 0, 1
+LAYOUT_ROWMAJOR, LAYOUT_GEMV = 0, 1
+GEMV_MAX_M = 64
+
+_DT = {torch.float32: F32, torch.bfloat16: BF16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise _lib.TesmError(f"tesm_b200: unsupported dtype {dt} (float32 or bfloat16)") from None
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+@dataclass
+class PackedWeight:
+    """Device-resident ternary weight of one BitLinear.
+
+    packed: (N, Kp/4) uint8 in the reference INT2 byte format, Kp = K rounded up to 256
+    tern:   (N, Kp) int8 ternary values for the tensor-core path (None until needed)
+    scale:  (1,) or (N,) float32 quantisation scale 1/mean|W|
+    deq:    (1,) or (N,) float32 dequantisation factor fl(1/scale)
+    """
+    packed: torch.Tensor
+    tern: Optional[torch.Tensor]
+    scale: torch.Tensor
+    deq: torch.Tensor
+    N: int
+    K: int
+    per_row: bool
+
+
+def weight_scale(w: torch.Tensor, eps: float, per_row: bool = False, scale_out=None, deq_out=None):
+    N, K = w.shape
+    n = N if per_row else 1
+    scale = scale_out if scale_out is not None else torch.empty(n, device=w.device, dtype=torch.float32)
+    deq = deq_out if deq_out is not None else torch.empty(n, device=w.device, dtype=torch.float32)
+    work = torch.empty(N, device=w.device, dtype=torch.float64)
+    _lib.call("tesm_b200_weight_scale", w.data_ptr(), dtype_code(w.dtype), N, K, w.stride(0), int(per_row),
+              float(eps), scale.data_ptr(), deq.data_ptr(), work.data_ptr(), _stream())
+    return scale, deq
+
+
+def pack_weight(w: torch.Tensor, eps: float = 1e-5, per_row: bool = False, with_tern: bool = True,
+                scale: Optional[torch.Tensor] = None) -> PackedWeight:
+    """Ternarise and pack a (N, K) weight; ``scale`` overrides the computed 1/mean|W|."""
+    assert w.is_cuda and w.dim() == 2 and w.stride(1) == 1
+    N, K = w.shape
+    Kp = round_up(K, 256)
+    if scale is None:
+        scale, deq = weight_scale(w, eps, per_row)
+    else:
+        scale = scale.to(device=w.device, dtype=torch.float32).reshape(-1).contiguous()
+        deq = torch.reciprocal(scale)  # not used on the parity path
+    packed = torch.empty(N, Kp // 4, device=w.device, dtype=torch.uint8)
+    tern = torch.empty(N, Kp, device=w.device, dtype=torch.int8) if with_tern else None
+    _lib.call("tesm_b200_pack_ternary", w.data_ptr(), dtype_code(w.dtype), N, K, w.stride(0), int(per_row),
+              scale.data_ptr(), packed.data_ptr(), packed.stride(0), _ptr(tern), Kp if tern is not None else 0,
+              _stream())
+    return PackedWeight(packed, tern, scale, deq, N, K, per_row)
+
+
+def ensure_tern(pw: PackedWeight, w: torch.Tensor):
+    if pw.tern is None:
+        Kp = round_up(pw.K, 256)
+        tern = torch.empty(pw.N, Kp, device=w.device, dtype=torch.int8)
+        scratch = torch.empty_like(pw.packed)
+        _lib.call("tesm_b200_pack_ternary", w.data_ptr(), dtype_code(w.dtype), pw.N, pw.K, w.stride(0),
+                  int(pw.per_row), pw.scale.data_ptr(), scratch.data_ptr(), scratch.stride(0), tern.data_ptr(), Kp,
+                  _stream())
+        pw.tern = tern
+    return pw.tern
+
+
+def quant_act(x2d: torch.Tensor, eps: float, layout: int):
+    """Per-row int8 codes of a (M, K) activation (row stride may exceed K)."""
+    assert x2d.is_cuda and x2d.dim() == 2 and x2d.stride(1) == 1
+    M, K = x2d.shape
+    ld = round_up(K, 256) if layout == LAYOUT_GEMV else round_up(K, 16)
+    codes = torch.empty(M, ld, device=x2d.device, dtype=torch.int8)
+    inv = torch.empty(M, device=x2d.device, dtype=torch.float32)
+    rowsum = torch.empty(M, device=x2d.device, dtype=torch.int32) if layout == LAYOUT_GEMV else None
+    _lib.call("tesm_b200_quant_act", x2d.data_ptr(), dtype_code(x2d.dtype), M, K, x2d.stride(0), float(eps),
+              codes.data_ptr(), ld, layout, inv.data_ptr(), _ptr(rowsum), _stream())
+    return codes, inv, rowsum
+
+
+def gemv(codes, inv, rowsum, pw: PackedWeight, M: int, out_dtype: torch.dtype, out=None, acc=False):
+    dev = codes.device
+    out = out if out is not None else torch.empty(M, pw.N, device=dev, dtype=out_dtype)
+    accb = torch.empty(M, pw.N, device=dev, dtype=torch.int32) if acc else None
+    _lib.call("tesm_b200_gemv_int2", codes.data_ptr(), codes.stride(0), inv.data_ptr(), rowsum.data_ptr(),
+              pw.packed.data_ptr(), pw.packed.stride(0), pw.deq.data_ptr(), int(pw.per_row), M, pw.N, pw.K,
+              out.data_ptr(), dtype_code(out.dtype), out.stride(0), _ptr(accb), pw.N, _stream())
+    return (out, accb) if acc else out
+
+
+def gemm(codes, inv, pw: PackedWeight, M: int, out_dtype: torch.dtype, out=None, acc=False):
+    dev = codes.device
+    out = out if out is not None else torch.empty(M, pw.N, device=dev, dtype=out_dtype)
+    accb = torch.empty(M, pw.N, device=dev, dtype=torch.int32) if acc else None
+    _lib.call("tesm_b200_gemm_i8", codes.data_ptr(), codes.stride(0), inv.data_ptr(), pw.tern.data_ptr(),
+              pw.tern.stride(0), pw.deq.data_ptr(), int(pw.per_row), M, pw.N, pw.K, out.data_ptr(),
+              dtype_code(out.dtype), out.stride(0), _ptr(accb), pw.N, _stream())
+    return (out, accb) if acc else out
+
+
+def bitlinear_2d(x2d: torch.Tensor, pw: PackedWeight, eps: float, out_dtype=None, out=None, acc=False,
+                 force: Optional[str] = None):
+    """Quantise a (M, K) activation and multiply by a packed ternary weight."""
+    M = x2d.shape[0]
+    out_dtype = out_dtype or x2d.dtype
+    path = force or ("gemv" if M <= GEMV_MAX_M else "gemm")
+    if path == "gemv":
+        codes, inv, rowsum = quant_act(x2d, eps, LAYOUT_GEMV)
+        return gemv(codes, inv, rowsum, pw, M, out_dtype, out, acc)
+    codes, inv, _ = quant_act(x2d, eps, LAYOUT_ROWMAJOR)
+    return gemm(codes, inv, pw, M, out_dtype, out, acc)

@@ -1,0 +1,162 @@
+"""Generate golden vectors by running the reference torch backend.
+
+Run where the reference package is importable (``TESM_REFERENCE`` points at the
+project root, default ``/root/reference``):
+
+    python tests/golden/gen_golden.py
+
+Every case seeds weights with ``torch.manual_seed(0)`` before constructing the
+reference module (the b200 mirror modules reproduce the same parameters from the
+same seed; ``tests/test_oracle_golden.py`` checks that here) and draws inputs from
+``torch.Generator().manual_seed(1)``.  Modules run in ``.eval()`` under
+``torch.no_grad()`` with ``kernel_backend="torch"`` in float32 -- the reference's
+torch path raises for bfloat16 SISO/MIMO modules (tesm.py:944 einsum dtype
+mismatch), so module parity is pinned in float32.  The saved ``.npz`` files hold
+inputs' seeds/shapes, outputs, and a SHA-256 of the reference state_dict.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("TESM_REFERENCE", "/root/reference")
+sys.path.insert(0, REF)
+
+from tesm_ssm.modules.tesm import BitLinear, TESM_SISO  # noqa: E402
+from tesm_ssm.modules.tesm_mimo import TESMMIMO_Optimized  # noqa: E402
+from tesm_ssm.models.config_tesm import TESMConfig  # noqa: E402
+from tesm_ssm.models.mixer_seq_simple import TESMLMHeadModel  # noqa: E402
+from tesm_ssm.utils.int2_quantization import pack_int2_to_uint8  # noqa: E402
+
+import cases  # noqa: E402  (shared case table; no reference import inside)
+
+
+def sd_hash(module):
+    h = hashlib.sha256()
+    for k, v in module.state_dict().items():
+        h.update(k.encode())
+        h.update(v.detach().cpu().contiguous().numpy().tobytes())
+    return h.hexdigest()
+
+
+def randn(shape, seed, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(dtype)
+
+
+def save(name, **arrays):
+    path = os.path.join(HERE, name + ".npz")
+    np.savez_compressed(path, **{k: np.asarray(v) for k, v in arrays.items()})
+    print("wrote", path, os.path.getsize(path), "bytes")
+
+
+def t2n(t):
+    return t.detach().cpu().numpy().copy()  # copy: reference caches alias their inputs
+
+
+def gen_bitlinear():
+    for c in cases.BITLINEAR:
+        torch.manual_seed(0)
+        dt = getattr(torch, c["dtype"])
+        lay = BitLinear(c["K"], c["N"], kernel_backend="torch")
+        with torch.no_grad():
+            lay.weight.copy_(randn((c["N"], c["K"]), 3) * c["wstd"])
+        lay = lay.to(dt).eval()
+        x = randn(c["xshape"], 1, dt)
+        with torch.no_grad():
+            y = lay(x)
+            qw = lay.quantized_weight()
+            scale = 1.0 / lay.weight.abs().mean().clamp_min(lay.bit_eps)
+            t = (lay.weight * scale).round().clamp(-1, 1).to(torch.int8)
+            sx = 127 / x.abs().max(dim=-1, keepdim=True).values.clamp_min(lay.bit_eps)
+            codes = (x * sx).round().clamp(-128, 127).to(torch.int8)
+            acc = codes.reshape(-1, c["K"]).int() @ t.int().T
+            packed, pscale = pack_int2_to_uint8(lay.weight.float())
+        save("bitlinear_" + c["name"], y=t2n(y.float()), t=t2n(t), scale=t2n(scale.float()),
+             deq=t2n(qw.float().abs().max()), codes=t2n(codes), sx=t2n(sx.float()), acc=t2n(acc),
+             packed=t2n(packed), pscale=t2n(pscale.float()))
+
+
+def run_siso(c):
+    torch.manual_seed(0)
+    m = TESM_SISO(kernel_backend="torch", **c["kw"]).eval()
+    out = {"sd_sha256": sd_hash(m)}
+    B, L = c["B"], c["L"]
+    x = randn((B, L, c["kw"]["d_model"]), 1)
+    cross = randn((B, L, c["kw"]["d_state"]), 2) if c.get("cross") else None
+    prev = randn((B, c["kw"]["d_state"]), 4).double() if c.get("prev") else None
+    ip = {"state_cache": m.allocate_inference_cache(B, c["kw"]["max_seq_len"])} if c.get("decode") else None
+    with torch.no_grad():
+        y, fs = m(x, inference_params=({"state_cache": ip["state_cache"]} if ip else None),
+                  cross_layer_state=cross, prev_state=prev)
+        out.update(y=t2n(y), final=t2n(fs), states=t2n(m._last_cross_layer_state))
+        for s in range(c.get("decode", 0)):
+            xt = randn((B, 1, c["kw"]["d_model"]), 10 + s)
+            ct = randn((B, c["kw"]["d_state"]), 20 + s) if c.get("cross") else None
+            yt, st = m(xt, inference_params={"state_cache": ip["state_cache"]}, cross_layer_state=ct)
+            out[f"dec{s}_y"] = t2n(yt)
+            out[f"dec{s}_state"] = t2n(st)
+        if ip:
+            ch = ip["state_cache"]
+            out.update(cache_k=t2n(ch["ent_k_cache"]), cache_v=t2n(ch["ent_v_cache"]),
+                       cache_idx=np.int64(ch["cache_idx"]), cache_pos=np.int64(ch["seq_pos"]))
+    save("siso_" + c["name"], **out)
+
+
+def run_mimo(c):
+    torch.manual_seed(0)
+    m = TESMMIMO_Optimized(kernel_backend="torch", **c["kw"]).eval()
+    out = {"sd_sha256": sd_hash(m)}
+    B, L = c["B"], c["L"]
+    H, D = c["kw"]["n_heads"], c["kw"]["d_state"]
+    x = randn((B, L, c["kw"]["d_model"]), 1)
+    ip = {"state_cache": m.allocate_inference_cache(B, c["kw"]["max_seq_len"])} if c.get("decode") else None
+    with torch.no_grad():
+        y, fs = m(x, inference_params=({"state_cache": ip["state_cache"]} if ip else None))
+        out.update(y=t2n(y), final=t2n(fs), cross=t2n(m._last_cross_layer_state))
+        for s in range(c.get("decode", 0)):
+            xt = randn((B, 1, c["kw"]["d_model"]), 10 + s)
+            ct = randn((B, H, D), 20 + s) if c.get("cross") else None
+            yt, st = m(xt, inference_params={"state_cache": ip["state_cache"]}, cross_layer_state=ct)
+            out[f"dec{s}_y"] = t2n(yt)
+            out[f"dec{s}_state"] = t2n(st)
+    save("mimo_" + c["name"], **out)
+
+
+def run_model(c):
+    torch.manual_seed(0)
+    cfg = TESMConfig(kernel_backend="torch", **c["cfg"])
+    m = TESMLMHeadModel(cfg).eval()
+    out = {"sd_sha256": sd_hash(m)}
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (c["B"], c["L"]), generator=g)
+    out["ids"] = t2n(ids)
+    with torch.no_grad():
+        o, _ = m(ids)
+        out["logits"] = t2n(o.logits)
+        if c.get("decode"):
+            ip = {"state_cache": m.backbone.allocate_inference_cache(c["B"], cfg.max_seq_len)}
+            o, _ = m(ids, inference_params=ip)
+            out["prefill_logits"] = t2n(o.logits)
+            for s in range(c["decode"]):
+                nt = torch.randint(0, cfg.vocab_size, (c["B"], 1), generator=g)
+                o, _ = m(nt, inference_params=ip)
+                out[f"dec{s}_ids"] = t2n(nt)
+                out[f"dec{s}_logits"] = t2n(o.logits)
+    save("model_" + c["name"], **out)
+
+
+if __name__ == "__main__":
+    torch.set_num_threads(8)
+    gen_bitlinear()
+    for c in cases.SISO:
+        run_siso(c)
+    for c in cases.MIMO:
+        run_mimo(c)
+    for c in cases.MODEL:
+        run_model(c)
