@@ -91,6 +91,96 @@ int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_sc
                       int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K, void *out,
                       int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc, tesm_stream_t stream);
 
+/* ---------------------------------------------------------------- TESM layer (prefill)
+ * `proj` is the in_proj output (B*L rows, row stride ldp elements, dtype TESM_F32/BF16) with the
+ * reference column split [local Dm | value C | decay C | write C | gate Dm | q Rc | k Rc]
+ * (tesm.py:1195-1205; MIMO tesm_mimo.py:940-956 with C = H*D, Rc = H*R, head-major).
+ *
+ * Selective state scan (replaces TESM_SISO._parallel_state_scan, tesm.py:1091-1164; MIMO
+ * _parallel_state_scan_mimo, tesm_mimo.py:281-392): a = sigmoid(decay + decay_bias),
+ * u = sigmoid(write)*tanh(value) (MIMO: u_r = (write*x_r)*(value*x_r), x = mimo_x[h,r,:]),
+ * h_t = a_t h_{t-1} + u_t.  states: (B, L, RM, C) fp32; final_*: rank-0 state at t = L-1.
+ * h0 (nullable, SISO only): prev_state (B, D) fp64.  workspace: caller-owned device
+ * memory of at least tesm_b200_scan_workspace() bytes (look-back aggregates and flags). */
+int tesm_b200_scan_workspace(int64_t B, int64_t L, int64_t C, int64_t RM, int64_t *bytes);
+int tesm_b200_siso_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t D,
+                        int64_t R, const float *decay_bias, const double *h0, float *states, float *final_f32,
+                        double *final_f64, void *workspace, int64_t ws_bytes, tesm_stream_t stream);
+int tesm_b200_mimo_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t H,
+                        int64_t D, int64_t R, int64_t RM, const float *decay_bias, const float *mimo_x,
+                        float *states, float *final_f32, double *final_f64, void *workspace, int64_t ws_bytes,
+                        tesm_stream_t stream);
+
+/* Local (sliding-window) ternary entanglement + lerp (replaces _compute_local_entanglement,
+ * tesm.py:853-952, and the lerp :1231-1232).  q, k are read from proj with RoPE applied on the
+ * fly; cross (nullable, (B*L, R) fp32) is the cross-layer q bias.  Outputs (B*L, D):
+ * out_tanh = tanh(ent), out_chg = ent - states, ent = s + es*(avg - s).  W in {4,8,16,32}. */
+int tesm_b200_siso_local_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                             int64_t D, int64_t R, int64_t W, const float *cross, const float *bias,
+                             const float *states, float thr, float es, float rope_base, void *out_tanh,
+                             void *out_chg, int out_dtype, tesm_stream_t stream);
+
+/* Relative-position bias vector of global entanglement (tesm.py:970-982), length 2L-1,
+ * entry d + L - 1 for d = i - j. */
+int tesm_b200_global_relbias(const float *embed, int64_t dim, float scale, float bias0, int64_t L, float *out,
+                             tesm_stream_t stream);
+
+/* Causal global ternary entanglement + lerp (replaces _compute_entanglement's global rung,
+ * tesm.py:963-1043); same outputs as tesm_b200_siso_local_ent. */
+int tesm_b200_siso_global_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                              int64_t D, int64_t R, const float *cross, const float *relb, const float *states,
+                              float thr, float es, float rope_base, void *out_tanh, void *out_chg, int out_dtype,
+                              tesm_stream_t stream);
+
+/* MIMO local entanglement with the rank merge (replaces _compute_local_entanglement_mimo and the
+ * mimo_o merge, tesm_mimo.py:394-588, :996-1017): out_tanh = tanh(sum_r mo_r*ent_r),
+ * out_chg = sum_r mo_r*(ent_r - s_r), (B*L, H*D).  quirk != 0 keeps the reference's window
+ * truncation for t < W-1.  (W, RM) in {8,16} x {1,2,4}. */
+int tesm_b200_mimo_local_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t H,
+                             int64_t D, int64_t R, int64_t RM, int64_t W, const float *bias, const float *mimo_o,
+                             const float *states, float thr, float es, float rope_base, int quirk, void *out_tanh,
+                             void *out_chg, int out_dtype, tesm_stream_t stream);
+
+/* Output combine y = local + sigmoid(gate) * sp + ep (tesm.py:1256-1260); sp, ep: (M, Dm). */
+int tesm_b200_combine(const void *proj, int dtype, int64_t ldp, int64_t M, int64_t Dm, int64_t D, int64_t R,
+                      const void *sp, const void *ep, int sdtype, void *y, int ydtype, tesm_stream_t stream);
+
+/* ---------------------------------------------------------------- decode cache
+ * Prefill -> cache (tesm.py:1235-1253; MIMO rank 0, tesm_mimo.py:1022-1038): rope(k) and states
+ * of the last min(L, W) positions into k_cache (B, W, H, R) / v_cache (B, W, H, D), state (B, H, D)
+ * fp64 <- final_f64, ctl = {L, 0, 0}. */
+int tesm_b200_cache_fill(const void *proj, int dtype, int64_t ldp, const float *states, int64_t RM, int64_t B,
+                         int64_t L, int64_t Dm, int64_t H, int64_t D, int64_t R, int64_t W, float rope_base,
+                         const double *final_f64, double *state, float *k_cache, float *v_cache, int *ctl,
+                         tesm_stream_t stream);
+
+/* One-token step (replaces TESM_SISO._forward_incremental, tesm.py:1274-1381, and the MIMO one,
+ * tesm_mimo.py:753-894; H = 1 for SISO): fp64 state update, ring write at ctl[1], the reference's
+ * window order and bias alignment, ternary average and lerp -> out_tanh / out_chg (B, H*D);
+ * new_state (nullable) gets the fp32 state; ctl = {seq_pos, cache_idx, 0} is advanced on device. */
+int tesm_b200_decode_step(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t Dm, int64_t H, int64_t D,
+                          int64_t R, int64_t W, const float *decay_bias, const float *bias, const float *cross,
+                          double *state, float *k_cache, float *v_cache, int *ctl, float thr, float es,
+                          float rope_base, void *out_tanh, void *out_chg, int out_dtype, float *new_state,
+                          tesm_stream_t stream);
+
+/* ---------------------------------------------------------------- model glue
+ * Embedding + learned positions (mixer_seq_simple.py:183-184); position offset from pos_dev[0]
+ * when non-null (graph replay), else pos_host. */
+int tesm_b200_embed(const int64_t *ids, int64_t B, int64_t L, const void *emb, const void *pos_emb, int wdtype,
+                    int64_t Dm, const int *pos_dev, int64_t pos_host, void *out, int odtype, tesm_stream_t stream);
+
+/* Block pre-norm fused with the next BitLinear's activation quantisation (block.py:28-45):
+ * residual_out = x + residual (fp32; residual nullable), y = RMSNorm(residual_out) * weight,
+ * codes/inv_scale/rowsum as tesm_b200_quant_act (codes nullable: norm only); y_out nullable. */
+int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const float *residual, float *residual_out,
+                                const float *weight, float eps, int64_t M, int64_t K, float qeps, int8_t *codes,
+                                int64_t ld_codes, int layout, float *inv_scale, int32_t *rowsum, void *y_out,
+                                int ydtype, tesm_stream_t stream);
+
+/* FeedForward gate: out[m, f] = silu(gu[m, f]) * gu[m, F + f] (mixer_seq_simple.py:59-66). */
+int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, void *out, int odtype, tesm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

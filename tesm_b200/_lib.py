@@ -33,6 +33,27 @@ SIGNATURES = {
                             c_i64, c_vp, c_i64, c_vp],
     "tesm_b200_gemm_i8": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
                           c_vp, c_i64, c_vp],
+    "tesm_b200_scan_workspace": [c_i64, c_i64, c_i64, c_i64, c_vp],
+    "tesm_b200_siso_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,
+                            c_vp, c_i64, c_vp],
+    "tesm_b200_mimo_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                            c_vp, c_vp, c_vp, c_i64, c_vp],
+    "tesm_b200_siso_local_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                                 c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp],
+    "tesm_b200_global_relbias": [c_vp, c_i64, c_float, c_float, c_i64, c_vp, c_vp],
+    "tesm_b200_siso_global_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                                  c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp],
+    "tesm_b200_mimo_local_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp,
+                                 c_vp, c_vp, c_float, c_float, c_float, c_int, c_vp, c_vp, c_int, c_vp],
+    "tesm_b200_combine": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_int, c_vp],
+    "tesm_b200_cache_fill": [c_vp, c_int, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                             c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "tesm_b200_decode_step": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                              c_vp, c_vp, c_vp, c_vp, c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp, c_vp],
+    "tesm_b200_embed": [c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_i64, c_vp, c_i64, c_vp, c_int, c_vp],
+    "tesm_b200_add_rmsnorm_quant": [c_vp, c_int, c_vp, c_vp, c_vp, c_float, c_i64, c_i64, c_float, c_vp, c_i64,
+                                    c_int, c_vp, c_vp, c_vp, c_int, c_vp],
+    "tesm_b200_silu_mul": [c_vp, c_int, c_i64, c_i64, c_vp, c_int, c_vp],
 }
 _RESTYPES = {"tesm_b200_last_error": ctypes.c_char_p}
 

@@ -1,0 +1,155 @@
+// One-token incremental step of a TESM layer against its recurrent-state cache.
+// SISO: TESM_SISO._forward_incremental (tesm.py:1274-1400); MIMO (H heads, no rank mixing):
+// TESMMIMO_Optimized._forward_incremental (tesm_mimo.py:753-912).
+//
+//  * new_state = a * state + w * tanh(v) in fp64, state kept in fp64 like the reference;
+//  * ring write of (rope(k), new_state as fp32) at slot cache_idx, then cache_idx advances;
+//  * window order follows the reference exactly: a full window is gathered from slot
+//    cache_idx (the entry just written) onward with bias[w]; a partial window reads slots
+//    [0, valid) with bias[W - valid + w];
+//  * ternary, normalised signed average, lerp -> tanh(ent) and ent - new_state.
+// seq_pos / cache_idx live in a device int pair so a captured CUDA graph can replay steps;
+// the last CTA to finish advances them (every CTA reads them before it increments the
+// completion counter, so no CTA can observe the advanced values).
+#include "layer_common.cuh"
+
+namespace tesm {
+
+struct DecodeParams {
+  ProjCols pc;                // (B, Nproj)
+  const float *decay_bias;    // (H*D)
+  const float *bias;          // (H, W)
+  const float *cross;         // (B, H*R) or null
+  double *state;              // (B, H, D)
+  float *kc;                  // (B, W, H, R)
+  float *vc;                  // (B, W, H, D)
+  int *ctl;                   // [seq_pos, cache_idx, done_counter]
+  int B, H, D, R, W;
+  float thr, es, sqrt_r, rope_base;
+  void *out_tanh, *out_chg;   // (B, H*D)
+  int out_dtype;
+  float *new_state;           // (B, H*D) fp32 (cross-layer state for the next layer)
+};
+
+__global__ void k_decode_step(DecodeParams p) {
+  extern __shared__ float sm[];
+  const int R = p.R, W = p.W, D = p.D, H = p.H;
+  float *q = sm;             // R
+  float *k = q + R;          // R
+  float *tw = k + R;         // W weights (ternary / norm)
+  int *slot = reinterpret_cast<int *>(tw + W);  // W
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int pos = p.ctl[0], idx = p.ctl[1];
+  const int valid = min(pos + 1, W);
+  const int64_t row = b;
+  const int C = H * D;
+  const int tid = threadIdx.x;
+  load_rope_row(q, p.pc, p.pc.c_q + h * R, row, R, pos, p.rope_base, p.cross ? p.cross + row * H * R + h * R : nullptr,
+                tid, blockDim.x);
+  load_rope_row(k, p.pc, p.pc.c_k + h * R, row, R, pos, p.rope_base, nullptr, tid, blockDim.x);
+  __syncthreads();
+  float *kslot = p.kc + (((int64_t)b * W + idx) * H + h) * R;
+  for (int i = tid; i < R; i += blockDim.x) kslot[i] = k[i];
+  double newd = 0.0;
+  for (int d = tid; d < D; d += blockDim.x) {  // blockDim >= D
+    const int c = h * D + d;
+    const float a = sigmoidf_(load_f(p.pc.proj, p.pc.dtype, row * p.pc.ld + p.pc.c_decay + c) + p.decay_bias[c]);
+    const float w = sigmoidf_(load_f(p.pc.proj, p.pc.dtype, row * p.pc.ld + p.pc.c_write + c));
+    const float v = tanhf(load_f(p.pc.proj, p.pc.dtype, row * p.pc.ld + p.pc.c_value + c));
+    const int64_t si = ((int64_t)b * H + h) * D + d;
+    newd = (double)a * p.state[si] + (double)w * (double)v;
+    p.vc[(((int64_t)b * W + idx) * H + h) * D + d] = (float)newd;
+  }
+  __syncthreads();  // the slot just written is read back below
+  // window scores: warp 0 (W <= 32)
+  if (tid < 32) {
+    float tv = 0.f;
+    int s = 0;
+    for (int w = 0; w < valid; ++w) {
+      const int sl = valid >= W ? (idx + w) % W : w;
+      const int bi = valid >= W ? w : W - valid + w;
+      const float *kr = p.kc + (((int64_t)b * W + sl) * H + h) * R;
+      float part = 0.f;
+      for (int i = tid; i < R; i += 32) part = fmaf(q[i], kr[i], part);
+      part = warp_sum(part);
+      const float t = ternary_of(__fdiv_rn(part, p.sqrt_r) + p.bias[h * W + bi], p.thr);
+      if (tid == w) {
+        tv = t;
+        s = sl;
+      }
+    }
+    float cnt = fabsf(tid < valid ? tv : 0.f);
+    cnt = warp_sum(cnt);
+    if (tid < W) {
+      tw[tid] = tid < valid ? tv / fmaxf(cnt, 1.f) : 0.f;
+      slot[tid] = tid < valid ? s : 0;
+    }
+  }
+  __syncthreads();
+  for (int d = tid; d < D; d += blockDim.x) {
+    const int c = h * D + d;
+    const float ns = (float)newd;
+    float avg = 0.f;
+    for (int w = 0; w < valid; ++w) avg = fmaf(tw[w], p.vc[(((int64_t)b * W + slot[w]) * H + h) * D + d], avg);
+    const float ent = ns + p.es * (avg - ns);
+    store_f(p.out_tanh, p.out_dtype, row * C + c, tanhf(ent));
+    store_f(p.out_chg, p.out_dtype, row * C + c, ent - ns);
+    p.state[((int64_t)b * H + h) * D + d] = newd;
+    if (p.new_state) p.new_state[row * C + c] = ns;
+  }
+  // completion: the last CTA advances (seq_pos, cache_idx)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const int done = atomicAdd(&p.ctl[2], 1);
+    if (done == (int)(gridDim.x * gridDim.y) - 1) {
+      p.ctl[0] = pos + 1;
+      p.ctl[1] = (idx + 1) % W;
+      p.ctl[2] = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace tesm
+
+using namespace tesm;
+
+extern "C" int tesm_b200_decode_step(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t Dm, int64_t H,
+                                     int64_t D, int64_t R, int64_t W, const float *decay_bias, const float *bias,
+                                     const float *cross, double *state, float *k_cache, float *v_cache, int *ctl,
+                                     float thr, float es, float rope_base, void *out_tanh, void *out_chg,
+                                     int out_dtype, float *new_state, tesm_stream_t stream) {
+  TESM_REQUIRE(proj && decay_bias && bias && state && k_cache && v_cache && ctl && out_tanh && out_chg,
+               "decode_step: null pointer");
+  TESM_REQUIRE(B > 0 && H > 0 && D > 0 && D <= 1024 && R > 0 && R % 2 == 0 && W > 0 && W <= 32,
+               "decode_step: bad shape (D <= 1024, W <= 32, even R)");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "decode_step: dtype");
+  DecodeParams p;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)(H * D), (int)(H * R));
+  p.decay_bias = decay_bias;
+  p.bias = bias;
+  p.cross = cross;
+  p.state = state;
+  p.kc = k_cache;
+  p.vc = v_cache;
+  p.ctl = ctl;
+  p.B = (int)B;
+  p.H = (int)H;
+  p.D = (int)D;
+  p.R = (int)R;
+  p.W = (int)W;
+  p.thr = thr;
+  p.es = es;
+  p.sqrt_r = (float)sqrt((double)R);
+  p.rope_base = rope_base;
+  p.out_tanh = out_tanh;
+  p.out_chg = out_chg;
+  p.out_dtype = out_dtype;
+  p.new_state = new_state;
+  const int threads = (int)round_up(D < 32 ? 32 : D, 32);
+  const size_t smem = sizeof(float) * (2 * R + W) + sizeof(int) * W;
+  dim3 grid((unsigned)H, (unsigned)B);
+  k_decode_step<<<grid, threads, smem, (cudaStream_t)stream>>>(p);
+  return check_launch("decode_step");
+}

@@ -1,0 +1,276 @@
+// Selective state scan h_t = a_t * h_{t-1} + u_t for SISO and MIMO layers.
+//
+//   SISO (tesm.py:1198-1223, scan :1091-1164): a = sigmoid(decay + decay_bias),
+//        u = sigmoid(write) * tanh(value); the reference scans in fp64 chunks, here fp32 FMA in
+//        time order (relative error ~1e-6, within the 1e-3 fp32 bar).
+//   MIMO (tesm_mimo.py:959-989, scan :375-392): ranks r share a; u_r = (write*x_r)*(value*x_r)
+//        with x_r = mimo_x[h, r, :]; the reference scans in fp32 with separate mul/add roundings,
+//        reproduced with __fmul_rn/__fadd_rn.
+//
+// Parallel structure: one thread per channel (all ranks of that channel), chunks of T
+// positions; the chunks of a (batch, channel-slice) chain exchange carries by decoupled
+// look-back.  Each chunk publishes its aggregate affine map (A, U_r) as soon as its first pass
+// is done, then its inclusive states once its carry-in is known; successors fold aggregates
+// until they meet an inclusive value.  Chunk order comes from an atomic ticket, so a chunk only
+// ever waits on chunks that are already running -- no deadlock regardless of launch order.
+// The wait is bounded (~2 s); on timeout the sticky device status is set.
+#include "layer_common.cuh"
+
+namespace tesm {
+
+struct ScanParams {
+  ProjCols pc;
+  const float *decay_bias;  // (C)
+  const float *mimo_x;      // (H, RM, D) or null (SISO)
+  const double *h0;         // (B, C) or null
+  int B, L, C, D, RM;
+  int T, nchunks, nslices;
+  float *states;            // (B, L, RM, C)
+  float *final_f32;         // (B, C) rank 0
+  double *final_f64;        // (B, C) rank 0
+  float *aggA;              // (B, nchunks, C)
+  float *aggU;              // (B, nchunks, RM, C)
+  float *incl;              // (B, nchunks, RM, C)
+  int *flags;               // (B, nslices, nchunks)
+  int *ticket;
+};
+
+template <int RM, bool MIMO>
+__device__ __forceinline__ void scan_inputs(const ScanParams &p, int64_t row, int c, float db, const float (&mx)[RM],
+                                            float &a, float (&u)[RM]) {
+  const int64_t base = row * p.pc.ld;
+  const float dr = load_f(p.pc.proj, p.pc.dtype, base + p.pc.c_decay + c);
+  const float wr = load_f(p.pc.proj, p.pc.dtype, base + p.pc.c_write + c);
+  const float vr = load_f(p.pc.proj, p.pc.dtype, base + p.pc.c_value + c);
+  a = sigmoidf_(dr + db);
+  const float w = sigmoidf_(wr), v = tanhf(vr);
+  if (MIMO) {
+#pragma unroll
+    for (int r = 0; r < RM; ++r) u[r] = __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r]));
+  } else {
+    u[0] = w * v;
+  }
+}
+
+template <bool MIMO>
+__device__ __forceinline__ float step(float a, float h, float u) {
+  return MIMO ? __fadd_rn(__fmul_rn(a, h), u) : fmaf(a, h, u);
+}
+
+template <int RM, bool MIMO>
+__global__ void k_scan(ScanParams p) {
+  __shared__ int s_tile, s_flag;
+  if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1);
+  __syncthreads();
+  const int tile = s_tile;
+  const int per_chunk = p.B * p.nslices;
+  const int chunk = tile / per_chunk;
+  const int bs = tile - chunk * per_chunk;
+  const int b = bs / p.nslices, slice = bs - b * p.nslices;
+  const int c = slice * blockDim.x + threadIdx.x;
+  const bool active = c < p.C;
+  const int t0 = chunk * p.T, t1 = min(t0 + p.T, p.L);
+  const float db = active ? p.decay_bias[c] : 0.f;
+  float mx[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) mx[r] = 0.f;
+  if (MIMO && active) {
+    const int h = c / p.D, d = c - h * p.D;
+#pragma unroll
+    for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
+  }
+  const int64_t row0 = (int64_t)b * p.L;
+
+  // pass 1: aggregate affine map of this chunk (A shared by the ranks)
+  float A = 1.f, U[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) U[r] = 0.f;
+  if (active) {
+    for (int t = t0; t < t1; ++t) {
+      float a, u[RM];
+      scan_inputs<RM, MIMO>(p, row0 + t, c, db, mx, a, u);
+#pragma unroll
+      for (int r = 0; r < RM; ++r) U[r] = step<MIMO>(a, U[r], u[r]);
+      A *= a;
+    }
+  }
+  int *flag_row = p.flags + ((int64_t)b * p.nslices + slice) * p.nchunks;
+  const int64_t cidx = ((int64_t)b * p.nchunks + chunk);
+  if (chunk > 0 && chunk + 1 < p.nchunks) {  // the last chunk has no successor
+    if (active) {
+      p.aggA[cidx * p.C + c] = A;
+#pragma unroll
+      for (int r = 0; r < RM; ++r) p.aggU[(cidx * RM + r) * p.C + c] = U[r];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) st_release(flag_row + chunk, 1);
+  }
+  // look-back for the carry entering this chunk
+  float h[RM];
+#pragma unroll
+  for (int r = 0; r < RM; ++r) h[r] = 0.f;
+  if (active && p.h0) h[0] = (float)p.h0[(int64_t)b * p.C + c];
+  if (chunk > 0) {
+    float Ar = 1.f, Ur[RM];
+#pragma unroll
+    for (int r = 0; r < RM; ++r) Ur[r] = 0.f;
+    int j = chunk - 1;
+    while (true) {
+      if (threadIdx.x == 0) {
+        const long long start = clock64();
+        int f;
+        while ((f = ld_acquire(flag_row + j)) == 0) {
+          if (clock64() - start > kSpinLimit * 64) {
+            flag_timeout();
+            f = -1;
+            break;
+          }
+        }
+        s_flag = f;
+      }
+      __syncthreads();
+      const int f = s_flag;
+      __syncthreads();
+      if (f < 0) break;
+      const int64_t jidx = (int64_t)b * p.nchunks + j;
+      if (f == 2) {
+        if (active) {
+#pragma unroll
+          for (int r = 0; r < RM; ++r) h[r] = fmaf(Ar, p.incl[(jidx * RM + r) * p.C + c], Ur[r]);
+        }
+        break;
+      }
+      if (active) {
+        const float gA = p.aggA[jidx * p.C + c];
+#pragma unroll
+        for (int r = 0; r < RM; ++r) Ur[r] = fmaf(Ar, p.aggU[(jidx * RM + r) * p.C + c], Ur[r]);
+        Ar *= gA;
+      }
+      --j;  // chunk 0 always publishes an inclusive value, so j stays >= 0
+    }
+  }
+  // publish the inclusive states for successors
+  if (chunk + 1 < p.nchunks) {
+    if (active) {
+#pragma unroll
+      for (int r = 0; r < RM; ++r) p.incl[(cidx * RM + r) * p.C + c] = fmaf(A, h[r], U[r]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) st_release(flag_row + chunk, 2);
+  }
+  // pass 2: states of this chunk from the carry
+  if (active) {
+    for (int t = t0; t < t1; ++t) {
+      float a, u[RM];
+      scan_inputs<RM, MIMO>(p, row0 + t, c, db, mx, a, u);
+#pragma unroll
+      for (int r = 0; r < RM; ++r) {
+        h[r] = step<MIMO>(a, h[r], u[r]);
+        p.states[((row0 + t) * RM + r) * p.C + c] = h[r];
+      }
+    }
+    if (t1 == p.L) {
+      p.final_f32[(int64_t)b * p.C + c] = h[0];
+      p.final_f64[(int64_t)b * p.C + c] = (double)h[0];
+    }
+  }
+}
+
+struct ScanLayout {
+  int T, slice, nchunks, nslices;
+  int64_t off_aggU, off_incl, off_flags, bytes;
+};
+
+static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
+  ScanLayout s;
+  s.T = 64;
+  s.slice = C < 128 ? (int)round_up(C, 32) : 128;
+  s.nchunks = (int)ceil_div(L, s.T);
+  s.nslices = (int)ceil_div(C, s.slice);
+  const int64_t nA = B * s.nchunks * C;
+  s.off_aggU = round_up(nA * 4, 256);
+  s.off_incl = s.off_aggU + round_up(nA * RM * 4, 256);
+  s.off_flags = s.off_incl + round_up(nA * RM * 4, 256);
+  s.bytes = s.off_flags + round_up((B * s.nslices * s.nchunks + 1) * 4, 256);
+  return s;
+}
+
+template <int RM, bool MIMO>
+static int launch_scan(ScanParams &p, cudaStream_t st, int slice) {
+  const int64_t grid = (int64_t)p.nchunks * p.B * p.nslices;
+  k_scan<RM, MIMO><<<(unsigned)grid, slice, 0, st>>>(p);
+  return check_launch("scan");
+}
+
+static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t H,
+                    int64_t D, int64_t R, int64_t RM, const float *decay_bias, const float *mimo_x,
+                    const double *h0, float *states, float *final_f32, double *final_f64, void *workspace,
+                    int64_t ws_bytes, cudaStream_t st) {
+  TESM_REQUIRE(proj && decay_bias && states && final_f32 && final_f64 && workspace, "scan: null pointer");
+  TESM_REQUIRE(B > 0 && L > 0 && D > 0 && H > 0 && ldp >= 2 * Dm + 3 * H * D + 2 * H * R, "scan: bad shape");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "scan: dtype");
+  const int64_t C = H * D;
+  ScanLayout s = scan_layout(B, L, C, RM);
+  TESM_REQUIRE(ws_bytes >= s.bytes, "scan: workspace too small (query the *_workspace function)");
+  ScanParams p;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)C, (int)(H * R));
+  p.decay_bias = decay_bias;
+  p.mimo_x = mimo_x;
+  p.h0 = h0;
+  p.B = (int)B;
+  p.L = (int)L;
+  p.C = (int)C;
+  p.D = (int)D;
+  p.RM = (int)RM;
+  p.T = s.T;
+  p.nchunks = s.nchunks;
+  p.nslices = s.nslices;
+  p.states = states;
+  p.final_f32 = final_f32;
+  p.final_f64 = final_f64;
+  uint8_t *ws = (uint8_t *)workspace;
+  p.aggA = (float *)ws;
+  p.aggU = (float *)(ws + s.off_aggU);
+  p.incl = (float *)(ws + s.off_incl);
+  p.flags = (int *)(ws + s.off_flags);
+  p.ticket = p.flags + B * s.nslices * s.nchunks;
+  cudaError_t e = cudaMemsetAsync(p.flags, 0, (B * s.nslices * s.nchunks + 1) * sizeof(int), st);
+  if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("scan memset: ") + cudaGetErrorString(e));
+  if (!mimo_x) return launch_scan<1, false>(p, st, s.slice);
+  switch (RM) {
+    case 1: return launch_scan<1, true>(p, st, s.slice);
+    case 2: return launch_scan<2, true>(p, st, s.slice);
+    case 4: return launch_scan<4, true>(p, st, s.slice);
+    case 8: return launch_scan<8, true>(p, st, s.slice);
+    default: return fail(TESM_EUNSUPPORTED, "scan: mimo_rank must be 1, 2, 4 or 8");
+  }
+}
+
+}  // namespace tesm
+
+using namespace tesm;
+
+extern "C" int tesm_b200_scan_workspace(int64_t B, int64_t L, int64_t C, int64_t RM, int64_t *bytes) {
+  TESM_REQUIRE(bytes && B > 0 && L > 0 && C > 0 && RM > 0, "scan_workspace: bad argument");
+  *bytes = scan_layout(B, L, C, RM).bytes;
+  return TESM_OK;
+}
+
+extern "C" int tesm_b200_siso_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                   int64_t D, int64_t R, const float *decay_bias, const double *h0, float *states,
+                                   float *final_f32, double *final_f64, void *workspace, int64_t ws_bytes,
+                                   tesm_stream_t stream) {
+  return run_scan(proj, dtype, ldp, B, L, Dm, 1, D, R, 1, decay_bias, nullptr, h0, states, final_f32, final_f64,
+                  workspace, ws_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int tesm_b200_mimo_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                   int64_t H, int64_t D, int64_t R, int64_t RM, const float *decay_bias,
+                                   const float *mimo_x, float *states, float *final_f32, double *final_f64,
+                                   void *workspace, int64_t ws_bytes, tesm_stream_t stream) {
+  TESM_REQUIRE(mimo_x != nullptr, "mimo_scan: null mimo_x");
+  return run_scan(proj, dtype, ldp, B, L, Dm, H, D, R, RM, decay_bias, mimo_x, nullptr, states, final_f32,
+                  final_f64, workspace, ws_bytes, (cudaStream_t)stream);
+}

@@ -1,0 +1,322 @@
+// SISO layer kernels: selective state scan, local / global ternary entanglement, output
+// combine.  Reference: tesm_ssm/modules/tesm.py (TESM_SISO.forward :1175-1272).
+//
+// Layout: the in_proj output `proj` is (B*L, Nproj) row-major with the reference's
+// column split [local Dm | value D | decay D | write D | gate Dm | q R | k R]
+// (tesm.py:1195-1205); kernels read their columns in place through offsets.
+#include "layer_common.cuh"
+
+namespace tesm {
+
+
+// ---------------------------------------------------------------- local entanglement
+// For lag o in [0, W): j = t - o valid iff j >= 0, score = q_t.k_j / sqrt(R) + bias[W-1-o];
+// avg_t = sum tern * states_j / max(sum|tern|, 1); ent = s + es (avg - s)  (tesm.py:922-952,1231).
+// Outputs tanh(ent) and ent - s, the inputs of state_proj / ent_proj.
+struct LocalEntParams {
+  ProjCols pc;
+  const float *cross;  // (B*L, R) additive q bias, or null
+  const float *bias;   // (W) local_entanglement_bias (full parameter)
+  const float *states; // (B, L, D)
+  int B, L, D, R, W, T;
+  float thr, es, inv_sqrt_r_div, rope_base;
+  float sqrt_r;
+  void *out_tanh;      // (B*L, D)
+  void *out_chg;
+  int out_dtype;
+};
+
+template <int W>
+__global__ void k_siso_local_ent(LocalEntParams p) {
+  extern __shared__ float sm[];
+  const int R = p.R, T = p.T;
+  const int RP = R + 1;
+  float *qs = sm;                    // T x RP
+  float *ks = qs + T * RP;           // (T + W - 1) x RP
+  float *tw = ks + (T + W - 1) * RP; // T x W ternary / norm
+  const int b = blockIdx.y;
+  const int t0 = blockIdx.x * T;
+  const int64_t row0 = (int64_t)b * p.L;
+  const int nt = min(T, p.L - t0);
+  // q rows (+ cross-layer bias), k rows with halo
+  const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < nt; r += nwarp) {
+    const int64_t row = row0 + t0 + r;
+    load_rope_row(qs + r * RP, p.pc, p.pc.c_q, row, R, t0 + r, p.rope_base,
+                  p.cross ? p.cross + row * R : nullptr, lane, 32);
+  }
+  for (int r = warp; r < nt + W - 1; r += nwarp) {
+    const int pos = t0 - (W - 1) + r;
+    if (pos < 0) continue;
+    load_rope_row(ks + r * RP, p.pc, p.pc.c_k, row0 + pos, R, pos, p.rope_base, nullptr, lane, 32);
+  }
+  __syncthreads();
+  // scores -> ternary weights; one warp per query position
+  for (int t = warp; t < nt; t += nwarp) {
+    float tern_o = 0.f;
+    float cnt = 0.f;
+    for (int o = 0; o < W; ++o) {
+      const int j = t0 + t - o;
+      float part = 0.f;
+      if (j >= 0) {
+        const float *qr = qs + t * RP;
+        const float *kr = ks + (t + W - 1 - o) * RP;
+        for (int i = lane; i < R; i += 32) part = fmaf(qr[i], kr[i], part);
+      }
+      part = warp_sum(part);
+      float tv = 0.f;
+      if (j >= 0) {
+        const float sc = __fdiv_rn(part, p.sqrt_r) + p.bias[W - 1 - o];
+        tv = ternary_of(sc, p.thr);
+      }
+      if (lane == o) tern_o = tv;
+      cnt += fabsf(tv);
+    }
+    const float norm = fmaxf(cnt, 1.f);
+    if (lane < W) tw[t * W + lane] = tern_o / norm;
+  }
+  __syncthreads();
+  // per channel: sliding window of states in registers
+  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+    float win[W];
+#pragma unroll
+    for (int o = 1; o < W; ++o) {
+      const int j = t0 - o;
+      win[o] = j >= 0 ? p.states[(row0 + j) * p.D + d] : 0.f;
+    }
+    for (int t = 0; t < nt; ++t) {
+#pragma unroll
+      for (int o = W - 1; o > 0; --o) win[o] = win[o - 1];
+      const int64_t row = row0 + t0 + t;
+      const float s = p.states[row * p.D + d];
+      win[0] = s;
+      float avg = 0.f;
+#pragma unroll
+      for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[o], avg);
+      const float ent = s + p.es * (avg - s);
+      store_f(p.out_tanh, p.out_dtype, row * p.D + d, tanhf(ent));
+      store_f(p.out_chg, p.out_dtype, row * p.D + d, ent - s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- global entanglement
+// Causal O(L^2) variant (tesm.py:963-1043): relative bias depends on i - j only and is
+// passed as a vector over d = i - j (index d + L - 1).
+__global__ void k_global_relbias(const float *embed, int dim, float scale, float bias0, int L, float *out) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= 2 * L - 1) return;
+  const float d = (float)(idx - (L - 1));
+  float ss = 0.f, cc = 0.f;
+  const float pi_f = 3.14159265358979323846f;
+  for (int k = 0; k < dim; ++k) {
+    const float f = __fdiv_rn(__fmul_rn((float)(k + 1), pi_f), 1000.f);
+    float sn, cs;
+    sincosf(d * f, &sn, &cs);
+    ss += sn * embed[k];
+    cc += cs * embed[k];
+  }
+  out[idx] = (ss + cc) * scale + bias0;
+}
+
+struct GlobalEntParams {
+  ProjCols pc;
+  const float *cross;
+  const float *relb;    // (2L - 1)
+  const float *states;  // (B, L, D)
+  int B, L, D, R;
+  float thr, es, sqrt_r, rope_base;
+  void *out_tanh, *out_chg;
+  int out_dtype;
+};
+
+// One CTA per (query tile of 32 rows, batch); loops over causal key tiles of 32.
+__global__ void __launch_bounds__(256) k_siso_global_ent(GlobalEntParams p) {
+  extern __shared__ float sm[];
+  constexpr int TQ = 32, TK = 32;
+  const int R = p.R, RP = R + 1, D = p.D;
+  float *qs = sm;               // TQ x RP
+  float *ks = qs + TQ * RP;     // TK x RP
+  float *tt = ks + TK * RP;     // TQ x TK ternary
+  float *cnt = tt + TQ * TK;    // TQ
+  float *vs = cnt + TQ;         // TK x D
+  float *acc = vs + TK * D;     // TQ x D
+  const int b = blockIdx.y, q0 = blockIdx.x * TQ;
+  const int64_t row0 = (int64_t)b * p.L;
+  const int nq = min(TQ, p.L - q0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  for (int r = warp; r < nq; r += nwarp) {
+    const int64_t row = row0 + q0 + r;
+    load_rope_row(qs + r * RP, p.pc, p.pc.c_q, row, R, q0 + r, p.rope_base, p.cross ? p.cross + row * R : nullptr,
+                  lane, 32);
+  }
+  for (int i = threadIdx.x; i < TQ * D; i += blockDim.x) acc[i] = 0.f;
+  if (threadIdx.x < TQ) cnt[threadIdx.x] = 0.f;
+  for (int k0 = 0; k0 < q0 + nq; k0 += TK) {
+    const int nk = min(TK, p.L - k0);
+    __syncthreads();
+    for (int r = warp; r < nk; r += nwarp)
+      load_rope_row(ks + r * RP, p.pc, p.pc.c_k, row0 + k0 + r, R, k0 + r, p.rope_base, nullptr, lane, 32);
+    for (int i = threadIdx.x; i < nk * D; i += blockDim.x) {
+      const int r = i / D, d = i - r * D;
+      vs[i] = p.states[(row0 + k0 + r) * D + d];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < TQ * TK; i += blockDim.x) {
+      const int qi = i / TK, kj = i - qi * TK;
+      float tv = 0.f;
+      const int gi = q0 + qi, gj = k0 + kj;
+      if (qi < nq && kj < nk && gj <= gi) {
+        float dot = 0.f;
+        for (int c = 0; c < R; ++c) dot = fmaf(qs[qi * RP + c], ks[kj * RP + c], dot);
+        const float sc = __fdiv_rn(dot, p.sqrt_r) + p.relb[gi - gj + p.L - 1];
+        tv = ternary_of(sc, p.thr);
+      }
+      tt[i] = tv;
+    }
+    __syncthreads();
+    if (threadIdx.x < TQ) {
+      float c = 0.f;
+      for (int kj = 0; kj < TK; ++kj) c += fabsf(tt[threadIdx.x * TK + kj]);
+      cnt[threadIdx.x] += c;
+    }
+    for (int i = threadIdx.x; i < TQ * D; i += blockDim.x) {
+      const int qi = i / D, d = i - qi * D;
+      float a = acc[i];
+      for (int kj = 0; kj < nk; ++kj) a = fmaf(tt[qi * TK + kj], vs[kj * D + d], a);
+      acc[i] = a;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nq * D; i += blockDim.x) {
+    const int qi = i / D, d = i - qi * D;
+    const int64_t row = row0 + q0 + qi;
+    const float s = p.states[row * D + d];
+    const float avg = acc[i] / fmaxf(cnt[qi], 1.f);
+    const float ent = s + p.es * (avg - s);
+    store_f(p.out_tanh, p.out_dtype, row * D + d, tanhf(ent));
+    store_f(p.out_chg, p.out_dtype, row * D + d, ent - s);
+  }
+}
+
+// ---------------------------------------------------------------- combine
+// y = local + sigmoid(gate) * sp + ep   (tesm.py:1256-1260)
+__global__ void k_combine(ProjCols pc, const void *sp, const void *ep, int sdtype, int64_t M, int Dm, void *y,
+                          int ydtype) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * Dm) return;
+  const int64_t m = i / Dm;
+  const int c = (int)(i - m * Dm);
+  const float loc = load_f(pc.proj, pc.dtype, m * pc.ld + pc.c_local + c);
+  const float g = sigmoidf_(load_f(pc.proj, pc.dtype, m * pc.ld + pc.c_gate + c));
+  const float v = loc + g * load_f(sp, sdtype, i) + load_f(ep, sdtype, i);
+  store_f(y, ydtype, i, v);
+}
+
+}  // namespace tesm
+
+using namespace tesm;
+
+template <int W>
+static int launch_local(LocalEntParams &p, cudaStream_t st) {
+  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    attr = true;
+  }
+  if (smem > 160 * 1024) return fail(TESM_EUNSUPPORTED, "local_ent: ent_rank too large");
+  dim3 grid((unsigned)ceil_div(p.L, p.T), (unsigned)p.B);
+  const int threads = p.D >= 256 ? 256 : (int)round_up(p.D, 32);
+  k_siso_local_ent<W><<<grid, threads < 64 ? 64 : threads, smem, st>>>(p);
+  return check_launch("local_ent");
+}
+
+extern "C" int tesm_b200_siso_local_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                        int64_t D, int64_t R, int64_t W, const float *cross, const float *bias,
+                                        const float *states, float thr, float es, float rope_base, void *out_tanh,
+                                        void *out_chg, int out_dtype, tesm_stream_t stream) {
+  TESM_REQUIRE(proj && bias && states && out_tanh && out_chg, "local_ent: null pointer");
+  TESM_REQUIRE(B > 0 && L > 0 && D > 0 && R > 0 && R % 2 == 0, "local_ent: bad shape");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "local_ent: dtype");
+  LocalEntParams p;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
+  p.cross = cross;
+  p.bias = bias;
+  p.states = states;
+  p.B = (int)B;
+  p.L = (int)L;
+  p.D = (int)D;
+  p.R = (int)R;
+  p.W = (int)W;
+  p.T = 64;
+  p.thr = thr;
+  p.es = es;
+  p.sqrt_r = (float)sqrt((double)R);
+  p.rope_base = rope_base;
+  p.out_tanh = out_tanh;
+  p.out_chg = out_chg;
+  p.out_dtype = out_dtype;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (W) {
+    case 4: return launch_local<4>(p, st);
+    case 8: return launch_local<8>(p, st);
+    case 16: return launch_local<16>(p, st);
+    case 32: return launch_local<32>(p, st);
+    default: return fail(TESM_EUNSUPPORTED, "local_ent: entanglement_window must be 4, 8, 16 or 32");
+  }
+}
+
+extern "C" int tesm_b200_global_relbias(const float *embed, int64_t dim, float scale, float bias0, int64_t L,
+                                        float *out, tesm_stream_t stream) {
+  TESM_REQUIRE(embed && out && dim > 0 && L > 0, "global_relbias: bad argument");
+  const int64_t n = 2 * L - 1;
+  k_global_relbias<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(embed, (int)dim, scale, bias0,
+                                                                                   (int)L, out);
+  return check_launch("global_relbias");
+}
+
+extern "C" int tesm_b200_siso_global_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L,
+                                         int64_t Dm, int64_t D, int64_t R, const float *cross, const float *relb,
+                                         const float *states, float thr, float es, float rope_base, void *out_tanh,
+                                         void *out_chg, int out_dtype, tesm_stream_t stream) {
+  TESM_REQUIRE(proj && relb && states && out_tanh && out_chg, "global_ent: null pointer");
+  TESM_REQUIRE(B > 0 && L > 0 && D > 0 && R > 0 && R % 2 == 0, "global_ent: bad shape");
+  GlobalEntParams p;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
+  p.cross = cross;
+  p.relb = relb;
+  p.states = states;
+  p.B = (int)B;
+  p.L = (int)L;
+  p.D = (int)D;
+  p.R = (int)R;
+  p.thr = thr;
+  p.es = es;
+  p.sqrt_r = (float)sqrt((double)R);
+  p.rope_base = rope_base;
+  p.out_tanh = out_tanh;
+  p.out_chg = out_chg;
+  p.out_dtype = out_dtype;
+  const size_t smem = sizeof(float) * (32 * (R + 1) * 2 + 32 * 32 + 32 + 32 * D * 2);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_siso_global_ent, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  TESM_REQUIRE(smem <= 200 * 1024, "global_ent: d_state too large");
+  dim3 grid((unsigned)ceil_div(L, 32), (unsigned)B);
+  k_siso_global_ent<<<grid, 256, smem, (cudaStream_t)stream>>>(p);
+  return check_launch("global_ent");
+}
+
+extern "C" int tesm_b200_combine(const void *proj, int dtype, int64_t ldp, int64_t M, int64_t Dm, int64_t D,
+                                 int64_t R, const void *sp, const void *ep, int sdtype, void *y, int ydtype,
+                                 tesm_stream_t stream) {
+  TESM_REQUIRE(proj && sp && ep && y && M >= 0 && Dm > 0, "combine: bad argument");
+  if (M == 0) return TESM_OK;
+  ProjCols pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
+  const int64_t n = M * Dm;
+  k_combine<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(pc, sp, ep, sdtype, M, (int)Dm, y, ydtype);
+  return check_launch("combine");
+}

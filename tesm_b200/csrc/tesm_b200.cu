@@ -4,3 +4,8 @@
 #include "quant.cu"
 #include "gemv.cu"
 #include "gemm_tc.cu"
+#include "scan.cu"
+#include "siso.cu"
+#include "mimo.cu"
+#include "decode.cu"
+#include "model.cu"

@@ -6,6 +6,7 @@ device; ownership stays with torch.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Optional
 
@@ -143,3 +144,143 @@ def bitlinear_2d(x2d: torch.Tensor, pw: PackedWeight, eps: float, out_dtype=None
         return gemv(codes, inv, rowsum, pw, M, out_dtype, out, acc)
     codes, inv, _ = quant_act(x2d, eps, LAYOUT_ROWMAJOR)
     return gemm(codes, inv, pw, M, out_dtype, out, acc)
+
+
+# ------------------------------------------------------------------ pre-quantised activations
+@dataclass
+class QuantAct:
+    """int8 activation codes of M rows ready for a BitLinear (layout GEMV or ROWMAJOR)."""
+    codes: torch.Tensor
+    inv: torch.Tensor
+    rowsum: Optional[torch.Tensor]
+    layout: int
+    M: int
+
+
+def layout_for(M: int) -> int:
+    return LAYOUT_GEMV if M <= GEMV_MAX_M else LAYOUT_ROWMAJOR
+
+
+def alloc_quant(M: int, K: int, device, layout: Optional[int] = None) -> QuantAct:
+    layout = layout_for(M) if layout is None else layout
+    ld = round_up(K, 256) if layout == LAYOUT_GEMV else round_up(K, 16)
+    codes = torch.empty(M, ld, device=device, dtype=torch.int8)
+    inv = torch.empty(M, device=device, dtype=torch.float32)
+    rowsum = torch.empty(M, device=device, dtype=torch.int32) if layout == LAYOUT_GEMV else None
+    return QuantAct(codes, inv, rowsum, layout, M)
+
+
+def quantize(x2d: torch.Tensor, eps: float) -> QuantAct:
+    M = x2d.shape[0]
+    layout = layout_for(M)
+    codes, inv, rowsum = quant_act(x2d, eps, layout)
+    return QuantAct(codes, inv, rowsum, layout, M)
+
+
+def matmul_q(q: QuantAct, pw: PackedWeight, out_dtype: torch.dtype, out=None):
+    if q.layout == LAYOUT_GEMV:
+        return gemv(q.codes, q.inv, q.rowsum, pw, q.M, out_dtype, out)
+    return gemm(q.codes, q.inv, pw, q.M, out_dtype, out)
+
+
+def pack_into(w: torch.Tensor, eps: float, packed: torch.Tensor, tern: Optional[torch.Tensor],
+              scale: torch.Tensor, deq: torch.Tensor):
+    """Pack one weight into caller-provided row slices (used to fuse gate/up weights)."""
+    N, K = w.shape
+    work = torch.empty(N, device=w.device, dtype=torch.float64)
+    _lib.call("tesm_b200_weight_scale", w.data_ptr(), dtype_code(w.dtype), N, K, w.stride(0), 0, float(eps),
+              scale.data_ptr(), deq.data_ptr(), work.data_ptr(), _stream())
+    _lib.call("tesm_b200_pack_ternary", w.data_ptr(), dtype_code(w.dtype), N, K, w.stride(0), 0, scale.data_ptr(),
+              packed.data_ptr(), packed.stride(0), _ptr(tern), tern.stride(0) if tern is not None else 0, _stream())
+
+
+# ------------------------------------------------------------------ layer kernels
+def scan_workspace(B: int, L: int, C: int, RM: int, device) -> torch.Tensor:
+    n = ctypes.c_int64(0)
+    _lib.call("tesm_b200_scan_workspace", B, L, C, RM, ctypes.addressof(n))
+    return torch.empty(n.value, device=device, dtype=torch.uint8)
+
+
+def siso_scan(proj, B, L, Dm, D, R, decay_bias, h0, states, f32, f64):
+    ws = scan_workspace(B, L, D, 1, proj.device)
+    _lib.call("tesm_b200_siso_scan", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, D, R,
+              decay_bias.data_ptr(), _ptr(h0), states.data_ptr(), f32.data_ptr(), f64.data_ptr(), ws.data_ptr(),
+              ws.numel(), _stream())
+
+
+def mimo_scan(proj, B, L, Dm, H, D, R, RM, decay_bias, mimo_x, states, f32, f64):
+    ws = scan_workspace(B, L, H * D, RM, proj.device)
+    _lib.call("tesm_b200_mimo_scan", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, H, D, R, RM,
+              decay_bias.data_ptr(), mimo_x.data_ptr(), states.data_ptr(), f32.data_ptr(), f64.data_ptr(),
+              ws.data_ptr(), ws.numel(), _stream())
+
+
+def siso_local_ent(proj, B, L, Dm, D, R, W, cross, bias, states, thr, es, base, out_tanh, out_chg):
+    _lib.call("tesm_b200_siso_local_ent", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, D, R, W,
+              _ptr(cross), bias.data_ptr(), states.data_ptr(), float(thr), float(es), float(base),
+              out_tanh.data_ptr(), out_chg.data_ptr(), dtype_code(out_tanh.dtype), _stream())
+
+
+def global_relbias(embed, scale, bias0, L):
+    out = torch.empty(2 * L - 1, device=embed.device, dtype=torch.float32)
+    _lib.call("tesm_b200_global_relbias", embed.data_ptr(), embed.numel(), float(scale), float(bias0), L,
+              out.data_ptr(), _stream())
+    return out
+
+
+def siso_global_ent(proj, B, L, Dm, D, R, cross, relb, states, thr, es, base, out_tanh, out_chg):
+    _lib.call("tesm_b200_siso_global_ent", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, D, R,
+              _ptr(cross), relb.data_ptr(), states.data_ptr(), float(thr), float(es), float(base),
+              out_tanh.data_ptr(), out_chg.data_ptr(), dtype_code(out_tanh.dtype), _stream())
+
+
+def mimo_local_ent(proj, B, L, Dm, H, D, R, RM, W, bias, mimo_o, states, thr, es, base, quirk, out_tanh, out_chg):
+    _lib.call("tesm_b200_mimo_local_ent", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, H, D, R,
+              RM, W, bias.data_ptr(), mimo_o.data_ptr(), states.data_ptr(), float(thr), float(es), float(base),
+              int(quirk), out_tanh.data_ptr(), out_chg.data_ptr(), dtype_code(out_tanh.dtype), _stream())
+
+
+def combine(proj, M, Dm, C, Rc, sp, ep, y):
+    _lib.call("tesm_b200_combine", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), M, Dm, C, Rc,
+              sp.data_ptr(), ep.data_ptr(), dtype_code(sp.dtype), y.data_ptr(), dtype_code(y.dtype), _stream())
+
+
+def cache_fill(proj, states, RM, B, L, Dm, H, D, R, W, base, final64, state, kc, vc, ctl):
+    _lib.call("tesm_b200_cache_fill", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), states.data_ptr(), RM,
+              B, L, Dm, H, D, R, W, float(base), final64.data_ptr(), state.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+              ctl.data_ptr(), _stream())
+
+
+def decode_step(proj, B, Dm, H, D, R, W, decay_bias, bias, cross, state, kc, vc, ctl, thr, es, base, out_tanh,
+                out_chg, new_state):
+    _lib.call("tesm_b200_decode_step", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, Dm, H, D, R, W,
+              decay_bias.data_ptr(), bias.data_ptr(), _ptr(cross), state.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+              ctl.data_ptr(), float(thr), float(es), float(base), out_tanh.data_ptr(), out_chg.data_ptr(),
+              dtype_code(out_tanh.dtype), _ptr(new_state), _stream())
+
+
+def embed(ids, emb, pos_emb, pos_dev, pos_host, out):
+    B, L = ids.shape
+    _lib.call("tesm_b200_embed", ids.data_ptr(), B, L, emb.data_ptr(), pos_emb.data_ptr(), dtype_code(emb.dtype),
+              emb.shape[1], _ptr(pos_dev), int(pos_host), out.data_ptr(), dtype_code(out.dtype), _stream())
+
+
+def add_rmsnorm_quant(x, residual, residual_out, weight, eps, qeps, q: Optional[QuantAct], y_out=None):
+    M, K = x.shape
+    _lib.call("tesm_b200_add_rmsnorm_quant", x.data_ptr(), dtype_code(x.dtype), _ptr(residual), _ptr(residual_out),
+              weight.data_ptr(), float(eps), M, K, float(qeps), _ptr(q.codes) if q else None,
+              q.codes.stride(0) if q else 0, q.layout if q else 0, _ptr(q.inv) if q else None,
+              _ptr(q.rowsum) if q else None, _ptr(y_out), dtype_code(y_out.dtype) if y_out is not None else 0,
+              _stream())
+
+
+def silu_mul(gu, F, out):
+    _lib.call("tesm_b200_silu_mul", gu.data_ptr(), dtype_code(gu.dtype), gu.shape[0], F, out.data_ptr(),
+              dtype_code(out.dtype), _stream())
+
+
+def device_status() -> int:
+    v = ctypes.c_int(0)
+    _lib.call("tesm_b200_device_status", ctypes.addressof(v))
+    return v.value
+

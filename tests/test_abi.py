@@ -37,3 +37,12 @@ def test_argument_validation_without_gpu():
     rc = lib.tesm_b200_quant_act(ctypes.c_void_p(16), 7, 1, 16, 16, 1e-5, ctypes.c_void_p(16), 256, 0,
                                  ctypes.c_void_p(16), None, None)
     assert rc == 2
+
+
+def test_argument_counts_match_header():
+    text = open(os.path.join(ROOT, "include", "tesm_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    for m in re.finditer(r"\b(tesm_b200_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.S):
+        name, params = m.group(1), m.group(2).strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert n == len(_lib.SIGNATURES[name]), f"{name}: header has {n} params, ctypes table {len(_lib.SIGNATURES[name])}"

@@ -1,0 +1,249 @@
+"""Scan / entanglement / decode kernels and the mirror modules vs oracle + golden (GPU).
+
+Tolerances (max|out-ref| / max|ref|): 1e-3 for fp32 layer outputs (north_star), 1e-5 for
+the fp32 scan states; ternary decisions whose score lies within 1e-4 of the threshold are
+"ambiguous" -- positions touched by one are excluded and must stay below 1e-4 of all.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle as O
+from helpers import build_mimo, build_model, build_siso, golden, max_rel, randn, siso_cfg, mimo_cfg, model_cfg, params_np
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops(lib):
+    from tesm_b200 import ops as _ops
+    return _ops
+
+
+def _proj(B, L, Dm, C, Rc, seed, scale=1.0):
+    N = 2 * Dm + 3 * C + 2 * Rc
+    return randn((B * L, N), seed) * scale
+
+
+def _split(P, Dm, C, Rc):
+    o = np.cumsum([0, Dm, C, C, C, Dm, Rc, Rc])
+    return [P[:, o[i]:o[i + 1]] for i in range(7)]
+
+
+def _ambiguous_rows(scores, thr, tol=1e-4):
+    s = np.abs(np.nan_to_num(scores, nan=1e9))
+    amb = np.abs(s - thr) < tol * np.maximum(1.0, s)
+    return amb.reshape(amb.shape[0], -1).any(-1) if amb.ndim > 1 else amb
+
+
+@pytest.mark.parametrize("B,L,D,h0", [(2, 200, 64, False), (3, 300, 300, True), (1, 7, 32, False),
+                                      (2, 4096, 256, True)])
+def test_siso_scan(ops, B, L, D, h0):
+    Dm, R = 32, 16
+    P = _proj(B, L, Dm, D, R, 40 + D)
+    db = torch.full((D,), 3.0) + randn((D,), 5) * 0.5
+    prev = randn((B, D), 6).double() if h0 else None
+    _, val, dec, wr, _, _, _ = _split(P.numpy(), Dm, D, R)
+    a = O.sigmoid(dec.reshape(B, L, D) + db.numpy())
+    u = (O.sigmoid(wr) * np.tanh(val)).reshape(B, L, D)
+    ref, fin = O.scan_chunked_f64(a, u, prev.numpy() if h0 else None)
+    st = torch.empty(B * L, D, device="cuda")
+    f32 = torch.empty(B, D, device="cuda")
+    f64 = torch.empty(B, D, device="cuda", dtype=torch.float64)
+    ops.siso_scan(P.cuda(), B, L, Dm, D, R, db.cuda(), prev.cuda() if h0 else None, st, f32, f64)
+    assert ops.device_status() == 0
+    assert max_rel(st.cpu().numpy().reshape(B, L, D), ref) <= 1e-5
+    assert max_rel(f64.cpu().numpy(), fin) <= 1e-5
+
+
+@pytest.mark.parametrize("B,L,D,R,W,cross", [(2, 100, 64, 64, 16, False), (2, 33, 40, 16, 8, True),
+                                             (1, 5, 32, 16, 16, False), (2, 1000, 256, 64, 16, True)])
+def test_siso_local_ent(ops, B, L, D, R, W, cross):
+    Dm = 16
+    P = _proj(B, L, Dm, D, R, 50 + L)
+    st = randn((B, L, D), 51)
+    bias = randn((W,), 52) * 0.3
+    cr = randn((B * L, R), 53) * 0.5 if cross else None
+    thr, es = 0.1, 0.2
+    Pn = P.numpy()
+    q = O.rope(Pn[:, 2 * Dm + 3 * D:2 * Dm + 3 * D + R].reshape(B, L, R))
+    k = O.rope(Pn[:, 2 * Dm + 3 * D + R:].reshape(B, L, R))
+    if cross:
+        q = q + cr.numpy().reshape(B, L, R)
+    avg, sc = O.local_ent(q, k, st.numpy(), bias.numpy(), thr, return_scores=True)
+    ent = st.numpy() + np.float32(es) * (avg - st.numpy())
+    th = torch.empty(B * L, D, device="cuda")
+    ch = torch.empty(B * L, D, device="cuda")
+    ops.siso_local_ent(P.cuda(), B, L, Dm, D, R, W, cr.cuda() if cross else None, bias.cuda(), st.cuda(), thr, es,
+                       1e4, th, ch)
+    amb = _ambiguous_rows(sc.reshape(B * L, -1), thr)
+    assert amb.mean() < 1e-4 or amb.sum() <= 1
+    keep = ~amb
+    assert max_rel(th.cpu().numpy()[keep], np.tanh(ent).reshape(B * L, D)[keep]) <= 1e-5
+    assert max_rel(ch.cpu().numpy()[keep], (ent - st.numpy()).reshape(B * L, D)[keep]) <= 1e-4
+
+
+@pytest.mark.parametrize("B,L,D,R", [(2, 48, 32, 16), (1, 300, 64, 64)])
+def test_siso_global_ent(ops, B, L, D, R):
+    Dm = 16
+    P = _proj(B, L, Dm, D, R, 60 + L)
+    st = randn((B, L, D), 61)
+    emb = randn((64,), 62) * 0.02
+    thr, es = 0.1, 0.2
+    Pn = P.numpy()
+    q = O.rope(Pn[:, 2 * Dm + 3 * D:2 * Dm + 3 * D + R].reshape(B, L, R))
+    k = O.rope(Pn[:, 2 * Dm + 3 * D + R:].reshape(B, L, R))
+    rb = O.global_rel_bias(L, emb.numpy(), 1.0, 0.0)
+    relb = ops.global_relbias(emb.cuda(), 1.0, 0.0, L)
+    assert max_rel(relb.cpu().numpy(), rb) <= 1e-5
+    avg, sc = O.global_ent(q, k, st.numpy(), rb, thr, return_scores=True)
+    ent = st.numpy() + np.float32(es) * (avg - st.numpy())
+    th = torch.empty(B * L, D, device="cuda")
+    ch = torch.empty(B * L, D, device="cuda")
+    ops.siso_global_ent(P.cuda(), B, L, Dm, D, R, None, relb, st.cuda(), thr, es, 1e4, th, ch)
+    i = np.arange(L)
+    sc = np.where((i[:, None] >= i[None, :])[None], sc, np.nan)
+    amb = _ambiguous_rows(sc.reshape(B * L, -1), thr)
+    keep = ~amb
+    assert max_rel(th.cpu().numpy()[keep], np.tanh(ent).reshape(B * L, D)[keep]) <= 1e-5
+
+
+@pytest.mark.parametrize("B,L,H,D,R,RM,W", [(2, 40, 4, 16, 8, 4, 8), (1, 200, 16, 64, 48, 4, 16),
+                                            (2, 9, 2, 16, 8, 2, 8)])
+def test_mimo_scan_ent(ops, B, L, H, D, R, RM, W):
+    Dm = 32
+    C, Rc = H * D, H * R
+    P = _proj(B, L, Dm, C, Rc, 70 + L)
+    db = torch.full((H, D), 3.0) + randn((H, D), 71) * 0.3
+    mx = 1.0 / RM + randn((H, RM, D), 72) * 0.05
+    mo = 1.0 / RM + randn((H, RM, D), 73) * 0.05
+    bias = randn((H, W), 74) * 0.02
+    thr, es = 0.5, 0.2
+    Pn = P.numpy()
+    _, val, dec, wr, _, qp, kp = _split(Pn, Dm, C, Rc)
+    a = O.sigmoid(dec.reshape(B, L, H, D) + db.numpy())
+    w = O.sigmoid(wr.reshape(B, L, H, D))
+    v = np.tanh(val.reshape(B, L, H, D)).astype(np.float32)
+    q = O.rope_mimo(qp.reshape(B, L, H, R))
+    k = O.rope_mimo(kp.reshape(B, L, H, R))
+    states = torch.empty(B * L, RM, C, device="cuda")
+    f32 = torch.empty(B, C, device="cuda")
+    f64 = torch.empty(B, C, device="cuda", dtype=torch.float64)
+    ops.mimo_scan(P.cuda(), B, L, Dm, H, D, R, RM, db.cuda(), mx.cuda(), states, f32, f64)
+    ent_ref = np.zeros((B, L, H, D), np.float32)
+    chg_ref = np.zeros((B, L, H, D), np.float32)
+    stg = states.cpu().numpy().reshape(B, L, RM, H, D)
+    sc_any = None
+    for r in range(RM):
+        upd = (w * mx.numpy()[None, None, :, r]) * (v * mx.numpy()[None, None, :, r])
+        st = O.scan_seq(a, upd.astype(np.float32))
+        assert max_rel(stg[:, :, r], st) <= 1e-5, f"rank {r} states"
+        avg, sc = O.local_ent_mimo(q, k, st, bias.numpy(), thr, return_scores=True)
+        sc_any = sc
+        e_r = st + np.float32(es) * (avg - st)
+        ent_ref += mo.numpy()[None, None, :, r] * e_r
+        chg_ref += mo.numpy()[None, None, :, r] * (e_r - st)
+    th = torch.empty(B * L, C, device="cuda")
+    ch = torch.empty(B * L, C, device="cuda")
+    ops.mimo_local_ent(P.cuda(), B, L, Dm, H, D, R, RM, W, bias.cuda(), mo.cuda(), states, thr, es, 1e4, True, th, ch)
+    amb = _ambiguous_rows(sc_any.reshape(B * L, -1), thr)
+    keep = ~amb
+    assert max_rel(th.cpu().numpy()[keep], np.tanh(ent_ref).reshape(B * L, C)[keep]) <= 1e-5
+    assert max_rel(ch.cpu().numpy()[keep], chg_ref.reshape(B * L, C)[keep]) <= 1e-4
+
+
+# ------------------------------------------------------------------ modules vs golden
+def _to_cuda(m):
+    return m.cuda().eval()
+
+
+@pytest.mark.parametrize("c", cases.SISO, ids=lambda c: c["name"])
+def test_siso_module_golden(lib, c):
+    g = golden("siso_" + c["name"])
+    m = _to_cuda(build_siso(c["kw"]))
+    B, L = c["B"], c["L"]
+    x = randn((B, L, m.d_model), 1).cuda()
+    cross = randn((B, L, m.d_state), 2).cuda() if c.get("cross") else None
+    prev = randn((B, m.d_state), 4).double().cuda() if c.get("prev") else None
+    ip = {"state_cache": m.allocate_inference_cache(B, m.max_seq_len)} if c.get("decode") else None
+    with torch.no_grad():
+        y, fs = m(x, inference_params=ip, cross_layer_state=cross, prev_state=prev)
+        assert max_rel(y.cpu().numpy(), g["y"]) <= 1e-3
+        assert max_rel(fs.cpu().numpy(), g["final"]) <= 1e-5
+        assert max_rel(m._last_cross_layer_state.cpu().numpy(), g["states"]) <= 1e-5
+        for s in range(c.get("decode", 0)):
+            xt = randn((B, 1, m.d_model), 10 + s).cuda()
+            ct = randn((B, m.d_state), 20 + s).cuda() if c.get("cross") else None
+            yt, st = m(xt, inference_params=ip, cross_layer_state=ct)
+            assert max_rel(yt.cpu().numpy(), g[f"dec{s}_y"]) <= 1e-3, f"decode step {s}"
+            assert max_rel(st.cpu().numpy(), g[f"dec{s}_state"]) <= 1e-5
+    if ip:
+        ch = ip["state_cache"]
+        assert ch["cache_idx"] == int(g["cache_idx"]) and ch["seq_pos"] == int(g["cache_pos"])
+        assert ch["_ctl"].cpu().tolist()[:2] == [int(g["cache_pos"]), int(g["cache_idx"])]
+        assert max_rel(ch["ent_k_cache"].cpu().numpy(), g["cache_k"]) <= 1e-5
+        assert max_rel(ch["ent_v_cache"].cpu().numpy(), g["cache_v"]) <= 1e-5
+
+
+@pytest.mark.parametrize("c", cases.MIMO, ids=lambda c: c["name"])
+def test_mimo_module_golden(lib, c):
+    g = golden("mimo_" + c["name"])
+    m = _to_cuda(build_mimo(c["kw"]))
+    B, L = c["B"], c["L"]
+    x = randn((B, L, m.d_model), 1).cuda()
+    ip = {"state_cache": m.allocate_inference_cache(B, m.max_seq_len)} if c.get("decode") else None
+    with torch.no_grad():
+        y, fs = m(x, inference_params=ip)
+        assert max_rel(y.cpu().numpy(), g["y"]) <= 1e-3
+        assert max_rel(fs.cpu().numpy(), g["final"]) <= 1e-5
+        assert max_rel(m._last_cross_layer_state.cpu().numpy(), g["cross"]) <= 1e-5
+        for s in range(c.get("decode", 0)):
+            xt = randn((B, 1, m.d_model), 10 + s).cuda()
+            ct = randn((B, m.n_heads, m.d_state), 20 + s).cuda() if c.get("cross") else None
+            yt, st = m(xt, inference_params=ip, cross_layer_state=ct)
+            assert max_rel(yt.cpu().numpy(), g[f"dec{s}_y"]) <= 1e-3, f"decode step {s}"
+            assert max_rel(st.cpu().numpy(), g[f"dec{s}_state"]) <= 1e-5
+
+
+@pytest.mark.parametrize("c", cases.MODEL, ids=lambda c: c["name"])
+def test_model_golden(lib, c):
+    g = golden("model_" + c["name"])
+    m = _to_cuda(build_model(c["cfg"]))
+    ids = torch.from_numpy(g["ids"]).cuda()
+    with torch.no_grad():
+        o, _ = m(ids)
+        assert max_rel(o.logits.cpu().numpy(), g["logits"]) <= 1e-3
+        ip = {"state_cache": m.backbone.allocate_inference_cache(c["B"], m.tesm_config.max_seq_len)}
+        o, _ = m(ids, inference_params=ip)
+        assert max_rel(o.logits.cpu().numpy(), g["prefill_logits"]) <= 1e-3
+        for s in range(c["decode"]):
+            o, _ = m(torch.from_numpy(g[f"dec{s}_ids"]).cuda(), inference_params=ip)
+            assert max_rel(o.logits.cpu().numpy(), g[f"dec{s}_logits"]) <= 1e-3, f"decode step {s}"
+
+
+def test_siso_bf16_activations_vs_oracle(lib):
+    """bf16 activations (the reference's torch path cannot run bf16 SISO modules): compared
+    with the fp32 oracle on the same weights at the bf16 bar 2e-2."""
+    c = cases.SISO[0]
+    m = build_siso(c["kw"])
+    P = params_np(m)
+    x = randn((c["B"], c["L"], m.d_model), 1)
+    y_ref, _, _ = O.siso_forward(P, siso_cfg(m), x.numpy())
+    m = m.cuda().eval()
+    with torch.no_grad():
+        y, _ = m(x.cuda().to(torch.bfloat16))
+    assert y.dtype == torch.bfloat16
+    assert max_rel(y.float().cpu().numpy(), y_ref) <= 2e-2
+
+
+def test_strict_backend_errors(lib):
+    m = build_siso(cases.SISO[1]["kw"]).cuda()
+    x = randn((1, 8, m.d_model), 1).cuda()
+    with pytest.raises(RuntimeError, match="kernel_backend='b200' specified but TESM_SISO kernel not available"):
+        m.train()(x)
+    m2 = build_siso(cases.SISO[1]["kw"], backend="torch").cuda().eval()
+    with torch.no_grad(), pytest.raises(RuntimeError, match="kernel_backend='torch' specified"):
+        m2(x)
