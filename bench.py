@@ -1,0 +1,339 @@
+"""Benchmark: full TESMLMHeadModel INT2 prefill on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+A step is one prefill of batch 32 x 4096 tokens per GPU through the public API
+(``TESMLMHeadModel.forward(ids, logits_to_keep=1)``): 32 layers, d_model 4096,
+d_state 256, window 16, vocab 32000, d_intermediate 11008, ent_rank 64, random
+weights (seed 0) and uniform token ids.  Multi-GPU runs are data-parallel replicas
+(weak scaling: every rank prefills its own 32 sequences; no collective on the data
+path).  Rank 0 prints one JSON line.
+
+``--impl reference`` times the CPU restatement of the reference path (the oracle
+port; the reference is a Python package that is not present on the GPU box) on
+the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(n_layer=32, d_model=4096, d_state=256, entanglement_window=16, vocab_size=32000, d_intermediate=11008,
+           max_seq_len=4608, ent_rank=64)
+BATCH, SEQ = 32, 4096
+METRIC = "prefill tokens/s"
+UNIT = "tokens/s"
+
+
+def workload(n):
+    return {"workload": "config5: TESMLMHeadModel INT2 prefill, batch 32 x 4096 per GPU", "model": "TESM 32L d4096",
+            "global_batch": BATCH * n, "seq_len": SEQ, "parallelism": f"dp{n}", "logits_to_keep": 1,
+            "layers": CFG["n_layer"], "d_model": CFG["d_model"], "d_state": CFG["d_state"],
+            "d_intermediate": CFG["d_intermediate"], "vocab": CFG["vocab_size"], "window": 16,
+            "l2": "inputs larger than L2: per-step activations are GBs (no flush needed)"}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ CPU legs (oracle port)
+def cpu_sample(layers=2, tokens=128):
+    """Time the CPU restatement of the reference prefill on `layers` full-width layers and
+    `tokens` tokens (last-token logits).  Returns (tokens/s for the 32-layer model, seconds):
+    the layer time is scaled by 32/layers, embedding and head are counted once."""
+    import numpy as np
+    import oracle as O
+    rng = np.random.default_rng(0)
+    D, Dm, R, Fd, V = CFG["d_state"], CFG["d_model"], CFG["ent_rank"], CFG["d_intermediate"], CFG["vocab_size"]
+
+    def w(n, k):
+        return (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+
+    P = {"backbone.embedding.weight": w(V, Dm), "backbone.position_embedding.weight": w(CFG["max_seq_len"], Dm),
+         "backbone.norm_f.weight": np.ones(Dm, np.float32)}
+    P["lm_head.weight"] = P["backbone.embedding.weight"]
+    for i in range(layers):
+        pre = f"backbone.layers.{i}."
+        P.update({pre + "norm.weight": np.ones(Dm, np.float32), pre + "norm2.weight": np.ones(Dm, np.float32),
+                  pre + "mixer.in_proj.weight": w(2 * Dm + 3 * D + 2 * R, Dm),
+                  pre + "mixer.state_proj.weight": w(Dm, D), pre + "mixer.ent_proj.weight": w(Dm, D),
+                  pre + "mixer.out_proj.weight": w(Dm, Dm), pre + "mixer.cross_layer_q_proj.weight": w(R, D),
+                  pre + "mixer.decay_bias": np.full(D, 3.0, np.float32),
+                  pre + "mixer.local_entanglement_bias": (rng.standard_normal(16) * 0.3).astype(np.float32),
+                  pre + "mlp.gate_proj.weight": w(Fd, Dm), pre + "mlp.up_proj.weight": w(Fd, Dm),
+                  pre + "mlp.down_proj.weight": w(Dm, Fd)})
+    cfg = dict(CFG, n_layer=layers, entanglement_threshold=0.1, entanglement_scale=0.2, bit_eps=1e-5, rope_base=1e4,
+               state_scan_chunk_size=16, use_mimo=False, n_heads=4, mimo_rank=4, norm_epsilon=1e-5)
+    ids = rng.integers(0, V, size=(1, tokens))
+    O.memo_weights(True)
+    O.model_forward(P, cfg, ids[:, :16], logits_to_keep=1)  # ternarise once, as the reference caches in eval
+    tm = {}
+    t0 = time.perf_counter()
+    O.model_forward(P, cfg, ids, logits_to_keep=1, timings=tm)
+    t1 = time.perf_counter()
+    O.memo_weights(False)
+    t_layers, t_head = tm["layers_done"] - t0, t1 - tm["layers_done"]
+    t_model = t_layers * CFG["n_layer"] / layers + t_head
+    return tokens / t_model, t1 - t0
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    n = cpu_threads()
+    for _ in range(args.warmup):
+        cpu_sample(layers=1, tokens=32)
+    vals = [cpu_sample(layers=2, tokens=128)[0] for _ in range(args.steps)]
+    v = statistics.median(vals)
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": BATCH * SEQ / v * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (numpy restatement of the reference torch path, exact integer GEMMs)",
+            "data": "synthetic", "impl": "reference", "config": workload(world),
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": n, "kind": "port",
+                             "sample": "2 of 32 full-width layers, 1 x 128 tokens per step; layer time x16 + head"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU leg
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, gpu):
+        self.path = tempfile.mktemp(suffix=".csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        for ln in open(self.path):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(self.NAMES, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_gpu(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from tesm_b200 import _lib, ops
+    from tesm_b200.models import TESMConfig, TESMLMHeadModel
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(0)
+    cfg = TESMConfig(kernel_backend="b200", **CFG)
+    with torch.device(dev):
+        model = TESMLMHeadModel(cfg, dtype=torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1000 + rank)
+    ids_host = torch.randint(0, CFG["vocab_size"], (BATCH, SEQ), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+    logits_host = torch.empty(BATCH, 1, CFG["vocab_size"], dtype=torch.bfloat16).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            model(ids, logits_to_keep=1)
+        barrier()
+        clocks = Clocks(local_rank) if rank == 0 else None
+        n0 = _lib.launch_count
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(args.steps):
+            model(ids, logits_to_keep=1)
+        e1.record()
+        barrier()
+        launches = (_lib.launch_count - n0) // args.steps
+        clk = clocks.stop() if clocks else None
+        t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+
+        # end to end: pinned host ids -> device, forward, next-token logits -> pinned host
+        barrier()
+        f0, f1 = ev(), ev()
+        f0.record()
+        for _ in range(args.steps):
+            ids.copy_(ids_host, non_blocking=True)
+            out, _ = model(ids, logits_to_keep=1)
+            logits_host.copy_(out.logits, non_blocking=True)
+        f1.record()
+        barrier()
+        t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+
+        # roofline of the dominant kernel (the tcgen05 int8 GEMM): events around each of its
+        # launches in one extra instrumented step, on the launching (current) stream
+        rec = []
+        orig = ops.gemm
+
+        def timed_gemm(codes, inv, pw, M, out_dtype, out=None, acc=False):
+            a, b = ev(), ev()
+            a.record()
+            r = orig(codes, inv, pw, M, out_dtype, out, acc)
+            b.record()
+            rec.append((a, b, 2.0 * M * pw.N * pw.K, M * pw.K + pw.N * pw.K + M * pw.N * 2))
+            return r
+
+        ops.gemm = timed_gemm
+        s0, s1 = ev(), ev()
+        s0.record()
+        model(ids, logits_to_keep=1)
+        s1.record()
+        torch.cuda.synchronize()
+        ops.gemm = orig
+        g_ms = sum(a.elapsed_time(b) for a, b, _, _ in rec)
+        g_ops = sum(o for _, _, o, _ in rec)
+        g_bytes = sum(bb for _, _, _, bb in rec)
+        step_ms = s0.elapsed_time(s1)
+        status = ops.device_status()
+
+    if rank != 0:
+        return 0
+    peaks, src = load_peaks()
+    # B200's dense int8 tensor rate is twice its bf16 rate; the GEMM runs inside a long step, so
+    # the sustained bf16 figure is the base of the denominator.
+    peak_int8 = 2.0 * peaks["bf16_tflops_sustained"]
+    achieved = g_ops / (g_ms / 1e3) / 1e12
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "gemm_i8_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            tj = json.load(f)
+        traffic = tj["dram_bytes"] / tj["ops"] * g_ops / len(rec)  # ncu bytes per op, scaled to one launch
+    tokens = BATCH * SEQ * world
+    cpu_v, cpu_dt = cpu_sample(layers=2, tokens=96)
+    line = {
+        "metric": METRIC, "value": tokens / (t_dev / args.steps), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_dev / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 x int2 -> int32 GEMMs; fp32 scan/entanglement; bf16 activations",
+        "data": "synthetic (uniform token ids, random-init weights seed 0)", "config": workload(world),
+        "e2e": {"value": tokens / (t_e2e / args.steps), "unit": UNIT, "h2d_bytes_per_step": BATCH * SEQ * 8,
+                "d2h_bytes_per_step": BATCH * CFG["vocab_size"] * 2},
+        "roofline": {"bound": "tensor", "kernel": "tesm::tc::k_gemm_i8 (tcgen05.mma kind::i8)",
+                     "achieved": achieved, "peak": peak_int8, "unit": "TOPS", "frac": achieved / peak_int8,
+                     "traffic": traffic, "launches_per_step": len(rec), "avg_launch_ms": g_ms / len(rec),
+                     "algorithmic_bytes_per_launch": g_bytes / len(rec), "share_of_step": g_ms / step_ms,
+                     "peak_source": f"2 x bf16_tflops_sustained, {src} MEASURED_PEAKS.json (int8 = 2x bf16 dense)"},
+        "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"oracle port, 2 of 32 full-width layers, 1 x 96 tokens ({cpu_dt:.1f} s); "
+                                   f"layer time x16 + head"},
+        "clocks": clk, "gpu_launches": launches, "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_kernel_case(args):
+    """Small standalone case of the dominant kernel for ncu captures: one int8 tcgen05 GEMM
+    of in_proj-like shape M=16384, N=11008, K=4096 (operands 109 MB + 360 MB output > L2)."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    M, N, K = 16384, 11008, 4096
+    w = torch.randn(N, K, device="cuda") * 0.02
+    pw = ops.pack_weight(w, 1e-5, with_tern=True)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    codes, inv, _ = ops.quant_act(x, 1e-5, ops.LAYOUT_ROWMAJOR)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(args.warmup):
+        ops.gemm(codes, inv, pw, M, torch.bfloat16, out)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        ops.gemm(codes, inv, pw, M, torch.bfloat16, out)
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / args.steps / 1e3
+    print(json.dumps({"kernel": "gemm_i8", "M": M, "N": N, "K": K, "ms": t * 1e3, "TOPS": 2.0 * M * N * K / t / 1e12,
+                      "algorithmic_bytes": M * K + N * K + M * N * 2, "ops": 2.0 * M * N * K}), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--kernel", default=None, choices=["gemm"], help="run the small ncu case of one kernel")
+    args = ap.parse_args()
+    if args.kernel:
+        return run_kernel_case(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        return run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

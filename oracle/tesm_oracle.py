@@ -10,6 +10,7 @@ restates.  Arrays are numpy; float32 unless stated.  ``dtype`` arguments take
 from __future__ import annotations
 
 import math
+import time
 
 import numpy as np
 
@@ -18,11 +19,11 @@ F64 = np.float64
 
 __all__ = [
     "bf16_round", "cast", "ternary_weight", "pack_int2", "unpack_int2",
-    "quant_act", "int_gemm", "bitlinear", "rope", "rope_mimo",
+    "quant_act", "quant_tie_margin", "int_gemm", "bitlinear", "rope", "rope_mimo",
     "scan_chunked_f64", "scan_seq", "ternary", "local_ent", "local_ent_mimo",
     "global_rel_bias", "global_ent", "siso_forward", "siso_decode",
     "mimo_forward", "mimo_decode", "alloc_cache", "rmsnorm", "ffn",
-    "model_forward", "model_alloc_cache", "sigmoid",
+    "model_forward", "model_alloc_cache", "sigmoid", "memo_weights",
 ]
 
 
@@ -108,12 +109,48 @@ def quant_act(x, eps=1e-5, dtype="float32"):
     return c, s.astype(F32)
 
 
+def quant_tie_margin(x, eps=1e-5, dtype="float32"):
+    """Per-row distance of x*s to the nearest rounding tie (k + 0.5) in the int8 activation
+    quantisation of :func:`quant_act`.  A row whose margin is below the fp32 error of x*s
+    (~1e-5) can legitimately round one element to a neighbouring code."""
+    x = cast(x, dtype)
+    mx = cast(np.maximum(np.abs(x).max(axis=-1), F32(eps)).astype(F32), dtype)
+    s = cast(cast(F32(1.0) / mx, dtype) * F32(127.0), dtype)
+    p = np.abs(cast(x * s[..., None], dtype)).astype(np.float64)
+    return np.abs(p - np.floor(p) - 0.5).min(axis=-1)
+
+
 def int_gemm(codes, t):
     """Exact integer product sum_k c[m,k] * t[n,k] (the int32 accumulator)."""
-    c = np.asarray(codes, dtype=np.int64).reshape(-1, codes.shape[-1])
-    acc = c @ np.asarray(t, dtype=np.int64).T
+    # a floating-point GEMM is exact here: |c*t| <= 128, so every partial sum is an integer
+    # below K*128; fp32 holds those exactly while K*128 < 2^24, fp64 beyond
+    K = codes.shape[-1]
+    ft = np.float32 if K * 128 < 2 ** 24 else np.float64
+    c = np.asarray(codes, dtype=ft).reshape(-1, K)
+    acc = c @ np.asarray(t, dtype=ft).T
     assert np.abs(acc).max(initial=0) < 2 ** 31
-    return acc.astype(np.int32).reshape(*codes.shape[:-1], t.shape[0])
+    return np.rint(acc).astype(np.int32).reshape(*codes.shape[:-1], t.shape[0])
+
+
+_WEIGHT_MEMO = None
+
+
+def memo_weights(enable=True):
+    """Cache ternary weights by array identity, like the reference's eval-mode cache
+    (tesm.py:226-236); used when timing the oracle as a CPU baseline."""
+    global _WEIGHT_MEMO
+    _WEIGHT_MEMO = {} if enable else None
+
+
+def _ternary_cached(w, eps, dtype, per_row):
+    if _WEIGHT_MEMO is None:
+        return ternary_weight(w, eps, dtype, per_row)
+    key = (id(w), eps, dtype, per_row)
+    hit = _WEIGHT_MEMO.get(key)
+    if hit is None:
+        hit = ternary_weight(w, eps, dtype, per_row)
+        _WEIGHT_MEMO[key] = hit
+    return hit
 
 
 def bitlinear(x, w, eps=1e-5, dtype="float32", per_row=False, return_acc=False):
@@ -122,7 +159,7 @@ def bitlinear(x, w, eps=1e-5, dtype="float32", per_row=False, return_acc=False):
     y = F.linear(c/s, t*deq) evaluated in float64 and rounded to ``dtype``.
     """
     x = np.asarray(x, dtype=F32)
-    t, _, deq = ternary_weight(w, eps, dtype, per_row)
+    t, _, deq = _ternary_cached(w, eps, dtype, per_row)
     c, s = quant_act(x, eps, dtype)
     acc = int_gemm(c, t)
     y = acc.astype(F64) * (1.0 / s.astype(F64))[..., None]
@@ -354,8 +391,10 @@ def siso_forward(P, cfg, u, cross=None, prev_state=None, cache=None, details=Fal
     y = (local + gate * sp + ep).astype(F32)
     out = bitlinear(y, P["out_proj.weight"], eps)
     if details:
+        tie = np.minimum(np.minimum(quant_tie_margin(np.tanh(ent), eps), quant_tie_margin(chg, eps)),
+                         quant_tie_margin(y, eps))
         return out, final, states, dict(proj=proj, q=q, k=k, states=states, avg=avg, ent=ent, chg=chg,
-                                        y=y, scores=scores, decay=decay, update=update)
+                                        y=y, scores=scores, decay=decay, update=update, tie_margin=tie)
     return out, final, states
 
 
@@ -536,10 +575,8 @@ def rmsnorm(x, w, eps=1e-5):
 
 def ffn(P, x, eps=1e-5):
     """``FeedForward.forward`` grouped gate/up path (mixer_seq_simple.py:45-67)."""
-    g = np.asarray(P["gate_proj.weight"], F32)
-    u = np.asarray(P["up_proj.weight"], F32)
-    tg, _, dg = ternary_weight(g, eps)
-    tu, _, du = ternary_weight(u, eps)
+    tg, _, dg = _ternary_cached(P["gate_proj.weight"], eps, "float32", False)
+    tu, _, du = _ternary_cached(P["up_proj.weight"], eps, "float32", False)
     c, s = quant_act(x, eps)
     inv_s = (1.0 / s.astype(F64))[..., None]
     gx = (int_gemm(c, tg).astype(F64) * inv_s * dg).astype(F32)
@@ -553,7 +590,7 @@ def model_alloc_cache(cfg, batch):
     return {i: alloc_cache(cfg, batch, cfg.get("use_mimo", False)) for i in range(cfg["n_layer"])}
 
 
-def model_forward(P, cfg, ids, cache=None):
+def model_forward(P, cfg, ids, cache=None, logits_to_keep=0, timings=None):
     """``TESMLMHeadModel.forward`` logits in eval (mixer_seq_simple.py:171-242, :290-345).
 
     P holds the reference state_dict names (``backbone.layers.{i}.mixer.*`` ...).
@@ -595,4 +632,8 @@ def model_forward(P, cfg, ids, cache=None):
         hidden = ffn(fp, h2)
     residual = (hidden + residual).astype(F32)
     hf = rmsnorm(residual, P["backbone.norm_f.weight"], neps)
+    if logits_to_keep > 0:
+        hf = hf[:, -logits_to_keep:]
+    if timings is not None:
+        timings["layers_done"] = time.perf_counter()
     return (hf.astype(F64) @ P["lm_head.weight"].astype(F64).T).astype(F32)

@@ -94,7 +94,15 @@ def check(status: int, what: str):
         raise TesmError(f"tesm_b200 {what} failed (status {status}): {last_error()}")
 
 
+# number of entry-point calls that enqueue device work (bench.py reports it as gpu_launches)
+launch_count = 0
+_NO_LAUNCH = {"tesm_b200_version", "tesm_b200_last_error", "tesm_b200_device_status", "tesm_b200_scan_workspace"}
+
+
 def call(name: str, *args):
+    global launch_count
+    if name not in _NO_LAUNCH:
+        launch_count += 1
     check(getattr(get(), name)(*args), name)
 
 

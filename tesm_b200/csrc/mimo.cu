@@ -68,12 +68,14 @@ __global__ void k_mimo_local_ent(MimoEntParams p) {
     float mo[RM];
 #pragma unroll
     for (int r = 0; r < RM; ++r) mo[r] = p.mimo_o[((int64_t)h * RM + r) * p.D + d];
-    float win[RM][W];
+    float win[RM][W];  // before the first shift win[r][o] = states_r[t0 - 1 - o]
+#pragma unroll
+    for (int r = 0; r < RM; ++r) win[r][W - 1] = 0.f;
 #pragma unroll
     for (int o = 1; o < W; ++o) {
       const int j = t0 - o;
 #pragma unroll
-      for (int r = 0; r < RM; ++r) win[r][o] = j >= 0 ? p.states[((row0 + j) * RM + r) * C + c] : 0.f;
+      for (int r = 0; r < RM; ++r) win[r][o - 1] = j >= 0 ? p.states[((row0 + j) * RM + r) * C + c] : 0.f;
     }
     for (int t = 0; t < nt; ++t) {
       const int64_t row = row0 + t0 + t;

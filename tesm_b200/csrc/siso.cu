@@ -78,11 +78,13 @@ __global__ void k_siso_local_ent(LocalEntParams p) {
   __syncthreads();
   // per channel: sliding window of states in registers
   for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+    // before the first shift win[o] holds states[t0 - 1 - o]; after it, win[o] = states[t - o]
     float win[W];
+    win[W - 1] = 0.f;
 #pragma unroll
     for (int o = 1; o < W; ++o) {
       const int j = t0 - o;
-      win[o] = j >= 0 ? p.states[(row0 + j) * p.D + d] : 0.f;
+      win[o - 1] = j >= 0 ? p.states[(row0 + j) * p.D + d] : 0.f;
     }
     for (int t = 0; t < nt; ++t) {
 #pragma unroll

@@ -1,8 +1,11 @@
 """Scan / entanglement / decode kernels and the mirror modules vs oracle + golden (GPU).
 
 Tolerances (max|out-ref| / max|ref|): 1e-3 for fp32 layer outputs (north_star), 1e-5 for
-the fp32 scan states; ternary decisions whose score lies within 1e-4 of the threshold are
-"ambiguous" -- positions touched by one are excluded and must stay below 1e-4 of all.
+the fp32 scan states.  Flip-aware comparison: a ternary decision whose oracle score lies
+within 2e-5 * max(1, |score|) of the threshold (about 5x the fp32 rounding spread of a
+64-term dot product) may legitimately flip, and so may an int8 activation code whose x*s
+lies within 2e-5 of a rounding tie; positions touched by either are excluded from the tight
+check and must stay below 1% (kernels) / 5% (layers) of all positions.
 """
 import math
 
@@ -33,7 +36,7 @@ def _split(P, Dm, C, Rc):
     return [P[:, o[i]:o[i + 1]] for i in range(7)]
 
 
-def _ambiguous_rows(scores, thr, tol=1e-4):
+def _ambiguous_rows(scores, thr, tol=2e-5):
     s = np.abs(np.nan_to_num(scores, nan=1e9))
     amb = np.abs(s - thr) < tol * np.maximum(1.0, s)
     return amb.reshape(amb.shape[0], -1).any(-1) if amb.ndim > 1 else amb
@@ -80,7 +83,7 @@ def test_siso_local_ent(ops, B, L, D, R, W, cross):
     ops.siso_local_ent(P.cuda(), B, L, Dm, D, R, W, cr.cuda() if cross else None, bias.cuda(), st.cuda(), thr, es,
                        1e4, th, ch)
     amb = _ambiguous_rows(sc.reshape(B * L, -1), thr)
-    assert amb.mean() < 1e-4 or amb.sum() <= 1
+    assert amb.mean() < 1e-2
     keep = ~amb
     assert max_rel(th.cpu().numpy()[keep], np.tanh(ent).reshape(B * L, D)[keep]) <= 1e-5
     assert max_rel(ch.cpu().numpy()[keep], (ent - st.numpy()).reshape(B * L, D)[keep]) <= 1e-4
@@ -169,9 +172,17 @@ def test_siso_module_golden(lib, c):
     cross = randn((B, L, m.d_state), 2).cuda() if c.get("cross") else None
     prev = randn((B, m.d_state), 4).double().cuda() if c.get("prev") else None
     ip = {"state_cache": m.allocate_inference_cache(B, m.max_seq_len)} if c.get("decode") else None
+    # oracle scores of the same layer (weights rebuilt from the seed, on the CPU) locate the
+    # ternary decisions on the threshold and int8 rounding ties; either only moves its position
+    P = params_np(build_siso(c["kw"]))
+    _, _, _, det = O.siso_forward(P, siso_cfg(m), x.cpu().numpy(), None if cross is None else cross.cpu().numpy(),
+                                  None if prev is None else prev.cpu().numpy(), None, details=True)
+    amb = _ambiguous_rows(det["scores"].reshape(B * L, -1), m.entanglement_threshold).reshape(B, L)
+    amb |= det["tie_margin"] < 2e-5
+    assert amb.mean() < 5e-2
     with torch.no_grad():
         y, fs = m(x, inference_params=ip, cross_layer_state=cross, prev_state=prev)
-        assert max_rel(y.cpu().numpy(), g["y"]) <= 1e-3
+        assert max_rel(y.cpu().numpy()[~amb], g["y"][~amb]) <= 1e-3
         assert max_rel(fs.cpu().numpy(), g["final"]) <= 1e-5
         assert max_rel(m._last_cross_layer_state.cpu().numpy(), g["states"]) <= 1e-5
         for s in range(c.get("decode", 0)):
