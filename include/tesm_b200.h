@@ -181,6 +181,20 @@ int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const float *residual
 /* FeedForward gate: out[m, f] = silu(gu[m, f]) * gu[m, F + f] (mixer_seq_simple.py:59-66). */
 int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, void *out, int odtype, tesm_stream_t stream);
 
+/* Allocation-free SISO scan.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory (runtimes with a fixed memory plan, embeddings of this
+ * library without a device allocator).  Same computation and arguments as
+ * tesm_b200_siso_scan minus the workspace: the look-back scratch is a fixed 8 MiB array
+ * inside the library, present on every GPU that loads it until the process exits.  Shapes
+ * whose scratch (tesm_b200_scan_workspace) exceeds 8 MiB are rejected with TESM_EUNSUPPORTED.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  Every call shares the one array, so calls
+ * that overlap on the GPU (different streams, or several host threads) race; serialise them.
+ * Nothing is allocated or freed. */
+int tesm_b200_siso_scan_noalloc(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                int64_t D, int64_t R, const float *decay_bias, const double *h0, float *states,
+                                float *final_f32, double *final_f64, tesm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,3 +9,4 @@
 #include "mimo.cu"
 #include "decode.cu"
 #include "model.cu"
+#include "noalloc.cu"
