@@ -178,8 +178,20 @@ int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const float *residual
                                 int64_t ld_codes, int layout, float *inv_scale, int32_t *rowsum, void *y_out,
                                 int ydtype, tesm_stream_t stream);
 
-/* FeedForward gate: out[m, f] = silu(gu[m, f]) * gu[m, F + f] (mixer_seq_simple.py:59-66). */
-int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, void *out, int odtype, tesm_stream_t stream);
+/* FeedForward gate (mixer_seq_simple.py:59-66): out[m, f] = silu(gate) * up, where gu (M, 2F) holds
+ * [gate | up] halves (blk = 0) or blocks of blk gate columns each followed by the matching blk up
+ * columns (blk = 128: the interleaved layout of tesm_b200_gemm_i8_swiglu's weights). */
+int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, int64_t blk, void *out, int odtype,
+                       tesm_stream_t stream);
+
+/* Grouped gate/up BitLinear with the SiLU gate in the GEMM epilogue (replaces
+ * FeedForward._grouped_gate_up + F.silu(gate)*up, mixer_seq_simple.py:45-66): tern (2F, ld_tern)
+ * holds the gate and up ternary rows interleaved in blocks of 128 ([gate 0..127 | up 0..127 | gate
+ * 128..255 | ...]), w_deq (2F) the per-row dequantisation factor in the same order; out (M, F) =
+ * silu(acc_g * inv_scale * deq_g) * (acc_u * inv_scale * deq_u).  F % 128 == 0. */
+int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
+                             int64_t ld_tern, const float *w_deq, int64_t M, int64_t F, int64_t K, void *out,
+                             int out_dtype, int64_t ldo, tesm_stream_t stream);
 
 /* Allocation-free SISO scan.  No counterpart in the reference: it exists for callers that
  * cannot allocate device memory (runtimes with a fixed memory plan, embeddings of this

@@ -41,6 +41,7 @@ struct Params {
   int64_t ld_acc;
   int num_m_tiles, num_n_tiles, num_k_blocks, group_m;
   int vec_store;
+  int swiglu;  // 1: weight rows interleaved [128 gate | 128 up] per tile; out = silu(g) * u, width N/2
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -239,6 +240,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool row_ok = row < p.M;
       const float xs = row_ok ? p.inv_scale[row] : 0.f;
       const float wd0 = p.w_deq[0];
+      if (BN == 256 && p.swiglu) {
+        // columns [0,128) of the tile are gate rows, [128,256) the matching up rows
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rg[32], ru[32];
+          const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+          tmem_ld32(tbase + c * 32, rg);
+          tmem_ld32(tbase + 128 + c * 32, ru);
+          const int ng = nt * BN + c * 32;    // weight row of the first gate column
+          const int no = nt * 128 + c * 32;   // output column
+          if (!row_ok || ng >= p.N) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float g = (float)(int32_t)rg[j] * xs * p.w_deq[ng + j];
+            const float u = (float)(int32_t)ru[j] * xs * p.w_deq[ng + 128 + j];
+            v[j] = (g / (1.f + expf(-g))) * u;
+          }
+          const int nout = p.N / 2;
+          if (p.vec_store && no + 32 <= nout) {
+            if (p.out_dtype == TESM_BF16) {
+              uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + (int64_t)row * p.ldo + no);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                __nv_bfloat162 h[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+                dst[j] = *reinterpret_cast<uint4 *>(h);
+              }
+            } else {
+              float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + (int64_t)row * p.ldo + no);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (no + j < nout) store_f(p.out, p.out_dtype, (int64_t)row * p.ldo + no + j, v[j]);
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -348,6 +393,32 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
 }  // namespace tesm
 
 using namespace tesm;
+
+extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, const float *inv_scale,
+                                        const int8_t *tern, int64_t ld_tern, const float *w_deq, int64_t M, int64_t F,
+                                        int64_t K, void *out, int out_dtype, int64_t ldo, tesm_stream_t stream) {
+  TESM_REQUIRE(codes && inv_scale && tern && w_deq && out, "gemm_i8_swiglu: null pointer");
+  TESM_REQUIRE(M >= 0 && F > 0 && F % 128 == 0 && K > 0 && M < (1ll << 31), "gemm_i8_swiglu: need F % 128 == 0");
+  if (M == 0) return TESM_OK;
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_swiglu: out dtype");
+  TESM_REQUIRE(ld_codes >= K && ld_codes % 16 == 0 && ((uintptr_t)codes & 15) == 0, "gemm_i8_swiglu: codes layout");
+  TESM_REQUIRE(ld_tern >= K && ld_tern % 16 == 0 && ((uintptr_t)tern & 15) == 0, "gemm_i8_swiglu: tern layout");
+  TESM_REQUIRE(ldo >= F, "gemm_i8_swiglu: ldo < F");
+  tc::Params p = {};
+  p.inv_scale = inv_scale;
+  p.w_deq = w_deq;
+  p.per_row = 1;
+  p.M = (int)M;
+  p.N = (int)(2 * F);
+  p.K = (int)K;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.ldo = ldo;
+  p.swiglu = 1;
+  const int esz = out_dtype == TESM_BF16 ? 2 : 4;
+  p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
+  return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
+}
 
 extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
                                  int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K,

@@ -4,6 +4,7 @@
 // Block.forward / RMSNorm (tesm_ssm/modules/block.py:14-45), FeedForward.forward
 // (mixer_seq_simple.py:59-67), prefill cache write (tesm.py:1235-1253, tesm_mimo.py:1022-1038).
 #include "layer_common.cuh"
+#include "rowio.cuh"
 
 namespace tesm {
 
@@ -21,56 +22,58 @@ __global__ void k_embed(const int64_t *ids, int64_t M, int L, const void *emb, c
 
 // residual_out = x (+ residual); y = residual_out * rsqrt(mean(residual_out^2) + eps) * w;
 // then the per-token int8 codes of y (same arithmetic as quant.cu), optionally y itself.
+// Rows are held in registers (GPT 16-element groups per thread) with 16-byte vector I/O.
 template <int GPT>
 __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *residual, float *residual_out,
                                     const float *w, float eps, int K, float qeps, int8_t *codes, int64_t ld_codes,
                                     int layout, int64_t groups_out, float *inv_scale, int32_t *rowsum, void *y_out,
-                                    int ydtype) {
+                                    int ydtype, int vec) {
   __shared__ float redf[32];
   __shared__ int redi[32];
-  __shared__ double redd[32];
   const int64_t row = blockIdx.x;
   const int64_t groups_in = (K + 15) / 16;
+  const int xsz = xdtype == TESM_BF16 ? 2 : 4, ysz = ydtype == TESM_BF16 ? 2 : 4;
+  const void *xrow = reinterpret_cast<const uint8_t *>(x) + row * K * xsz;
   float v[GPT][16];
-  double ss = 0.0;
+  float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < GPT; ++j) {
     const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+    if (g < groups_in) {
+      load16(xrow, xdtype, g * 16, K, vec, v[j]);
+      if (residual) {
+        float r[16];
+        load16(residual + row * K, TESM_F32, g * 16, K, vec, r);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int64_t k = g * 16 + e;
-      float r = 0.f;
-      if (g < groups_in && k < K) {
-        r = load_f(x, xdtype, row * K + k);
-        if (residual) r += residual[row * K + k];
-        if (residual_out) residual_out[row * K + k] = r;
+        for (int e = 0; e < 16; ++e) v[j][e] += r[e];
       }
-      v[j][e] = r;
-      ss += (double)r * (double)r;
+      if (residual_out) store16(residual_out + row * K, TESM_F32, g * 16, K, vec, v[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[j][e] = 0.f;
     }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss = fmaf(v[j][e], v[j][e], ss);
   }
-  ss = block_reduce(ss, redd, [](double a, double b) { return a + b; }, 0.0);
-  const float rs = rsqrtf((float)(ss / (double)K) + eps);
+  ss = block_reduce(ss, redf, [](float a, float b) { return a + b; }, 0.f);
+  const float rs = rsqrtf(ss / (float)K + eps);
   float amax = 0.f;
 #pragma unroll
   for (int j = 0; j < GPT; ++j) {
     const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+    if (g < groups_in) {
+      float wv[16];
+      load16(w, TESM_F32, g * 16, K, vec, wv);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int64_t k = g * 16 + e;
-      float y = 0.f;
-      if (g < groups_in && k < K) {
-        y = (v[j][e] * rs) * w[k];
-        if (y_out) store_f(y_out, ydtype, row * K + k, y);
-      }
-      v[j][e] = y;
-      amax = fmaxf(amax, fabsf(y));
+      for (int e = 0; e < 16; ++e) v[j][e] = (v[j][e] * rs) * wv[e];
+      if (y_out) store16(reinterpret_cast<uint8_t *>(y_out) + row * K * ysz, ydtype, g * 16, K, vec, v[j]);
     }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[j][e]));
   }
   if (!codes) return;
   amax = block_reduce(amax, redf, [](float a, float b) { return fmaxf(a, b); }, 0.f);
-  const float mx = fmaxf(amax, qeps);
-  const float s = __fmul_rn(__frcp_rn(mx), 127.f);
+  const float s = act_scale(amax, qeps, TESM_F32);
   if (threadIdx.x == 0) inv_scale[row] = __frcp_rn(s);
   int csum = 0;
   int8_t *crow = codes + row * ld_codes;
@@ -81,24 +84,10 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
     int c[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      c[e] = (int)fminf(fmaxf(rintf(__fmul_rn(v[j][e], s)), -128.f), 127.f);
+      c[e] = act_code(v[j][e], s, TESM_F32);
       csum += c[e];
     }
-    uint32_t wv[4];
-    if (layout == TESM_LAYOUT_GEMV) {
-#pragma unroll
-      for (int sw = 0; sw < 4; ++sw)
-        wv[sw] = (uint32_t)(uint8_t)c[sw] | ((uint32_t)(uint8_t)c[4 + sw] << 8) |
-                 ((uint32_t)(uint8_t)c[8 + sw] << 16) | ((uint32_t)(uint8_t)c[12 + sw] << 24);
-      const int64_t s256 = g >> 4, tig = (g >> 2) & 3, u = g & 3;
-      reinterpret_cast<uint4 *>(crow)[s256 * 16 + u * 4 + tig] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        wv[q] = (uint32_t)(uint8_t)c[4 * q] | ((uint32_t)(uint8_t)c[4 * q + 1] << 8) |
-                ((uint32_t)(uint8_t)c[4 * q + 2] << 16) | ((uint32_t)(uint8_t)c[4 * q + 3] << 24);
-      reinterpret_cast<uint4 *>(crow)[g] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    }
+    store_codes16(crow, g, layout, c);
   }
   if (rowsum) {
     csum = block_reduce(csum, redi, [](int a, int b) { return a + b; }, 0);
@@ -106,14 +95,24 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
   }
 }
 
-// out[m, f] = silu(gu[m, f]) * gu[m, F + f]
-__global__ void k_silu_mul(const void *gu, int dtype, int64_t M, int F, void *out, int odtype) {
+// out[m, f] = silu(gate[m, f]) * up[m, f]; gu holds [gate | up] halves (blk == 0) or
+// blocks of `blk` gate columns followed by the matching `blk` up columns.
+__global__ void k_silu_mul(const void *gu, int dtype, int64_t M, int F, void *out, int odtype, int blk) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * F) return;
   const int64_t m = i / F;
   const int f = (int)(i - m * F);
-  const float g = load_f(gu, dtype, m * 2 * F + f);
-  const float u = load_f(gu, dtype, m * 2 * F + F + f);
+  int64_t gi, ui;
+  if (blk) {
+    const int b = f / blk, j = f - b * blk;
+    gi = m * 2 * F + (int64_t)b * 2 * blk + j;
+    ui = gi + blk;
+  } else {
+    gi = m * 2 * F + f;
+    ui = gi + F;
+  }
+  const float g = load_f(gu, dtype, gi);
+  const float u = load_f(gu, dtype, ui);
   store_f(out, odtype, i, (g * sigmoidf_(g)) * u);
 }
 
@@ -173,18 +172,23 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
   int64_t threads = round_up(ceil_div(groups_out, 4), 32);
   if (threads < 32) threads = 32;
   TESM_REQUIRE(threads <= 1024, "add_rmsnorm_quant: K too large");
+  const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && (!residual || (uintptr_t)residual % 16 == 0) &&
+                  (!residual_out || (uintptr_t)residual_out % 16 == 0) && ((uintptr_t)weight % 16 == 0) &&
+                  (!y_out || (uintptr_t)y_out % 16 == 0);
   k_add_rmsnorm_quant<4><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
       x, xdtype, residual, residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale,
-      rowsum, y_out, ydtype);
+      rowsum, y_out, ydtype, vec);
   return check_launch("add_rmsnorm_quant");
 }
 
-extern "C" int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, void *out, int odtype,
-                                  tesm_stream_t stream) {
+extern "C" int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, int64_t blk, void *out,
+                                  int odtype, tesm_stream_t stream) {
+  TESM_REQUIRE(blk == 0 || F % blk == 0, "silu_mul: F must be a multiple of the interleave block");
   TESM_REQUIRE(gu && out && M >= 0 && F > 0, "silu_mul: bad argument");
   if (M == 0) return TESM_OK;
   const int64_t n = M * F;
-  k_silu_mul<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(gu, dtype, M, (int)F, out, odtype);
+  k_silu_mul<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(gu, dtype, M, (int)F, out, odtype,
+                                                                             (int)blk);
   return check_launch("silu_mul");
 }
 

@@ -9,7 +9,7 @@
 //    RNE reproduces torch's bf16 multiply.
 //  * torch.round is round-half-to-even == rintf.
 // This file is compiled without fast-math; explicit _rn intrinsics keep it that way.
-#include "common.cuh"
+#include "rowio.cuh"
 
 namespace tesm {
 
@@ -86,36 +86,36 @@ __global__ void k_pack(const void *__restrict__ w, int dtype, int64_t N, int64_t
 }
 
 // ---------------------------------------------------------------- activation quant
-// One block per row; each thread owns up to GPT 16-element groups (kept in registers).
-// GEMV layout: natural column k = s*256 + tig*64 + u*16 + 4*i + sw is stored at
-// s*256 + u*64 + tig*16 + sw*4 + i (see gemv.cu for the consumer side).
+// One block per row; each thread owns up to GPT 16-element groups kept in registers
+// (16-byte vector loads when the row is aligned).
 constexpr int kQuantGPT = 4;
 
 template <int GPT>
 __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, int64_t ldx, float eps,
                             int8_t *__restrict__ codes, int64_t ld_codes, int layout, int64_t groups_out,
-                            float *__restrict__ inv_scale, int32_t *__restrict__ rowsum) {
+                            float *__restrict__ inv_scale, int32_t *__restrict__ rowsum, int vec) {
   __shared__ float redf[32];
   __shared__ int redi[32];
   const int64_t row = blockIdx.x;
   const int64_t groups_in = (K + 15) / 16;
+  const int esz = dtype == TESM_BF16 ? 2 : 4;
+  const void *xrow = reinterpret_cast<const uint8_t *>(x) + row * ldx * esz;
   float v[GPT][16];
   float amax = 0.f;
 #pragma unroll
   for (int j = 0; j < GPT; ++j) {
     const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+    if (g < groups_in) {
+      load16(xrow, dtype, g * 16, K, vec, v[j]);
+    } else {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int64_t k = g * 16 + e;
-      float xv = 0.f;
-      if (g < groups_in && k < K) xv = load_f(x, dtype, row * ldx + k);
-      v[j][e] = xv;
-      amax = fmaxf(amax, fabsf(xv));
+      for (int e = 0; e < 16; ++e) v[j][e] = 0.f;
     }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[j][e]));
   }
   amax = block_reduce(amax, redf, [](float a, float b) { return fmaxf(a, b); }, 0.f);
-  const float mx = round_to(dtype, fmaxf(amax, eps));
-  const float s = round_to(dtype, __fmul_rn(round_to(dtype, __frcp_rn(mx)), 127.f));
+  const float s = act_scale(amax, eps, dtype);
   if (threadIdx.x == 0) inv_scale[row] = __frcp_rn(s);
   int csum = 0;
   int8_t *crow = codes + row * ld_codes;
@@ -126,27 +126,10 @@ __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, in
     int c[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      float p = rintf(round_to(dtype, __fmul_rn(v[j][e], s)));
-      c[e] = (int)fminf(fmaxf(p, -128.f), 127.f);
+      c[e] = act_code(v[j][e], s, dtype);
       csum += c[e];
     }
-    uint32_t wv[4];
-    if (layout == TESM_LAYOUT_GEMV) {
-      // word sw holds elements e = 4*i + sw in byte i
-#pragma unroll
-      for (int sw = 0; sw < 4; ++sw)
-        wv[sw] = (uint32_t)(uint8_t)c[sw] | ((uint32_t)(uint8_t)c[4 + sw] << 8) |
-                 ((uint32_t)(uint8_t)c[8 + sw] << 16) | ((uint32_t)(uint8_t)c[12 + sw] << 24);
-      const int64_t s256 = g >> 4, tig = (g >> 2) & 3, u = g & 3;
-      const int64_t slot = s256 * 16 + u * 4 + tig;
-      reinterpret_cast<uint4 *>(crow)[slot] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        wv[q] = (uint32_t)(uint8_t)c[4 * q] | ((uint32_t)(uint8_t)c[4 * q + 1] << 8) |
-                ((uint32_t)(uint8_t)c[4 * q + 2] << 16) | ((uint32_t)(uint8_t)c[4 * q + 3] << 24);
-      reinterpret_cast<uint4 *>(crow)[g] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    }
+    store_codes16(crow, g, layout, c);
   }
   if (rowsum) {
     csum = block_reduce(csum, redi, [](int a, int b) { return a + b; }, 0);
@@ -213,7 +196,9 @@ extern "C" int tesm_b200_quant_act(const void *x, int dtype, int64_t M, int64_t 
   int64_t threads = round_up(ceil_div(groups_out, kQuantGPT), 32);
   if (threads < 32) threads = 32;
   TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
+  const int esz = dtype == TESM_BF16 ? 2 : 4;
+  const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
   k_quant_act<kQuantGPT><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-      x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum);
+      x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec);
   return check_launch("quant_act");
 }

@@ -348,9 +348,14 @@ def _norm_quant(norm, x2d, residual, residual_out, qeps):
     return q
 
 
+SWIGLU_BLK = 128
+
+
 def ffn_packed(ffn):
-    """Fused gate/up weight: rows [0, F) gate, [F, 2F) up, each with its own per-tensor
-    ternary scale, expressed as a per-row dequantisation vector (mixer_seq_simple.py:45-57)."""
+    """Fused gate/up weight of one FeedForward (mixer_seq_simple.py:45-57): each projection keeps
+    its own per-tensor ternary scale, expressed as a per-row dequantisation vector.  When
+    d_intermediate % 128 == 0 the rows are interleaved in blocks of 128 ([gate | up] per block)
+    so the tensor-core GEMM applies the SiLU gate in its epilogue."""
     g, u = ffn.gate_proj.weight, ffn.up_proj.weight
     key = (g.data_ptr(), g._version, u.data_ptr(), u._version)
     hit = ffn.__dict__.get("_b200_gu")
@@ -358,28 +363,39 @@ def ffn_packed(ffn):
         Fd, K = g.shape
         Kp = ops.round_up(K, 256)
         dev = g.device
+        blk = SWIGLU_BLK if Fd % SWIGLU_BLK == 0 else 0
         packed = torch.empty(2 * Fd, Kp // 4, device=dev, dtype=torch.uint8)
         tern = torch.empty(2 * Fd, Kp, device=dev, dtype=torch.int8)
         scale = torch.empty(2, device=dev, dtype=torch.float32)
         deq2 = torch.empty(2, device=dev, dtype=torch.float32)
+        tmp_p = torch.empty(Fd, Kp // 4, device=dev, dtype=torch.uint8)
+        tmp_t = torch.empty(Fd, Kp, device=dev, dtype=torch.int8)
+        rows = torch.arange(2 * Fd, device=dev)
         for i, w in enumerate((g, u)):
             wc = w.detach().contiguous()
-            ops.pack_into(wc, ffn.gate_proj.bit_eps, packed[i * Fd:(i + 1) * Fd], tern[i * Fd:(i + 1) * Fd],
-                          scale[i:i + 1], deq2[i:i + 1])
-        deq = deq2.repeat_interleave(Fd)
+            ops.pack_into(wc, ffn.gate_proj.bit_eps, tmp_p, tmp_t, scale[i:i + 1], deq2[i:i + 1])
+            f = torch.arange(Fd, device=dev)
+            dst = (f // blk) * 2 * blk + i * blk + f % blk if blk else f + i * Fd
+            packed[dst] = tmp_p
+            tern[dst] = tmp_t
+            rows[dst] = i
+        deq = deq2[rows]
         pw = ops.PackedWeight(packed, tern, deq.clone(), deq, 2 * Fd, K, True)
-        hit = (key, pw)
+        hit = (key, pw, blk)
         ffn.__dict__["_b200_gu"] = hit
-    return hit[1]
+    return hit[1], hit[2]
 
 
 def ffn_q(ffn, q: ops.QuantAct, act_dtype):
     """``FeedForward.forward`` on pre-quantised input (mixer_seq_simple.py:59-67)."""
-    pw = ffn_packed(ffn)
+    pw, blk = ffn_packed(ffn)
     Fd = ffn.gate_proj.out_features
-    gu = ops.matmul_q(q, pw, act_dtype)
-    h = torch.empty(q.M, Fd, device=gu.device, dtype=act_dtype)
-    ops.silu_mul(gu, Fd, h)
+    if blk and q.layout == ops.LAYOUT_ROWMAJOR:
+        h = ops.gemm_swiglu(q, pw, act_dtype)
+    else:
+        gu = ops.matmul_q(q, pw, act_dtype)
+        h = torch.empty(q.M, Fd, device=gu.device, dtype=act_dtype)
+        ops.silu_mul(gu, Fd, h, blk)
     return linear(ffn.down_proj, h, act_dtype)
 
 

@@ -274,9 +274,19 @@ def add_rmsnorm_quant(x, residual, residual_out, weight, eps, qeps, q: Optional[
               _stream())
 
 
-def silu_mul(gu, F, out):
-    _lib.call("tesm_b200_silu_mul", gu.data_ptr(), dtype_code(gu.dtype), gu.shape[0], F, out.data_ptr(),
+def silu_mul(gu, F, out, blk=0):
+    _lib.call("tesm_b200_silu_mul", gu.data_ptr(), dtype_code(gu.dtype), gu.shape[0], F, blk, out.data_ptr(),
               dtype_code(out.dtype), _stream())
+
+
+def gemm_swiglu(q: QuantAct, pw: PackedWeight, out_dtype, out=None):
+    """Interleaved gate/up weight (blocks of 128 rows) -> silu(gate) * up, width pw.N // 2."""
+    F = pw.N // 2
+    out = out if out is not None else torch.empty(q.M, F, device=q.codes.device, dtype=out_dtype)
+    _lib.call("tesm_b200_gemm_i8_swiglu", q.codes.data_ptr(), q.codes.stride(0), q.inv.data_ptr(), pw.tern.data_ptr(),
+              pw.tern.stride(0), pw.deq.data_ptr(), q.M, F, pw.K, out.data_ptr(), dtype_code(out.dtype),
+              out.stride(0), _stream())
+    return out
 
 
 def device_status() -> int:

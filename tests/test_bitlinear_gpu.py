@@ -153,3 +153,32 @@ def test_module_forward(lib):
     lay.train()
     with pytest.raises(RuntimeError, match="kernel_backend='b200' specified but BitLinear kernel not available"):
         lay(randn(c["xshape"], 1).cuda())
+
+
+@pytest.mark.parametrize("M", [20, 300])
+def test_ffn_swiglu_interleaved(lib, M):
+    """FeedForward with d_intermediate % 128 == 0: gate/up rows interleaved in 128-blocks; the
+    tensor-core path applies silu(gate)*up in the GEMM epilogue, the GEMV path in a kernel."""
+    from tesm_b200.models import FeedForward, TESMConfig
+    cfg = TESMConfig(d_model=256, d_intermediate=384, kernel_backend="b200")
+    torch.manual_seed(0)
+    ffn = FeedForward(cfg)
+    for lin in (ffn.gate_proj, ffn.up_proj, ffn.down_proj):
+        torch.nn.init.normal_(lin.weight, std=0.02)
+    P = {k: v.detach().numpy() for k, v in ffn.state_dict().items()}
+    x = randn((M, 256), 41)
+    ref = O.ffn(P, x.numpy())
+    g, u = ffn.gate_proj.weight.detach().numpy(), ffn.up_proj.weight.detach().numpy()
+    c, s = O.quant_act(x.numpy())
+    tg, _, dg = O.ternary_weight(g)
+    tu, _, du = O.ternary_weight(u)
+    inv = (1.0 / s.astype(np.float64))[:, None]
+    gx = O.int_gemm(c, tg) * inv * dg
+    ux = O.int_gemm(c, tu) * inv * du
+    h = (gx / (1 + np.exp(-gx)) * ux).astype(np.float32)
+    tie = O.quant_tie_margin(h) < 2e-5
+    ffn = ffn.cuda().eval()
+    with torch.no_grad():
+        y = ffn(x.cuda()).cpu().numpy()
+    assert tie.mean() < 5e-2
+    assert max_rel(y[~tie], ref[~tie]) <= 1e-4
