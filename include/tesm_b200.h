@@ -87,6 +87,17 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
  * TMEM accumulators, TMA-staged operands); same contract as tesm_b200_gemv_int2 but the
  * activation codes are row-major (TESM_LAYOUT_ROWMAJOR, ld_codes multiple of 16) and the
  * weights are the int8 ternary matrix from tesm_b200_pack_ternary (ld_tern multiple of 16). */
+/* state_proj + ent_proj + output combine in one tcgen05 GEMM (tesm.py:1256-1260): two TMEM
+ * accumulators, acc1 over the first Kh columns (codes of tanh(ent) x state_proj ternary weights),
+ * acc2 over the next Kh (codes of ent - s x ent_proj weights); the epilogue writes
+ *   out = local + sigmoid(gate) * acc1 * inv1 * deq1[0] + acc2 * inv2 * deq2[0]
+ * with local / gate read from proj at columns c_local / c_gate.  tern (N, ld_tern) = [W_state | W_ent]
+ * ternary rows, each half Kh wide (zero padded), Kh % 128 == 0. */
+int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, int64_t Kh, const float *inv1, const float *inv2,
+                              const int8_t *tern, int64_t ld_tern, const float *deq1, const float *deq2,
+                              const void *proj, int proj_dtype, int64_t ldp, int64_t c_local, int64_t c_gate,
+                              int64_t M, int64_t N, void *out, int out_dtype, int64_t ldo, tesm_stream_t stream);
+
 int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
                       int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K, void *out,
                       int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc, tesm_stream_t stream);
@@ -119,6 +130,16 @@ int tesm_b200_siso_local_ent(const void *proj, int dtype, int64_t ldp, int64_t B
                              int64_t D, int64_t R, int64_t W, const float *cross, const float *bias,
                              const float *states, float thr, float es, float rope_base, void *out_tanh,
                              void *out_chg, int out_dtype, tesm_stream_t stream);
+
+/* Local entanglement fused with the per-token int8 quantisation of its two outputs (the inputs of
+ * state_proj and ent_proj, tesm.py:1256-1257, quantised as BitLinear.quantized_input with eps1 / eps2
+ * after rounding to act_dtype).  codes (B*L, ldc): tanh(ent) codes in [0, D), ent - s codes in
+ * [Dp, Dp + D), zeros elsewhere (Dp = D rounded up to 128, ldc >= 2*Dp); inv1 / inv2 = 1/s per row. */
+int tesm_b200_siso_local_ent_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                   int64_t D, int64_t R, int64_t W, const float *cross, const float *bias,
+                                   const float *states, float thr, float es, float rope_base, int act_dtype,
+                                   float eps1, float eps2, int8_t *codes, int64_t ldc, int64_t Dp, float *inv1,
+                                   float *inv2, tesm_stream_t stream);
 
 /* Relative-position bias vector of global entanglement (tesm.py:970-982), length 2L-1,
  * entry d + L - 1 for d = i - j. */

@@ -54,6 +54,11 @@ SIGNATURES = {
     "tesm_b200_add_rmsnorm_quant": [c_vp, c_int, c_vp, c_vp, c_vp, c_float, c_i64, c_i64, c_float, c_vp, c_i64,
                                     c_int, c_vp, c_vp, c_vp, c_int, c_vp],
     "tesm_b200_silu_mul": [c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int, c_vp],
+    "tesm_b200_siso_local_ent_codes": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                       c_vp, c_float, c_float, c_float, c_int, c_float, c_float, c_vp, c_i64, c_i64,
+                                       c_vp, c_vp, c_vp],
+    "tesm_b200_gemm_i8_combine": [c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_i64, c_i64,
+                                  c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_vp],
     "tesm_b200_gemm_i8_swiglu": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
                                  c_vp],
     "tesm_b200_siso_scan_noalloc": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,

@@ -11,7 +11,7 @@
 //   warps 2..5 : epilogue: tcgen05.ld 32 lanes x 32 columns, scale, convert, store.
 // Every mbarrier wait is bounded; a wait that gives up sets the sticky device status
 // (TESM_ETIMEOUT) and the CTA drains and exits instead of hanging.
-#include "common.cuh"
+#include "rowio.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -42,6 +42,16 @@ struct Params {
   int num_m_tiles, num_n_tiles, num_k_blocks, group_m;
   int vec_store;
   int swiglu;  // 1: weight rows interleaved [128 gate | 128 up] per tile; out = silu(g) * u, width N/2
+  // dual-accumulator combine (DUAL kernels): k-blocks [0, ksplit) accumulate acc1, the rest acc2;
+  // out = local + sigmoid(gate) * acc1*inv_scale*w_deq[0] + acc2*inv_scale2*w_deq2[0]
+  int ksplit;
+  const float *inv_scale2;
+  const float *w_deq2;
+  const void *proj;
+  int proj_dtype;
+  int64_t ldp;
+  int c_local, c_gate;
+  int proj_vec;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -136,7 +146,7 @@ __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int
   mt = first_m + (r - nt * gm);
 }
 
-template <int BN>
+template <int BN, bool DUAL>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -150,7 +160,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : BN;  // TMEM columns of one tile's accumulator(s)
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -206,8 +217,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t buf = tile_i & 1, use = tile_i >> 1;
         if (!mbar_wait(&tempty[buf], (use & 1) ^ 1)) break;
         fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
+          const bool second = DUAL && kb >= p.ksplit;
+          const uint32_t d_tmem = tmem_base + buf * ACC_COLS + (second ? BN : 0);
+          const int kb0 = second ? kb - p.ksplit : kb;
           const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
           if (!mbar_wait(&full[stage], phase)) {
             ok = false;
@@ -219,7 +232,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             // advance 32 bytes along K inside the swizzle atom: +2 in 16-byte units
-            mma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+            mma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
           }
           mma_commit(&empty[stage]);
         }
@@ -240,6 +253,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool row_ok = row < p.M;
       const float xs = row_ok ? p.inv_scale[row] : 0.f;
       const float wd0 = p.w_deq[0];
+      if (DUAL) {
+        const float xs2 = row_ok ? p.inv_scale2[row] : 0.f;
+        const float s1 = xs * wd0, s2 = xs2 * p.w_deq2[0];
+        const int esz = p.proj_dtype == TESM_BF16 ? 2 : 4;
+        const uint8_t *prow = reinterpret_cast<const uint8_t *>(p.proj) + (int64_t)(row_ok ? row : 0) * p.ldp * esz;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r1[32], r2[32];
+          const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + c * 32;
+          tmem_ld32(tbase, r1);
+          tmem_ld32(tbase + BN, r2);
+          const int n0 = nt * BN + c * 32;
+          if (!row_ok || n0 >= p.N) continue;
+          float v[32];
+          const bool full = p.proj_vec && n0 + 32 <= p.N;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float loc[16], gt[16];
+            load16(prow + (int64_t)p.c_local * esz, p.proj_dtype, n0 + 16 * h, p.N, full, loc);
+            load16(prow + (int64_t)p.c_gate * esz, p.proj_dtype, n0 + 16 * h, p.N, full, gt);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int jj = 16 * h + j;
+              const float sig = 1.f / (1.f + expf(-gt[j]));
+              v[jj] = loc[j] + sig * ((float)(int32_t)r1[jj] * s1) + (float)(int32_t)r2[jj] * s2;
+            }
+          }
+          const bool vs = p.vec_store && n0 + 32 <= p.N;
+          uint8_t *orow = reinterpret_cast<uint8_t *>(p.out) + (int64_t)row * p.ldo * (p.out_dtype == TESM_BF16 ? 2 : 4);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float w16[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w16[j] = v[16 * h + j];
+            store16(orow, p.out_dtype, n0 + 16 * h, p.N, vs, w16);
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        continue;
+      }
       if (BN == 256 && p.swiglu) {
         // columns [0,128) of the tile are gate rows, [128,256) the matching up rows
 #pragma unroll 1
@@ -366,7 +421,7 @@ static int make_map(CUtensorMap *map, const void *ptr, int64_t inner, int64_t ou
   return TESM_OK;
 }
 
-template <int BN>
+template <int BN, bool DUAL = false>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
   CUtensorMap ma, mb;
   int rc = make_map(&ma, A, p.K, p.M, lda, BM);
@@ -376,7 +431,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   const size_t smem = 1024 + (size_t)STAGES * (BM * BK + BN * BK) + 256;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_gemm_i8<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_gemm_i8<BN, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
   p.num_m_tiles = (int)ceil_div(p.M, BM);
@@ -385,7 +440,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   p.group_m = 16;
   const int total = p.num_m_tiles * p.num_n_tiles;
   const int grid = total < sm_count() ? total : sm_count();
-  k_gemm_i8<BN><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
+  k_gemm_i8<BN, DUAL><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
   return check_launch("gemm_i8");
 }
 
@@ -418,6 +473,43 @@ extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, c
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
+}
+
+extern "C" int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, int64_t Kh, const float *inv1,
+                                         const float *inv2, const int8_t *tern, int64_t ld_tern, const float *deq1,
+                                         const float *deq2, const void *proj, int proj_dtype, int64_t ldp,
+                                         int64_t c_local, int64_t c_gate, int64_t M, int64_t N, void *out,
+                                         int out_dtype, int64_t ldo, tesm_stream_t stream) {
+  TESM_REQUIRE(codes && inv1 && inv2 && tern && deq1 && deq2 && proj && out, "gemm_i8_combine: null pointer");
+  TESM_REQUIRE(M >= 0 && N > 0 && Kh > 0 && Kh % 128 == 0 && M < (1ll << 31), "gemm_i8_combine: need Kh % 128 == 0");
+  if (M == 0) return TESM_OK;
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_combine: out dtype");
+  if (proj_dtype != TESM_F32 && proj_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_combine: proj dtype");
+  TESM_REQUIRE(ld_codes >= 2 * Kh && ld_codes % 16 == 0 && ((uintptr_t)codes & 15) == 0, "gemm_i8_combine: codes");
+  TESM_REQUIRE(ld_tern >= 2 * Kh && ld_tern % 16 == 0 && ((uintptr_t)tern & 15) == 0, "gemm_i8_combine: tern");
+  TESM_REQUIRE(ldo >= N && ldp >= c_local + N && ldp >= c_gate + N, "gemm_i8_combine: strides");
+  tc::Params p = {};
+  p.inv_scale = inv1;
+  p.w_deq = deq1;
+  p.inv_scale2 = inv2;
+  p.w_deq2 = deq2;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)(2 * Kh);
+  p.ksplit = (int)(Kh / 128);
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.ldo = ldo;
+  p.proj = proj;
+  p.proj_dtype = proj_dtype;
+  p.ldp = ldp;
+  p.c_local = (int)c_local;
+  p.c_gate = (int)c_gate;
+  const int esz = out_dtype == TESM_BF16 ? 2 : 4, psz = proj_dtype == TESM_BF16 ? 2 : 4;
+  p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
+  p.proj_vec = ((uintptr_t)proj % 16 == 0) && ((ldp * psz) % 16 == 0) && ((c_local * psz) % 16 == 0) &&
+               ((c_gate * psz) % 16 == 0);
+  return tc::launch<128, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
 }
 
 extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,

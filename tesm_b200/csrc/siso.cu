@@ -5,6 +5,7 @@
 // column split [local Dm | value D | decay D | write D | gate Dm | q R | k R]
 // (tesm.py:1195-1205); kernels read their columns in place through offsets.
 #include "layer_common.cuh"
+#include "rowio.cuh"
 
 namespace tesm {
 
@@ -99,6 +100,113 @@ __global__ void k_siso_local_ent(LocalEntParams p) {
       store_f(p.out_tanh, p.out_dtype, row * p.D + d, tanhf(ent));
       store_f(p.out_chg, p.out_dtype, row * p.D + d, ent - s);
     }
+  }
+}
+
+// Same computation, but the two outputs go straight to int8: the per-token codes of tanh(ent)
+// (state_proj input) and of ent - s (ent_proj input), quantised exactly like
+// tesm_b200_quant_act over the full d_state row (values first rounded to `act_dtype`).  The
+// codes land in one (M, ldc) matrix: tanh codes in columns [0, D), chg codes in [Dp, Dp + D),
+// zero padding up to Dp and 2*Dp -- the A operand of tesm_b200_gemm_i8_combine.
+struct LocalEntCodesParams {
+  LocalEntParams e;
+  int act_dtype;
+  float eps1, eps2;
+  int8_t *codes;
+  int64_t ldc;
+  int Dp;
+  float *inv1, *inv2;
+};
+
+template <int W>
+__global__ void k_siso_local_ent_codes(LocalEntCodesParams pp) {
+  extern __shared__ float sm[];
+  const LocalEntParams &p = pp.e;
+  const int R = p.R, T = p.T, D = p.D, DP1 = D + 1;
+  const int RP = R + 1;
+  float *qs = sm;
+  float *ks = qs + T * RP;
+  float *tw = ks + (T + W - 1) * RP;
+  float *oT = tw + T * W;      // T x (D+1)
+  float *oC = oT + T * DP1;    // T x (D+1)
+  const int b = blockIdx.y;
+  const int t0 = blockIdx.x * T;
+  const int64_t row0 = (int64_t)b * p.L;
+  const int nt = min(T, p.L - t0);
+  const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < nt; r += nwarp) {
+    const int64_t row = row0 + t0 + r;
+    load_rope_row(qs + r * RP, p.pc, p.pc.c_q, row, R, t0 + r, p.rope_base, p.cross ? p.cross + row * R : nullptr,
+                  lane, 32);
+  }
+  for (int r = warp; r < nt + W - 1; r += nwarp) {
+    const int pos = t0 - (W - 1) + r;
+    if (pos < 0) continue;
+    load_rope_row(ks + r * RP, p.pc, p.pc.c_k, row0 + pos, R, pos, p.rope_base, nullptr, lane, 32);
+  }
+  __syncthreads();
+  for (int t = warp; t < nt; t += nwarp) {
+    float tern_o = 0.f, cnt = 0.f;
+    for (int o = 0; o < W; ++o) {
+      const int j = t0 + t - o;
+      float part = 0.f;
+      if (j >= 0) {
+        const float *qr = qs + t * RP;
+        const float *kr = ks + (t + W - 1 - o) * RP;
+        for (int i = lane; i < R; i += 32) part = fmaf(qr[i], kr[i], part);
+      }
+      part = warp_sum(part);
+      float tv = 0.f;
+      if (j >= 0) tv = ternary_of(__fdiv_rn(part, p.sqrt_r) + p.bias[W - 1 - o], p.thr);
+      if (lane == o) tern_o = tv;
+      cnt += fabsf(tv);
+    }
+    if (lane < W) tw[t * W + lane] = tern_o / fmaxf(cnt, 1.f);
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float win[W];
+    win[W - 1] = 0.f;
+#pragma unroll
+    for (int o = 1; o < W; ++o) {
+      const int j = t0 - o;
+      win[o - 1] = j >= 0 ? p.states[(row0 + j) * D + d] : 0.f;
+    }
+    for (int t = 0; t < nt; ++t) {
+#pragma unroll
+      for (int o = W - 1; o > 0; --o) win[o] = win[o - 1];
+      const float s = p.states[(row0 + t0 + t) * D + d];
+      win[0] = s;
+      float avg = 0.f;
+#pragma unroll
+      for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[o], avg);
+      const float ent = s + p.es * (avg - s);
+      oT[t * DP1 + d] = round_to(pp.act_dtype, tanhf(ent));
+      oC[t * DP1 + d] = round_to(pp.act_dtype, ent - s);
+    }
+  }
+  __syncthreads();
+  // per-token quantisation: one warp per (row, output)
+  for (int item = warp; item < 2 * nt; item += nwarp) {
+    const int t = item >> 1, which = item & 1;
+    const float *src = (which ? oC : oT) + t * DP1;
+    float amax = 0.f;
+    for (int d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(src[d]));
+    amax = warp_max(amax);
+    const float sc = act_scale(amax, which ? pp.eps2 : pp.eps1, pp.act_dtype);
+    const int64_t row = row0 + t0 + t;
+    int8_t *crow = pp.codes + row * pp.ldc + (which ? pp.Dp : 0);
+    for (int d4 = lane * 4; d4 < pp.Dp; d4 += 128) {
+      uint32_t wv = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = d4 + i;
+        const int c = d < D ? act_code(src[d], sc, pp.act_dtype) : 0;
+        wv |= (uint32_t)(uint8_t)c << (8 * i);
+      }
+      *reinterpret_cast<uint32_t *>(crow + d4) = wv;
+    }
+    if (lane == 0) (which ? pp.inv2 : pp.inv1)[row] = __frcp_rn(sc);
   }
 }
 
@@ -266,6 +374,70 @@ extern "C" int tesm_b200_siso_local_ent(const void *proj, int dtype, int64_t ldp
     case 16: return launch_local<16>(p, st);
     case 32: return launch_local<32>(p, st);
     default: return fail(TESM_EUNSUPPORTED, "local_ent: entanglement_window must be 4, 8, 16 or 32");
+  }
+}
+
+template <int W>
+static int launch_local_codes(LocalEntCodesParams &pp, cudaStream_t st) {
+  const LocalEntParams &p = pp.e;
+  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
+                                       2 * (size_t)p.T * (p.D + 1));
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  if (smem > 200 * 1024) return fail(TESM_EUNSUPPORTED, "local_ent_codes: d_state / ent_rank too large");
+  dim3 grid((unsigned)ceil_div(p.L, p.T), (unsigned)p.B);
+  const int threads = p.D >= 256 ? 256 : (p.D <= 64 ? 64 : 128);
+  k_siso_local_ent_codes<W><<<grid, threads, smem, st>>>(pp);
+  return check_launch("local_ent_codes");
+}
+
+extern "C" int tesm_b200_siso_local_ent_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L,
+                                              int64_t Dm, int64_t D, int64_t R, int64_t W, const float *cross,
+                                              const float *bias, const float *states, float thr, float es,
+                                              float rope_base, int act_dtype, float eps1, float eps2, int8_t *codes,
+                                              int64_t ldc, int64_t Dp, float *inv1, float *inv2,
+                                              tesm_stream_t stream) {
+  TESM_REQUIRE(proj && bias && states && codes && inv1 && inv2, "local_ent_codes: null pointer");
+  TESM_REQUIRE(B > 0 && L > 0 && D > 0 && R > 0 && R % 2 == 0, "local_ent_codes: bad shape");
+  TESM_REQUIRE(Dp >= D && Dp % 128 == 0 && ldc >= 2 * Dp && ldc % 16 == 0 && ((uintptr_t)codes & 15) == 0,
+               "local_ent_codes: codes layout (Dp multiple of 128 >= D, ldc >= 2*Dp, 16-byte rows)");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "local_ent_codes: dtype");
+  LocalEntCodesParams pp;
+  LocalEntParams &p = pp.e;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
+  p.cross = cross;
+  p.bias = bias;
+  p.states = states;
+  p.B = (int)B;
+  p.L = (int)L;
+  p.D = (int)D;
+  p.R = (int)R;
+  p.W = (int)W;
+  p.T = 32;
+  p.thr = thr;
+  p.es = es;
+  p.sqrt_r = (float)sqrt((double)R);
+  p.rope_base = rope_base;
+  p.out_tanh = p.out_chg = nullptr;
+  p.out_dtype = act_dtype;
+  pp.act_dtype = act_dtype;
+  pp.eps1 = eps1;
+  pp.eps2 = eps2;
+  pp.codes = codes;
+  pp.ldc = ldc;
+  pp.Dp = (int)Dp;
+  pp.inv1 = inv1;
+  pp.inv2 = inv2;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (W) {
+    case 4: return launch_local_codes<4>(pp, st);
+    case 8: return launch_local_codes<8>(pp, st);
+    case 16: return launch_local_codes<16>(pp, st);
+    case 32: return launch_local_codes<32>(pp, st);
+    default: return fail(TESM_EUNSUPPORTED, "local_ent_codes: entanglement_window must be 4, 8, 16 or 32");
   }
 }
 

@@ -174,6 +174,23 @@ def _tail(mod, proj, M, C, Rc, tanh_e, chg, act_dtype):
     return linear(mod.out_proj, y, act_dtype)
 
 
+def combine_weight(mod):
+    """[state_proj | ent_proj] ternary rows side by side (each half D rounded up to 128, zero
+    padded) for the dual-accumulator combine GEMM, plus the two dequantisation scalars."""
+    sw, ew = mod.state_proj.weight, mod.ent_proj.weight
+    key = (sw.data_ptr(), sw._version, ew.data_ptr(), ew._version)
+    hit = mod.__dict__.get("_b200_comb")
+    if hit is None or hit[0] != key:
+        ps = packed_weight(mod.state_proj, need_tern=True)
+        pe = packed_weight(mod.ent_proj, need_tern=True)
+        D = ps.K
+        Dp = ops.round_up(D, 128)
+        tern = torch.cat([ps.tern[:, :Dp], pe.tern[:, :Dp]], dim=1).contiguous()
+        hit = (key, tern, ps.deq, pe.deq, Dp)
+        mod.__dict__["_b200_comb"] = hit
+    return hit[1:]
+
+
 def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, act_dtype=None, shape=None):
     """``TESM_SISO.forward`` prefill in eval (tesm.py:1175-1272).  ``u`` is (B, L, Dm) or a
     pre-quantised QuantAct with ``shape=(B, L)``."""
@@ -192,13 +209,20 @@ def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, ac
     fin64 = torch.empty(B, D, device=dev, dtype=torch.float64)
     h0 = prev_state.to(device=dev, dtype=torch.float64).contiguous() if prev_state is not None else None
     ops.siso_scan(proj, B, L, Dm, D, R, _param_cache(mod, "decay_bias"), h0, states, fin32, fin64)
-    tanh_e = torch.empty(M, D, device=dev, dtype=act_dtype)
-    chg = torch.empty(M, D, device=dev, dtype=act_dtype)
     thr, es, base = mod.entanglement_threshold, mod.entanglement_scale, mod.rope_base
-    if W > 0:
+    fused = W > 0 and M > ops.GEMV_MAX_M and W in (4, 8, 16, 32)
+    if fused:
+        # entanglement -> int8 codes -> one dual-accumulator GEMM with the combine epilogue
+        codes, inv1, inv2, Dp = ops.siso_local_ent_codes(
+            proj, B, L, Dm, D, R, W, cross_bias, _param_cache(mod, "local_entanglement_bias"), states, thr, es,
+            base, act_dtype, mod.state_proj.bit_eps, mod.ent_proj.bit_eps)
+    else:
+        tanh_e = torch.empty(M, D, device=dev, dtype=act_dtype)
+        chg = torch.empty(M, D, device=dev, dtype=act_dtype)
+    if not fused and W > 0:
         ops.siso_local_ent(proj, B, L, Dm, D, R, W, cross_bias, _param_cache(mod, "local_entanglement_bias"), states,
                            thr, es, base, tanh_e, chg)
-    else:
+    elif not fused:
         relb = ops.global_relbias(_param_cache(mod, "global_rel_pos_embed"), float(mod.global_rel_pos_scale),
                                   float(mod.global_rel_pos_bias), L)
         ops.siso_global_ent(proj, B, L, Dm, D, R, cross_bias, relb, states, thr, es, base, tanh_e, chg)
@@ -207,7 +231,13 @@ def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, ac
         ops.cache_fill(proj, states, 1, B, L, Dm, 1, D, R, cache["ent_k_cache"].shape[1], base, fin64,
                        cache["state"], cache["ent_k_cache"], cache["ent_v_cache"], cache["_ctl"])
         _set_prefilled(cache, L)
-    out = _tail(mod, proj, M, D, R, tanh_e, chg, act_dtype)
+    if fused:
+        tern, deq1, deq2, _ = combine_weight(mod)
+        y = torch.empty(M, Dm, device=dev, dtype=act_dtype)
+        ops.gemm_combine(codes, Dp, inv1, inv2, tern, deq1, deq2, proj, 0, Dm + 3 * D, M, Dm, y)
+        out = linear(mod.out_proj, y, act_dtype)
+    else:
+        out = _tail(mod, proj, M, D, R, tanh_e, chg, act_dtype)
     mod.last_entanglement_map = None
     mod.last_entanglement_stats = None
     mod._last_cross_layer_state = states.view(B, L, D)

@@ -294,3 +294,25 @@ def device_status() -> int:
     _lib.call("tesm_b200_device_status", ctypes.addressof(v))
     return v.value
 
+
+
+def siso_local_ent_codes(proj, B, L, Dm, D, R, W, cross, bias, states, thr, es, base, act_dtype, eps1, eps2):
+    """Local entanglement emitting the int8 codes of tanh(ent) | ent - s (see the C header)."""
+    Dp = round_up(D, 128)
+    M = B * L
+    codes = torch.empty(M, 2 * Dp, device=proj.device, dtype=torch.int8)
+    inv1 = torch.empty(M, device=proj.device, dtype=torch.float32)
+    inv2 = torch.empty(M, device=proj.device, dtype=torch.float32)
+    _lib.call("tesm_b200_siso_local_ent_codes", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, D,
+              R, W, _ptr(cross), bias.data_ptr(), states.data_ptr(), float(thr), float(es), float(base),
+              dtype_code(act_dtype), float(eps1), float(eps2), codes.data_ptr(), codes.stride(0), Dp,
+              inv1.data_ptr(), inv2.data_ptr(), _stream())
+    return codes, inv1, inv2, Dp
+
+
+def gemm_combine(codes, Kh, inv1, inv2, tern, deq1, deq2, proj, c_local, c_gate, M, N, out):
+    _lib.call("tesm_b200_gemm_i8_combine", codes.data_ptr(), codes.stride(0), Kh, inv1.data_ptr(), inv2.data_ptr(),
+              tern.data_ptr(), tern.stride(0), deq1.data_ptr(), deq2.data_ptr(), proj.data_ptr(),
+              dtype_code(proj.dtype), proj.stride(0), c_local, c_gate, M, N, out.data_ptr(), dtype_code(out.dtype),
+              out.stride(0), _stream())
+    return out
