@@ -2,13 +2,14 @@
 //   D[m,n] = sum_k A[m,k] * B[n,k]      (A: activation codes, B: ternary weights, int32 exact)
 //   out[m,n] = D * inv_scale[m] * w_deq[n|0]
 //
-// Persistent, warp-specialised CTA (one per SM):
+// Persistent, warp-specialised CTA (one per SM, 320 threads):
 //   warp 0     : TMA producer (one elected thread), 128-byte swizzled K-major tiles,
 //                STAGES-deep smem ring guarded by full/empty mbarriers;
 //   warp 1     : TMEM allocator + MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::i8,
 //                M=128 x N=BN x K=32 per instruction, accumulator in TMEM, double-buffered
 //                across output tiles so the epilogue of tile i overlaps the MMAs of tile i+1;
-//   warps 2..5 : epilogue: tcgen05.ld 32 lanes x 32 columns, scale, convert, store.
+//   warps 2..9 : epilogue: tcgen05.ld 32 lanes x 32 columns, scale, convert, store; warp w
+//                reads TMEM lanes 32*(w%4).. and half of the tile's columns.
 // Every mbarrier wait is bounded; a wait that gives up sets the sticky device status
 // (TESM_ETIMEOUT) and the CTA drains and exits instead of hanging.
 #include "rowio.cuh"
@@ -26,7 +27,8 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes (= int8 elements) per k-block: one 128B swizzle atom
 constexpr int STAGES = 4;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 8;  // two epilogue warps per TMEM lane quarter, splitting the columns
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at B200 clocks
 
 struct Params {
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], EPI_WARPS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
@@ -240,8 +242,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarter q = warp % 4
+    // epilogue warps 2..9 -> TMEM lane quarter q = warp % 4
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp stores
     uint32_t tile_i = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tile_i) {
       int mt, nt;
@@ -259,7 +262,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int esz = p.proj_dtype == TESM_BF16 ? 2 : 4;
         const uint8_t *prow = reinterpret_cast<const uint8_t *>(p.proj) + (int64_t)(row_ok ? row : 0) * p.ldp * esz;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           uint32_t r1[32], r2[32];
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + c * 32;
           tmem_ld32(tbase, r1);
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (BN == 256 && p.swiglu) {
         // columns [0,128) of the tile are gate rows, [128,256) the matching up rows
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = half * 2; c < half * 2 + 2; ++c) {
           uint32_t rg[32], ru[32];
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
           tmem_ld32(tbase + c * 32, rg);
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         continue;
       }
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32;
         tmem_ld32(taddr, r);
