@@ -242,6 +242,32 @@ def run_gpu(args, rank, world, local_rank):
         g_ops = sum(o for _, _, o, _ in rec)
         g_bytes = sum(bb for _, _, _, bb in rec)
         step_ms = s0.elapsed_time(s1)
+
+        # decode (config 5): batch 256, 16-token prompt, greedy steps replayed from a CUDA graph
+        from tesm_b200.layers import DecodeGraph
+        del out
+        torch.cuda.empty_cache()
+        dec = {}
+        if args.decode_steps > 0:
+            Bd = 256
+            ip = {"state_cache": model.backbone.allocate_inference_cache(Bd, CFG["max_seq_len"])}
+            prompt = torch.randint(0, CFG["vocab_size"], (Bd, 16), generator=g).to(dev)
+            o, _ = model(prompt, inference_params=ip, logits_to_keep=1)
+            dg = DecodeGraph(model, ip, o.logits[:, -1, :].argmax(-1, keepdim=True))
+            for _ in range(3):
+                dg.step()
+            barrier()
+            d0, d1 = ev(), ev()
+            d0.record()
+            for _ in range(args.decode_steps):
+                dg.step()
+            d1.record()
+            barrier()
+            t_dec = max_over_ranks(d0.elapsed_time(d1) / 1e3)
+            dec = {"metric": "decode tokens/s", "value": Bd * args.decode_steps * world / t_dec, "unit": UNIT,
+                   "batch_per_gpu": Bd, "prompt": 16, "steps": args.decode_steps,
+                   "ms_per_step": t_dec / args.decode_steps * 1e3, "cuda_graph": True, "sampling": "greedy argmax"}
+            del dg, ip
         status = ops.device_status()
 
     if rank != 0:
@@ -289,7 +315,7 @@ def run_gpu(args, rank, world, local_rank):
         "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
                          "sample": f"oracle port, 2 of 32 full-width layers, 1 x 96 tokens ({cpu_dt:.1f} s); "
                                    f"layer time x16 + head"},
-        "clocks": clk, "gpu_launches": launches, "device_status": status,
+        "decode": dec, "clocks": clk, "gpu_launches": launches, "device_status": status,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -328,6 +354,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
     ap.add_argument("--kernel", default=None, choices=["gemm"], help="run the small ncu case of one kernel")
     args = ap.parse_args()
     if args.kernel:

@@ -86,7 +86,10 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
 /* Prefill-shaped int8 GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8,
  * TMEM accumulators, TMA-staged operands); same contract as tesm_b200_gemv_int2 but the
  * activation codes are row-major (TESM_LAYOUT_ROWMAJOR, ld_codes multiple of 16) and the
- * weights are the int8 ternary matrix from tesm_b200_pack_ternary (ld_tern multiple of 16). */
+ * weights are the int8 ternary matrix from tesm_b200_pack_ternary (ld_tern multiple of 16).
+ * splitk_ws (nullable, >= M*N int32, zero-filled before its first use and left zeroed by every
+ * call): when there are fewer output tiles than SMs (decode batches), K is split across CTAs and
+ * the int32 partials are summed atomically into it -- exact, so the result is deterministic. */
 /* state_proj + ent_proj + output combine in one tcgen05 GEMM (tesm.py:1256-1260): two TMEM
  * accumulators, acc1 over the first Kh columns (codes of tanh(ent) x state_proj ternary weights),
  * acc2 over the next Kh (codes of ent - s x ent_proj weights); the epilogue writes
@@ -100,7 +103,8 @@ int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, int64_t Kh,
 
 int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
                       int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K, void *out,
-                      int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc, tesm_stream_t stream);
+                      int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc, int32_t *splitk_ws,
+                      int64_t ws_bytes, tesm_stream_t stream);
 
 /* ---------------------------------------------------------------- TESM layer (prefill)
  * `proj` is the in_proj output (B*L rows, row stride ldp elements, dtype TESM_F32/BF16) with the
@@ -212,7 +216,7 @@ int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, int64_t 
  * silu(acc_g * inv_scale * deq_g) * (acc_u * inv_scale * deq_u).  F % 128 == 0. */
 int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
                              int64_t ld_tern, const float *w_deq, int64_t M, int64_t F, int64_t K, void *out,
-                             int out_dtype, int64_t ldo, tesm_stream_t stream);
+                             int out_dtype, int64_t ldo, int32_t *splitk_ws, int64_t ws_bytes, tesm_stream_t stream);
 
 /* Allocation-free SISO scan.  No counterpart in the reference: it exists for callers that
  * cannot allocate device memory (runtimes with a fixed memory plan, embeddings of this

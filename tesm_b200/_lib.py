@@ -32,7 +32,7 @@ SIGNATURES = {
     "tesm_b200_gemv_int2": [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int,
                             c_i64, c_vp, c_i64, c_vp],
     "tesm_b200_gemm_i8": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
-                          c_vp, c_i64, c_vp],
+                          c_vp, c_i64, c_vp, c_i64, c_vp],
     "tesm_b200_scan_workspace": [c_i64, c_i64, c_i64, c_i64, c_vp],
     "tesm_b200_siso_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,
                             c_vp, c_i64, c_vp],
@@ -60,7 +60,7 @@ SIGNATURES = {
     "tesm_b200_gemm_i8_combine": [c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_i64, c_i64,
                                   c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_vp],
     "tesm_b200_gemm_i8_swiglu": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
-                                 c_vp],
+                                 c_vp, c_i64, c_vp],
     "tesm_b200_siso_scan_noalloc": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,
                                     c_vp, c_vp],
 }

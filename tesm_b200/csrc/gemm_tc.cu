@@ -54,6 +54,10 @@ struct Params {
   int64_t ldp;
   int c_local, c_gate;
   int proj_vec;
+  // split-K (small M): work unit = (tile, split); int32 partials are added atomically into ws
+  // (exact, so the result does not depend on the order), a finalize kernel scales them
+  int splits;
+  int32_t *ws;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -188,17 +192,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total = p.num_m_tiles * p.num_n_tiles;
-  const int nk = p.num_k_blocks;
+  const int total = p.num_m_tiles * p.num_n_tiles * p.splits;
+  const int nk_all = p.num_k_blocks;
 
   if (warp == 0) {
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         int mt, nt;
+        const int t = u / p.splits, sp = u - t * p.splits;
         tile_coords(p, t, mt, nt);
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int kb_lo = sp * nk_all / p.splits, kb_hi = (sp + 1) * nk_all / p.splits;
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             ok = false;
@@ -215,14 +221,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc = idesc_i8(BN);
       uint32_t it = 0, tile_i = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tile_i) {
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++tile_i) {
         const uint32_t buf = tile_i & 1, use = tile_i >> 1;
+        const int sp = u % p.splits;
+        const int kb_lo = sp * nk_all / p.splits, kb_hi = (sp + 1) * nk_all / p.splits;
         if (!mbar_wait(&tempty[buf], (use & 1) ^ 1)) break;
         fence_after();
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const bool second = DUAL && kb >= p.ksplit;
           const uint32_t d_tmem = tmem_base + buf * ACC_COLS + (second ? BN : 0);
-          const int kb0 = second ? kb - p.ksplit : kb;
+          const int kb0 = second ? kb - p.ksplit : kb - kb_lo;
           const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
           if (!mbar_wait(&full[stage], phase)) {
             ok = false;
@@ -246,14 +254,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp stores
     uint32_t tile_i = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++tile_i) {
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++tile_i) {
       int mt, nt;
-      tile_coords(p, t, mt, nt);
+      tile_coords(p, u / p.splits, mt, nt);
       const uint32_t buf = tile_i & 1, use = tile_i >> 1;
       if (!mbar_wait(&tfull[buf], use & 1)) break;
       fence_after();
       const int row = mt * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
+      if (!DUAL && p.splits > 1) {
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, r);
+          const int n0 = nt * BN + c * 32;
+          if (!row_ok || n0 >= p.N) continue;
+          int32_t *wrow = p.ws + (int64_t)row * p.N + n0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) atomicAdd(wrow + j, (int32_t)r[j]);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        continue;
+      }
       const float xs = row_ok ? p.inv_scale[row] : 0.f;
       const float wd0 = p.w_deq[0];
       if (DUAL) {
@@ -394,6 +419,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// Split-K finalize: scale the int32 sums (optionally the SiLU gate over 128-row interleaved
+// gate/up blocks), write the output, and zero the workspace for its next use.
+__global__ void k_splitk_finalize(int32_t *ws, int M, int N, const float *inv_scale, const float *w_deq, int per_row,
+                                  int swiglu, void *out, int out_dtype, int64_t ldo, int32_t *acc_out,
+                                  int64_t ld_acc) {
+  const int nout = swiglu ? N / 2 : N;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)M * nout) return;
+  const int m = (int)(i / nout), n = (int)(i - (int64_t)m * nout);
+  const float xs = inv_scale[m];
+  if (swiglu) {
+    const int b = n >> 7, j = n & 127;
+    const int ng = b * 256 + j, nu = ng + 128;
+    int32_t *wr = ws + (int64_t)m * N;
+    const float g = (float)wr[ng] * xs * w_deq[ng];
+    const float u = (float)wr[nu] * xs * w_deq[nu];
+    wr[ng] = 0;
+    wr[nu] = 0;
+    store_f(out, out_dtype, (int64_t)m * ldo + n, (g / (1.f + expf(-g))) * u);
+  } else {
+    int32_t *w = ws + (int64_t)m * N + n;
+    const int32_t a = *w;
+    *w = 0;
+    const float wd = per_row ? w_deq[n] : w_deq[0];
+    store_f(out, out_dtype, (int64_t)m * ldo + n, (float)a * xs * wd);
+    if (acc_out) acc_out[(int64_t)m * ld_acc + n] = a;
+  }
+}
+
 // ------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -441,10 +495,24 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   p.num_n_tiles = (int)ceil_div(p.N, BN);
   p.num_k_blocks = (int)ceil_div(p.K, BK);
   p.group_m = 16;
-  const int total = p.num_m_tiles * p.num_n_tiles;
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  p.splits = 1;
+  if (!DUAL && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
+    int s = (int)ceil_div(sm_count(), tiles);
+    if (s > 8) s = 8;
+    if (s > p.num_k_blocks / 4) s = p.num_k_blocks / 4;
+    if (s >= 2) p.splits = s;
+  }
+  const int total = tiles * p.splits;
   const int grid = total < sm_count() ? total : sm_count();
   k_gemm_i8<BN, DUAL><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
-  return check_launch("gemm_i8");
+  int rc2 = check_launch("gemm_i8");
+  if (rc2 || p.splits == 1) return rc2;
+  const int64_t n = (int64_t)p.M * (p.swiglu ? p.N / 2 : p.N);
+  k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(p.ws, p.M, p.N, p.inv_scale, p.w_deq, p.per_row,
+                                                                p.swiglu, p.out, p.out_dtype, p.ldo, p.acc_out,
+                                                                p.ld_acc);
+  return check_launch("gemm_i8 split-K finalize");
 }
 
 }  // namespace tc
@@ -454,7 +522,8 @@ using namespace tesm;
 
 extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, const float *inv_scale,
                                         const int8_t *tern, int64_t ld_tern, const float *w_deq, int64_t M, int64_t F,
-                                        int64_t K, void *out, int out_dtype, int64_t ldo, tesm_stream_t stream) {
+                                        int64_t K, void *out, int out_dtype, int64_t ldo, int32_t *splitk_ws,
+                                        int64_t ws_bytes, tesm_stream_t stream) {
   TESM_REQUIRE(codes && inv_scale && tern && w_deq && out, "gemm_i8_swiglu: null pointer");
   TESM_REQUIRE(M >= 0 && F > 0 && F % 128 == 0 && K > 0 && M < (1ll << 31), "gemm_i8_swiglu: need F % 128 == 0");
   if (M == 0) return TESM_OK;
@@ -473,6 +542,7 @@ extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, c
   p.out_dtype = out_dtype;
   p.ldo = ldo;
   p.swiglu = 1;
+  if (splitk_ws && ws_bytes >= M * 2 * F * 4 && ((uintptr_t)splitk_ws & 15) == 0) p.ws = splitk_ws;
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
@@ -518,7 +588,7 @@ extern "C" int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, 
 extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_scale, const int8_t *tern,
                                  int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K,
                                  void *out, int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc,
-                                 tesm_stream_t stream) {
+                                 int32_t *splitk_ws, int64_t ws_bytes, tesm_stream_t stream) {
   TESM_REQUIRE(codes && inv_scale && tern && w_deq && out, "gemm_i8: null pointer");
   TESM_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31), "gemm_i8: bad shape");
   if (M == 0) return TESM_OK;
@@ -540,6 +610,7 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
   p.ldo = ldo;
   p.acc_out = acc_out;
   p.ld_acc = ld_acc;
+  if (splitk_ws && ws_bytes >= M * N * 4 && ((uintptr_t)splitk_ws & 15) == 0) p.ws = splitk_ws;
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   cudaStream_t st = (cudaStream_t)stream;

@@ -472,7 +472,13 @@ def mixer_model_forward(model, input_ids, inference_params=None, prev_states=Non
     require_b200(model.layers[0].mixer, input_ids, "MixerModel")
     ids = input_ids.contiguous()
     hidden = torch.empty(B * L, emb.shape[1], device=ids.device, dtype=emb.dtype)
-    ops.embed(ids, emb, model.position_embedding.weight, None, pos_offset, hidden)
+    # one-token steps read the position from layer 0's device control word, so a captured
+    # decode graph replays with the right offset
+    pos_dev = caches[0]["_ctl"] if (caches is not None and L == 1 and caches.get(0) is not None
+                                     and "_ctl" in caches[0]) else None
+    if pos_dev is not None:
+        _prepare_cache(caches[0], ids.device)
+    ops.embed(ids, emb, model.position_embedding.weight, pos_dev, pos_offset, hidden)
     hidden = hidden.view(B, L, -1)
     residual = None
     cross = None
@@ -513,6 +519,46 @@ def lm_forward(lm, input_ids, labels=None, inference_params=None, prev_states=No
     from .models import TESMCausalLMOutput
     return TESMCausalLMOutput(loss=loss, logits=logits, hidden_states=hidden, entanglement_maps=maps,
                               entanglement_stats=stats), final_states
+
+
+class DecodeGraph:
+    """One greedy decode step of a TESMLMHeadModel captured in a CUDA graph.
+
+    ``step()`` replays embedding -> every layer's incremental step -> lm_head -> argmax and
+    writes the chosen tokens back into the static input buffer; the host mirrors of each
+    layer's ``seq_pos`` / ``cache_idx`` are advanced after every replay (the device copies are
+    advanced inside the graph by the decode kernels).
+    """
+
+    def __init__(self, lm, inference_params, first_tokens):
+        self.lm = lm
+        self.ip = inference_params
+        self.caches = inference_params["state_cache"]
+        self.ids = first_tokens.clone()
+        for c in self.caches.values():
+            _prepare_cache(c, self.ids.device)
+        # warm-up outside capture (allocates the split-K workspace, packs nothing new)
+        snap = [(c["state"].clone(), c["ent_k_cache"].clone(), c["ent_v_cache"].clone(), c["_ctl"].clone(),
+                 c["seq_pos"], c["cache_idx"], c["_ctl_host"]) for c in self.caches.values()]
+        self.lm(self.ids, inference_params=self.ip)
+        for c, s in zip(self.caches.values(), snap):
+            c["state"].copy_(s[0]); c["ent_k_cache"].copy_(s[1]); c["ent_v_cache"].copy_(s[2]); c["_ctl"].copy_(s[3])
+            c["seq_pos"], c["cache_idx"], c["_ctl_host"] = s[4], s[5], s[6]
+        torch.cuda.synchronize()
+        hosts = [(c["seq_pos"], c["cache_idx"], c["_ctl_host"]) for c in self.caches.values()]
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            out, _ = self.lm(self.ids, inference_params=self.ip)
+            self.logits = out.logits
+            self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1, keepdim=True))
+        for c, h in zip(self.caches.values(), hosts):  # capture ran no kernel; restore the mirrors
+            c["seq_pos"], c["cache_idx"], c["_ctl_host"] = h
+
+    def step(self):
+        self.graph.replay()
+        for c in self.caches.values():
+            _advance_host(c, c["ent_k_cache"].shape[1])
+        return self.ids
 
 
 @torch.no_grad()

@@ -123,13 +123,33 @@ def gemv(codes, inv, rowsum, pw: PackedWeight, M: int, out_dtype: torch.dtype, o
     return (out, accb) if acc else out
 
 
+_SPLITK = {}
+SPLITK_MAX_M = 1024
+
+
+def splitk_workspace(M: int, N: int, device):
+    """Zero-filled int32 split-K workspace shared by the small-M tensor-core GEMMs of a device
+    (every GEMM call leaves it zeroed).  None for large M, where split-K is never chosen."""
+    if M > SPLITK_MAX_M:
+        return None
+    need = M * N
+    key = torch.device(device).index
+    buf = _SPLITK.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.zeros(max(need, 1 << 20), device=device, dtype=torch.int32)
+        _SPLITK[key] = buf
+    return buf
+
+
 def gemm(codes, inv, pw: PackedWeight, M: int, out_dtype: torch.dtype, out=None, acc=False):
     dev = codes.device
     out = out if out is not None else torch.empty(M, pw.N, device=dev, dtype=out_dtype)
     accb = torch.empty(M, pw.N, device=dev, dtype=torch.int32) if acc else None
+    ws = splitk_workspace(M, pw.N, dev)
     _lib.call("tesm_b200_gemm_i8", codes.data_ptr(), codes.stride(0), inv.data_ptr(), pw.tern.data_ptr(),
               pw.tern.stride(0), pw.deq.data_ptr(), int(pw.per_row), M, pw.N, pw.K, out.data_ptr(),
-              dtype_code(out.dtype), out.stride(0), _ptr(accb), pw.N, _stream())
+              dtype_code(out.dtype), out.stride(0), _ptr(accb), pw.N, _ptr(ws), ws.numel() * 4 if ws is not None else 0,
+              _stream())
     return (out, accb) if acc else out
 
 
@@ -283,9 +303,10 @@ def gemm_swiglu(q: QuantAct, pw: PackedWeight, out_dtype, out=None):
     """Interleaved gate/up weight (blocks of 128 rows) -> silu(gate) * up, width pw.N // 2."""
     F = pw.N // 2
     out = out if out is not None else torch.empty(q.M, F, device=q.codes.device, dtype=out_dtype)
+    ws = splitk_workspace(q.M, pw.N, q.codes.device)
     _lib.call("tesm_b200_gemm_i8_swiglu", q.codes.data_ptr(), q.codes.stride(0), q.inv.data_ptr(), pw.tern.data_ptr(),
               pw.tern.stride(0), pw.deq.data_ptr(), q.M, F, pw.K, out.data_ptr(), dtype_code(out.dtype),
-              out.stride(0), _stream())
+              out.stride(0), _ptr(ws), ws.numel() * 4 if ws is not None else 0, _stream())
     return out
 
 

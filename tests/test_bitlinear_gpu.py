@@ -107,7 +107,7 @@ def test_gemv_exact(ops, MNK):
 
 
 GEMM_SHAPES = [(65, 80, 96), (128, 256, 256), (300, 1000, 520), (1000, 11008, 4096), (256, 4096, 11008),
-               (77, 130, 37), (4096, 512, 2048)]
+               (77, 130, 37), (4096, 512, 2048), (128, 4096, 4096), (200, 300, 2048)]  # last three: split-K
 
 
 @pytest.mark.parametrize("MNK", GEMM_SHAPES, ids=lambda s: "x".join(map(str, s)))
@@ -155,18 +155,18 @@ def test_module_forward(lib):
         lay(randn(c["xshape"], 1).cuda())
 
 
-@pytest.mark.parametrize("M", [20, 300])
-def test_ffn_swiglu_interleaved(lib, M):
+@pytest.mark.parametrize("M,Dm", [(20, 256), (300, 256), (200, 2048)])
+def test_ffn_swiglu_interleaved(lib, M, Dm):
     """FeedForward with d_intermediate % 128 == 0: gate/up rows interleaved in 128-blocks; the
     tensor-core path applies silu(gate)*up in the GEMM epilogue, the GEMV path in a kernel."""
     from tesm_b200.models import FeedForward, TESMConfig
-    cfg = TESMConfig(d_model=256, d_intermediate=384, kernel_backend="b200")
+    cfg = TESMConfig(d_model=Dm, d_intermediate=384, kernel_backend="b200")
     torch.manual_seed(0)
     ffn = FeedForward(cfg)
     for lin in (ffn.gate_proj, ffn.up_proj, ffn.down_proj):
         torch.nn.init.normal_(lin.weight, std=0.02)
     P = {k: v.detach().numpy() for k, v in ffn.state_dict().items()}
-    x = randn((M, 256), 41)
+    x = randn((M, Dm), 41)
     ref = O.ffn(P, x.numpy())
     g, u = ffn.gate_proj.weight.detach().numpy(), ffn.up_proj.weight.detach().numpy()
     c, s = O.quant_act(x.numpy())
