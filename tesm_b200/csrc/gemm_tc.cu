@@ -152,12 +152,14 @@ __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int
   mt = first_m + (r - nt * gm);
 }
 
-template <int BN, bool DUAL>
+template <int BN, bool DUAL, int MT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  constexpr int A_BYTES = BM * BK;
+  // MT = 2 ("skinny", decode batches): one CTA covers 256 token rows as two M=128 MMAs sharing
+  // each weight tile, so a narrow N tile still reads every weight byte once
+  constexpr int A_BYTES = MT * BM * BK;
   constexpr int B_BYTES = BN * BK;
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_BYTES;
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : BN;  // TMEM columns of one tile's accumulator(s)
+  constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : MT * BN;  // TMEM columns of one tile's accumulator(s)
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
 
   if (threadIdx.x == 0) {
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM * MT);
           tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
         }
       }
@@ -242,7 +244,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             // advance 32 bytes along K inside the swizzle atom: +2 in 16-byte units
-            mma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
+#pragma unroll
+            for (int s = 0; s < MT; ++s)  // second M sub-tile: +16 KB = +1024 in 16-byte units
+              mma_i8(d_tmem + s * BN, adesc + 2 * kk + s * (BM * BK / 16), bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
           }
           mma_commit(&empty[stage]);
         }
@@ -260,7 +264,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t buf = tile_i & 1, use = tile_i >> 1;
       if (!mbar_wait(&tfull[buf], use & 1)) break;
       fence_after();
-      const int row = mt * BM + q * 32 + lane;
+      const int sub = MT == 2 ? half : 0;  // skinny tiles: each warp half owns one M sub-tile
+      const int row = (mt * MT + sub) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
       if (!DUAL && p.splits > 1) {
 #pragma unroll 1
@@ -323,7 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&tempty[buf]);
         continue;
       }
-      if (BN == 256 && p.swiglu) {
+      if (BN == 256 && MT == 1 && p.swiglu) {
         // columns [0,128) of the tile are gate rows, [128,256) the matching up rows
 #pragma unroll 1
         for (int c = half * 2; c < half * 2 + 2; ++c) {
@@ -367,10 +372,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&tempty[buf]);
         continue;
       }
+      const int c_lo = MT == 2 ? 0 : half * (BN / 64), c_hi = MT == 2 ? BN / 32 : (half + 1) * (BN / 64);
 #pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      for (int c = c_lo; c < c_hi; ++c) {
         uint32_t r[32];
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32;
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + sub * BN + c * 32;
         tmem_ld32(taddr, r);
         const int n0 = nt * BN + c * 32;
         if (!row_ok || n0 >= p.N) continue;
@@ -478,26 +484,26 @@ static int make_map(CUtensorMap *map, const void *ptr, int64_t inner, int64_t ou
   return TESM_OK;
 }
 
-template <int BN, bool DUAL = false>
+template <int BN, bool DUAL = false, int MT = 1>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
   CUtensorMap ma, mb;
-  int rc = make_map(&ma, A, p.K, p.M, lda, BM);
+  int rc = make_map(&ma, A, p.K, p.M, lda, BM * MT);
   if (rc) return rc;
   rc = make_map(&mb, B, p.K, p.N, ldb, BN);
   if (rc) return rc;
-  const size_t smem = 1024 + (size_t)STAGES * (BM * BK + BN * BK) + 256;
+  const size_t smem = 1024 + (size_t)STAGES * (MT * BM * BK + BN * BK) + 256;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_gemm_i8<BN, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_gemm_i8<BN, DUAL, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
-  p.num_m_tiles = (int)ceil_div(p.M, BM);
+  p.num_m_tiles = (int)ceil_div(p.M, BM * MT);
   p.num_n_tiles = (int)ceil_div(p.N, BN);
   p.num_k_blocks = (int)ceil_div(p.K, BK);
   p.group_m = 16;
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   p.splits = 1;
-  if (!DUAL && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
+  if (!DUAL && MT == 1 && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
     int s = (int)ceil_div(sm_count(), tiles);
     if (s > 8) s = 8;
     if (s > p.num_k_blocks / 4) s = p.num_k_blocks / 4;
@@ -505,7 +511,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   }
   const int total = tiles * p.splits;
   const int grid = total < sm_count() ? total : sm_count();
-  k_gemm_i8<BN, DUAL><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
+  k_gemm_i8<BN, DUAL, MT><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
   int rc2 = check_launch("gemm_i8");
   if (rc2 || p.splits == 1) return rc2;
   const int64_t n = (int64_t)p.M * (p.swiglu ? p.N / 2 : p.N);
@@ -614,6 +620,10 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   cudaStream_t st = (cudaStream_t)stream;
+  if (M <= 256) {  // decode-sized batches: skinny tiles, enough CTAs, weights streamed once
+    if (ceil_div(N, 64) >= 100) return tc::launch<64, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
+    return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
+  }
   if (N <= 128) return tc::launch<128>(codes, ld_codes, tern, ld_tern, p, st);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, st);
 }

@@ -303,6 +303,10 @@ def gemm_swiglu(q: QuantAct, pw: PackedWeight, out_dtype, out=None):
     """Interleaved gate/up weight (blocks of 128 rows) -> silu(gate) * up, width pw.N // 2."""
     F = pw.N // 2
     out = out if out is not None else torch.empty(q.M, F, device=q.codes.device, dtype=out_dtype)
+    if q.M <= 256:  # decode batches: skinny-tile GEMM, then the gate on the interleaved output
+        gu = gemm(q.codes, q.inv, pw, q.M, out_dtype)
+        silu_mul(gu, F, out, 128)
+        return out
     ws = splitk_workspace(q.M, pw.N, q.codes.device)
     _lib.call("tesm_b200_gemm_i8_swiglu", q.codes.data_ptr(), q.codes.stride(0), q.inv.data_ptr(), pw.tern.data_ptr(),
               pw.tern.stride(0), pw.deq.data_ptr(), q.M, F, pw.K, out.data_ptr(), dtype_code(out.dtype),
