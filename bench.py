@@ -348,6 +348,28 @@ def run_kernel_case(args):
     return 0
 
 
+def run_decode_case(args):
+    """Config-5 model, batch 256: 16-token prefill then `steps` eager one-token decode steps
+    (the kernels a decode graph replays), for launch-list captures."""
+    import torch
+    from tesm_b200.models import TESMConfig, TESMLMHeadModel
+    torch.manual_seed(0)
+    cfg = TESMConfig(kernel_backend="b200", **CFG)
+    with torch.device("cuda"):
+        model = TESMLMHeadModel(cfg, dtype=torch.bfloat16).eval()
+    with torch.no_grad():
+        ip = {"state_cache": model.backbone.allocate_inference_cache(256, CFG["max_seq_len"])}
+        prompt = torch.randint(0, CFG["vocab_size"], (256, 16), device="cuda")
+        o, _ = model(prompt, inference_params=ip, logits_to_keep=1)
+        tok = o.logits[:, -1, :].argmax(-1, keepdim=True)
+        for _ in range(args.warmup + args.steps):
+            o, _ = model(tok, inference_params=ip)
+            tok = o.logits[:, -1, :].argmax(-1, keepdim=True)
+        torch.cuda.synchronize()
+    print(json.dumps({"kernel": "decode", "batch": 256, "steps": args.warmup + args.steps}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,8 +377,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
-    ap.add_argument("--kernel", default=None, choices=["gemm"], help="run the small ncu case of one kernel")
+    ap.add_argument("--kernel", default=None, choices=["gemm", "decode"], help="run a small ncu case")
     args = ap.parse_args()
+    if args.kernel == "decode":
+        return run_decode_case(args)
     if args.kernel:
         return run_kernel_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
