@@ -61,29 +61,33 @@ __global__ void k_decode_step(DecodeParams p) {
     p.vc[(((int64_t)b * W + idx) * H + h) * D + d] = (float)newd;
   }
   __syncthreads();  // the slot just written is read back below
-  // window scores: warp 0 (W <= 32)
-  if (tid < 32) {
-    float tv = 0.f;
-    int s = 0;
-    for (int w = 0; w < valid; ++w) {
+  // window scores: all W lags at once, 8 lanes per lag (W <= 32 needs blockDim >= 8*W, else a
+  // second pass), partial dot products combined with shuffles within each 8-lane group
+  for (int w0 = 0; w0 < W; w0 += blockDim.x / 8) {
+    const int w = w0 + tid / 8, part_i = tid & 7;
+    float part = 0.f;
+    if (w < valid) {
       const int sl = valid >= W ? (idx + w) % W : w;
-      const int bi = valid >= W ? w : W - valid + w;
       const float *kr = p.kc + (((int64_t)b * W + sl) * H + h) * R;
-      float part = 0.f;
-      for (int i = tid; i < R; i += 32) part = fmaf(q[i], kr[i], part);
-      part = warp_sum(part);
-      const float t = ternary_of(__fdiv_rn(part, p.sqrt_r) + p.bias[h * W + bi], p.thr);
-      if (tid == w) {
-        tv = t;
-        s = sl;
+      for (int i = part_i; i < R; i += 8) part = fmaf(q[i], kr[i], part);
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (part_i == 0 && w < W) {
+      float t = 0.f;
+      if (w < valid) {
+        const int bi = valid >= W ? w : W - valid + w;
+        t = ternary_of(__fdiv_rn(part, p.sqrt_r) + p.bias[h * W + bi], p.thr);
       }
+      tw[w] = t;
+      slot[w] = w < valid ? (valid >= W ? (idx + w) % W : w) : 0;
     }
-    float cnt = fabsf(tid < valid ? tv : 0.f);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float cnt = tid < W ? fabsf(tw[tid]) : 0.f;
     cnt = warp_sum(cnt);
-    if (tid < W) {
-      tw[tid] = tid < valid ? tv / fmaxf(cnt, 1.f) : 0.f;
-      slot[tid] = tid < valid ? s : 0;
-    }
+    if (tid < W) tw[tid] = tw[tid] / fmaxf(cnt, 1.f);
   }
   __syncthreads();
   for (int d = tid; d < D; d += blockDim.x) {
