@@ -157,6 +157,17 @@ int tesm_b200_siso_global_ent(const void *proj, int dtype, int64_t ldp, int64_t 
                               float thr, float es, float rope_base, void *out_tanh, void *out_chg, int out_dtype,
                               tesm_stream_t stream);
 
+/* MIMO global entanglement with the rank merge (replaces _compute_global_entanglement_mimo's torch
+ * rung, tesm_mimo.py:590-687, as used per rank at :1007-1017): scores over all heads' flattened
+ * q.k / sqrt(H*R) (RoPE per head) + relative bias, ternary, causal; per rank avg_r = (tern/norm) @
+ * states_r with NO lerp (the reference's global MIMO path returns the average itself);
+ * out_tanh = tanh(sum_r mo_r * avg_r), out_chg = sum_r mo_r * (avg_r - s_r).  acc_e / acc_c: fp32
+ * (B*L, H*D) caller workspaces (unused when RM == 1). */
+int tesm_b200_mimo_global_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t H,
+                              int64_t D, int64_t R, int64_t RM, const float *relb, const float *mimo_o,
+                              const float *states, float thr, float rope_base, float *acc_e, float *acc_c,
+                              void *out_tanh, void *out_chg, int out_dtype, tesm_stream_t stream);
+
 /* MIMO local entanglement with the rank merge (replaces _compute_local_entanglement_mimo and the
  * mimo_o merge, tesm_mimo.py:394-588, :996-1017): out_tanh = tanh(sum_r mo_r*ent_r),
  * out_chg = sum_r mo_r*(ent_r - s_r), (B*L, H*D).  quirk != 0 keeps the reference's window

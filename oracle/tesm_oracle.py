@@ -492,7 +492,7 @@ def mimo_forward(P, cfg, u, cache=None, details=False):
     base = cfg.get("rope_base", 10000.0)
     q = rope_mimo(q.reshape(B, L, H, R), 0, base)
     k = rope_mimo(k.reshape(B, L, H, R), 0, base)
-    bias = P["local_entanglement_bias"]
+    bias = P.get("local_entanglement_bias")
     ent = np.zeros((B, L, H, D), F32)
     chg = np.zeros((B, L, H, D), F32)
     states0 = None
@@ -501,8 +501,16 @@ def mimo_forward(P, cfg, u, cache=None, details=False):
         st = scan_seq(decay, upd)
         if r == 0:
             states0 = st
-        avg = local_ent_mimo(q, k, st, bias, thr)
-        e_r = (st + F32(es) * (avg - st)).astype(F32)
+        if cfg["entanglement_window"] > 0:
+            avg = local_ent_mimo(q, k, st, bias, thr)
+            e_r = (st + F32(es) * (avg - st)).astype(F32)
+        else:
+            # global rung (tesm_mimo.py:651-687): heads flattened, sqrt(H*R), no lerp
+            rb = global_rel_bias(L, P["global_rel_pos_embed"], P["global_rel_pos_scale"][0],
+                                 P["global_rel_pos_bias"][0])
+            avg = global_ent(q.reshape(B, L, H * R), k.reshape(B, L, H * R), st.reshape(B, L, H * D), rb, thr,
+                             H * R).reshape(B, L, H, D)
+            e_r = avg
         c_r = (e_r - st).astype(F32)
         ent = (ent + e_r * mo[None, None, :, r]).astype(F32)
         chg = (chg + c_r * mo[None, None, :, r]).astype(F32)

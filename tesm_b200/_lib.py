@@ -45,6 +45,8 @@ SIGNATURES = {
                                   c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp],
     "tesm_b200_mimo_local_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp,
                                  c_vp, c_vp, c_float, c_float, c_float, c_int, c_vp, c_vp, c_int, c_vp],
+    "tesm_b200_mimo_global_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                  c_vp, c_float, c_float, c_vp, c_vp, c_vp, c_vp, c_int, c_vp],
     "tesm_b200_combine": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_int, c_vp],
     "tesm_b200_cache_fill": [c_vp, c_int, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                              c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],

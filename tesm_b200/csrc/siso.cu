@@ -233,43 +233,56 @@ struct GlobalEntParams {
   ProjCols pc;
   const float *cross;
   const float *relb;    // (2L - 1)
-  const float *states;  // (B, L, D)
-  int B, L, D, R;
+  const float *states;  // row r, channel c at states[r * s_ld + s_off + c]
+  int64_t s_ld;
+  int s_off;
+  int B, L, D, R;       // D: state channels (H*Dh for MIMO), R: q/k columns (H*Rh for MIMO)
+  int rope_heads;       // RoPE applied per head on R / rope_heads columns
+  int dslice;           // channels per CTA (blockIdx.z)
   float thr, es, sqrt_r, rope_base;
   void *out_tanh, *out_chg;
   int out_dtype;
+  // MIMO rank accumulation (tesm_mimo.py:1007-1017 with the global rung :669-687, no lerp)
+  int mimo, RM, r, Dh;
+  const float *mo;
+  float *acc_e, *acc_c;
 };
 
-// One CTA per (query tile of 32 rows, batch); loops over causal key tiles of 32.
+// One CTA per (query tile of 32 rows, batch, channel slice); loops over causal key tiles of 32.
 __global__ void __launch_bounds__(256) k_siso_global_ent(GlobalEntParams p) {
   extern __shared__ float sm[];
   constexpr int TQ = 32, TK = 32;
-  const int R = p.R, RP = R + 1, D = p.D;
+  const int R = p.R, RP = R + 1, DS = p.dslice;
+  const int d0 = blockIdx.z * DS, DL = min(DS, p.D - d0);
+  const int Rh = R / p.rope_heads;
   float *qs = sm;               // TQ x RP
   float *ks = qs + TQ * RP;     // TK x RP
   float *tt = ks + TK * RP;     // TQ x TK ternary
   float *cnt = tt + TQ * TK;    // TQ
-  float *vs = cnt + TQ;         // TK x D
-  float *acc = vs + TK * D;     // TQ x D
+  float *vs = cnt + TQ;         // TK x DS
+  float *acc = vs + TK * DS;    // TQ x DS
   const int b = blockIdx.y, q0 = blockIdx.x * TQ;
   const int64_t row0 = (int64_t)b * p.L;
   const int nq = min(TQ, p.L - q0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
   for (int r = warp; r < nq; r += nwarp) {
     const int64_t row = row0 + q0 + r;
-    load_rope_row(qs + r * RP, p.pc, p.pc.c_q, row, R, q0 + r, p.rope_base, p.cross ? p.cross + row * R : nullptr,
-                  lane, 32);
+    for (int h = 0; h < p.rope_heads; ++h)
+      load_rope_row(qs + r * RP + h * Rh, p.pc, p.pc.c_q + h * Rh, row, Rh, q0 + r, p.rope_base,
+                    p.cross ? p.cross + row * R + h * Rh : nullptr, lane, 32);
   }
-  for (int i = threadIdx.x; i < TQ * D; i += blockDim.x) acc[i] = 0.f;
+  for (int i = threadIdx.x; i < TQ * DS; i += blockDim.x) acc[i] = 0.f;
   if (threadIdx.x < TQ) cnt[threadIdx.x] = 0.f;
   for (int k0 = 0; k0 < q0 + nq; k0 += TK) {
     const int nk = min(TK, p.L - k0);
     __syncthreads();
     for (int r = warp; r < nk; r += nwarp)
-      load_rope_row(ks + r * RP, p.pc, p.pc.c_k, row0 + k0 + r, R, k0 + r, p.rope_base, nullptr, lane, 32);
-    for (int i = threadIdx.x; i < nk * D; i += blockDim.x) {
-      const int r = i / D, d = i - r * D;
-      vs[i] = p.states[(row0 + k0 + r) * D + d];
+      for (int h = 0; h < p.rope_heads; ++h)
+        load_rope_row(ks + r * RP + h * Rh, p.pc, p.pc.c_k + h * Rh, row0 + k0 + r, Rh, k0 + r, p.rope_base,
+                      nullptr, lane, 32);
+    for (int i = threadIdx.x; i < nk * DL; i += blockDim.x) {
+      const int r = i / DL, d = i - r * DL;
+      vs[r * DS + d] = p.states[(row0 + k0 + r) * p.s_ld + p.s_off + d0 + d];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < TQ * TK; i += blockDim.x) {
@@ -290,23 +303,52 @@ __global__ void __launch_bounds__(256) k_siso_global_ent(GlobalEntParams p) {
       for (int kj = 0; kj < TK; ++kj) c += fabsf(tt[threadIdx.x * TK + kj]);
       cnt[threadIdx.x] += c;
     }
-    for (int i = threadIdx.x; i < TQ * D; i += blockDim.x) {
-      const int qi = i / D, d = i - qi * D;
-      float a = acc[i];
-      for (int kj = 0; kj < nk; ++kj) a = fmaf(tt[qi * TK + kj], vs[kj * D + d], a);
-      acc[i] = a;
+    for (int i = threadIdx.x; i < TQ * DL; i += blockDim.x) {
+      const int qi = i / DL, d = i - qi * DL;
+      float a = acc[qi * DS + d];
+      for (int kj = 0; kj < nk; ++kj) a = fmaf(tt[qi * TK + kj], vs[kj * DS + d], a);
+      acc[qi * DS + d] = a;
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < nq * D; i += blockDim.x) {
-    const int qi = i / D, d = i - qi * D;
+  for (int i = threadIdx.x; i < nq * DL; i += blockDim.x) {
+    const int qi = i / DL, d = i - qi * DL, c = d0 + d;
     const int64_t row = row0 + q0 + qi;
-    const float s = p.states[row * D + d];
-    const float avg = acc[i] / fmaxf(cnt[qi], 1.f);
-    const float ent = s + p.es * (avg - s);
-    store_f(p.out_tanh, p.out_dtype, row * D + d, tanhf(ent));
-    store_f(p.out_chg, p.out_dtype, row * D + d, ent - s);
+    const float s = p.states[row * p.s_ld + p.s_off + c];
+    const float avg = acc[qi * DS + d] / fmaxf(cnt[qi], 1.f);
+    if (!p.mimo) {
+      const float ent = s + p.es * (avg - s);
+      store_f(p.out_tanh, p.out_dtype, row * p.D + c, tanhf(ent));
+      store_f(p.out_chg, p.out_dtype, row * p.D + c, ent - s);
+    } else {
+      const int h = c / p.Dh, dd = c - h * p.Dh;
+      const float m = p.mo[((int64_t)h * p.RM + p.r) * p.Dh + dd];
+      const int64_t o = row * p.D + c;
+      const float e = (p.r ? p.acc_e[o] : 0.f) + m * avg;
+      const float cg = (p.r ? p.acc_c[o] : 0.f) + m * (avg - s);
+      if (p.r + 1 < p.RM) {
+        p.acc_e[o] = e;
+        p.acc_c[o] = cg;
+      } else {
+        store_f(p.out_tanh, p.out_dtype, o, tanhf(e));
+        store_f(p.out_chg, p.out_dtype, o, cg);
+      }
+    }
   }
+}
+
+static int launch_global(GlobalEntParams &p, cudaStream_t st) {
+  p.dslice = p.D <= 256 ? p.D : 256;
+  const size_t smem = sizeof(float) * (32 * (p.R + 1) * 2 + 32 * 32 + 32 + 32 * (size_t)p.dslice * 2);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_siso_global_ent, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  if (smem > 200 * 1024) return fail(TESM_EUNSUPPORTED, "global_ent: ent_rank too large");
+  dim3 grid((unsigned)ceil_div(p.L, 32), (unsigned)p.B, (unsigned)ceil_div(p.D, p.dslice));
+  k_siso_global_ent<<<grid, 256, smem, st>>>(p);
+  return check_launch("global_ent");
 }
 
 // ---------------------------------------------------------------- combine
@@ -472,16 +514,54 @@ extern "C" int tesm_b200_siso_global_ent(const void *proj, int dtype, int64_t ld
   p.out_tanh = out_tanh;
   p.out_chg = out_chg;
   p.out_dtype = out_dtype;
-  const size_t smem = sizeof(float) * (32 * (R + 1) * 2 + 32 * 32 + 32 + 32 * D * 2);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_siso_global_ent, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
+  p.states = states;
+  p.s_ld = D;
+  p.s_off = 0;
+  p.rope_heads = 1;
+  p.mimo = 0;
+  return launch_global(p, (cudaStream_t)stream);
+}
+
+extern "C" int tesm_b200_mimo_global_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                         int64_t H, int64_t D, int64_t R, int64_t RM, const float *relb,
+                                         const float *mimo_o, const float *states, float thr, float rope_base,
+                                         float *acc_e, float *acc_c, void *out_tanh, void *out_chg, int out_dtype,
+                                         tesm_stream_t stream) {
+  TESM_REQUIRE(proj && relb && mimo_o && states && out_tanh && out_chg, "mimo_global_ent: null pointer");
+  TESM_REQUIRE(B > 0 && L > 0 && H > 0 && D > 0 && R > 0 && R % 2 == 0 && RM > 0, "mimo_global_ent: bad shape");
+  TESM_REQUIRE(RM == 1 || (acc_e && acc_c), "mimo_global_ent: accumulators needed for mimo_rank > 1");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "mimo_global_ent: dtype");
+  GlobalEntParams p;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)(H * D), (int)(H * R));
+  p.cross = nullptr;
+  p.relb = relb;
+  p.states = states;
+  p.s_ld = RM * H * D;
+  p.B = (int)B;
+  p.L = (int)L;
+  p.D = (int)(H * D);
+  p.R = (int)(H * R);
+  p.rope_heads = (int)H;
+  p.thr = thr;
+  p.es = 0.f;
+  p.sqrt_r = (float)sqrt((double)(H * R));
+  p.rope_base = rope_base;
+  p.out_tanh = out_tanh;
+  p.out_chg = out_chg;
+  p.out_dtype = out_dtype;
+  p.mimo = 1;
+  p.RM = (int)RM;
+  p.Dh = (int)D;
+  p.mo = mimo_o;
+  p.acc_e = acc_e;
+  p.acc_c = acc_c;
+  for (int r = 0; r < RM; ++r) {
+    p.r = r;
+    p.s_off = (int)(r * H * D);
+    int rc = launch_global(p, (cudaStream_t)stream);
+    if (rc) return rc;
   }
-  TESM_REQUIRE(smem <= 200 * 1024, "global_ent: d_state too large");
-  dim3 grid((unsigned)ceil_div(L, 32), (unsigned)B);
-  k_siso_global_ent<<<grid, 256, smem, (cudaStream_t)stream>>>(p);
-  return check_launch("global_ent");
+  return TESM_OK;
 }
 
 extern "C" int tesm_b200_combine(const void *proj, int dtype, int64_t ldp, int64_t M, int64_t Dm, int64_t D,

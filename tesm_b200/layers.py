@@ -278,8 +278,6 @@ def mimo_prefill(mod, u, cache=None, act_dtype=None, shape=None):
     act_dtype = act_dtype or u.dtype
     Dm, D, R, H, RM, W = mod.d_model, mod.d_state, mod.ent_rank, mod.n_heads, mod.mimo_rank, mod.entanglement_window
     C, M = H * D, B * L
-    if W <= 0 or mod.local_entanglement_bias is None:
-        raise TesmError("tesm_b200: MIMO global entanglement (entanglement_window=0) is not built yet")
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(M, Dm))
     dev = q.codes.device
     proj = linear_q(mod.in_proj, q, act_dtype)
@@ -290,9 +288,15 @@ def mimo_prefill(mod, u, cache=None, act_dtype=None, shape=None):
                   fin32, fin64)
     tanh_e = torch.empty(M, C, device=dev, dtype=act_dtype)
     chg = torch.empty(M, C, device=dev, dtype=act_dtype)
-    ops.mimo_local_ent(proj, B, L, Dm, H, D, R, RM, W, _param_cache(mod, "local_entanglement_bias"),
-                       _param_cache(mod, "mimo_o"), states, mod.entanglement_threshold, mod.entanglement_scale,
-                       mod.rope_base, True, tanh_e, chg)
+    if W > 0 and mod.local_entanglement_bias is not None:
+        ops.mimo_local_ent(proj, B, L, Dm, H, D, R, RM, W, _param_cache(mod, "local_entanglement_bias"),
+                           _param_cache(mod, "mimo_o"), states, mod.entanglement_threshold, mod.entanglement_scale,
+                           mod.rope_base, True, tanh_e, chg)
+    else:
+        relb = ops.global_relbias(_param_cache(mod, "global_rel_pos_embed"), float(mod.global_rel_pos_scale),
+                                  float(mod.global_rel_pos_bias), L)
+        ops.mimo_global_ent(proj, B, L, Dm, H, D, R, RM, relb, _param_cache(mod, "mimo_o"), states,
+                            mod.entanglement_threshold, mod.rope_base, tanh_e, chg)
     if cache is not None and "state" in cache:
         _prepare_cache(cache, dev)
         ops.cache_fill(proj, states, RM, B, L, Dm, H, D, R, cache["ent_k_cache"].shape[1], mod.rope_base, fin64,

@@ -341,3 +341,13 @@ def gemm_combine(codes, Kh, inv1, inv2, tern, deq1, deq2, proj, c_local, c_gate,
               dtype_code(proj.dtype), proj.stride(0), c_local, c_gate, M, N, out.data_ptr(), dtype_code(out.dtype),
               out.stride(0), _stream())
     return out
+
+
+def mimo_global_ent(proj, B, L, Dm, H, D, R, RM, relb, mimo_o, states, thr, base, out_tanh, out_chg):
+    acc_e = acc_c = None
+    if RM > 1:
+        acc_e = torch.empty(B * L, H * D, device=proj.device, dtype=torch.float32)
+        acc_c = torch.empty_like(acc_e)
+    _lib.call("tesm_b200_mimo_global_ent", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, H, D,
+              R, RM, relb.data_ptr(), mimo_o.data_ptr(), states.data_ptr(), float(thr), float(base), _ptr(acc_e),
+              _ptr(acc_c), out_tanh.data_ptr(), out_chg.data_ptr(), dtype_code(out_tanh.dtype), _stream())

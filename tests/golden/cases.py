@@ -34,6 +34,8 @@ MIMO = [
                  entanglement_threshold=0.3)),
     dict(name="short", B=1, L=5, kw=dict(d_model=32, d_state=16, n_heads=2, ent_rank=8, entanglement_window=8,
                                         max_seq_len=32)),
+    dict(name="global", B=2, L=20, kw=dict(d_model=64, d_state=16, n_heads=4, ent_rank=8, entanglement_window=0,
+                                          max_seq_len=64)),
 ]
 
 _tiny = dict(n_layer=2, d_model=64, d_state=32, ent_rank=16, d_intermediate=96, vocab_size=128,
