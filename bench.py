@@ -370,15 +370,158 @@ def run_decode_case(args):
     return 0
 
 
+def _graph_time(fn, reps=10, inner=8):
+    """Median per-call device time of `fn` replayed from a CUDA graph of `inner` calls."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(inner):
+            fn(i)
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b) / inner / 1e3)
+    return statistics.median(ts)
+
+
+def run_cfg2(args, peaks):
+    """BitLinear INT2 microbench, per-tensor and per-row scales.  One call =
+    activation quantisation + GEMV (M <= 64) or tensor-core GEMM; weights rotate over enough
+    copies to exceed L2 so every call reads them from HBM."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    out = []
+    for (N, K) in [(11008, 4096), (4096, 11008)]:
+        for per_row in (False, True):
+            w = torch.randn(N, K, device="cuda") * 0.02
+            ncopy = 14
+            pws = [ops.pack_weight(w.roll(i, 0), 1e-5, per_row=per_row, with_tern=True) for i in range(ncopy)]
+            for M in (1, 16, 128, 4096):
+                x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+                y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+                t = _graph_time(lambda i: ops.bitlinear_2d(x, pws[i % ncopy], 1e-5, torch.bfloat16, y),
+                                inner=ncopy if M <= 128 else 4)
+                byts = N * K / 4 + M * K * 2 + M * N * 2 + 4 * N + 4 * M
+                ops_ = 2.0 * M * N * K
+                gbs, tops = byts / t / 1e9, ops_ / t / 1e12
+                bound = "hbm" if M <= 16 else ("mixed" if M <= 128 else "tensor")
+                out.append({"workload": "cfg2 BitLinear", "N": N, "K": K, "M": M, "scale": "row" if per_row else "tensor",
+                            "path": "gemv (mma.sync, packed int2)" if M <= 64 else "tcgen05 int8",
+                            "us": t * 1e6, "tokens_per_s": M / t, "GB_s": gbs, "TOPS": tops, "bound": bound,
+                            "hbm_frac": gbs / peaks["hbm_gbs"]})
+            del pws
+    return out
+
+
+def run_cfg3(args, peaks):
+    """standalone SISO scan + local entanglement (+ codes) + global entanglement
+    + fused output GEMM at batch 8 x 8192, d_state 256, d_model 2048, window 16, ent_rank 64.
+    Synthetic in_proj output: decay pre-activation ~ N(0,1) with decay_bias 0 (a = sigmoid(N(0,1))),
+    write / value / q / k / local / gate ~ N(0,1), bf16."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    B, L, D, Dm, R, W = 8, 8192, 256, 2048, 64, 16
+    M = B * L
+    Np = 2 * Dm + 3 * D + 2 * R
+    proj = torch.randn(M, Np, device="cuda").to(torch.bfloat16)
+    db = torch.zeros(D, device="cuda")
+    bias = torch.randn(W, device="cuda") * 0.3
+    states = torch.empty(M, D, device="cuda")
+    f32 = torch.empty(B, D, device="cuda")
+    f64 = torch.empty(B, D, device="cuda", dtype=torch.float64)
+    th = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    ch = torch.empty_like(th)
+    res = []
+    t = _graph_time(lambda i: ops.siso_scan(proj, B, L, Dm, D, R, db, None, states, f32, f64), inner=4)
+    byts = M * D * (3 * 2 + 4)  # decay, write, value bf16 in; fp32 states out
+    res.append({"kernel": "k_scan (SISO)", "ms": t * 1e3, "GB_s": byts / t / 1e9, "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"],
+                "algorithmic_bytes": byts})
+    t = _graph_time(lambda i: ops.siso_local_ent(proj, B, L, Dm, D, R, W, None, bias, states, 0.1, 0.2, 1e4, th, ch),
+                    inner=4)
+    byts = M * (2 * R * 2 + D * 4 + 2 * D * 2)
+    res.append({"kernel": "k_siso_local_ent<16>", "ms": t * 1e3, "GB_s": byts / t / 1e9,
+                "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": byts})
+    t = _graph_time(lambda i: ops.siso_local_ent_codes(proj, B, L, Dm, D, R, W, None, bias, states, 0.1, 0.2, 1e4,
+                                                       torch.bfloat16, 1e-5, 1e-5), inner=4)
+    byts = M * (2 * R * 2 + D * 4 + 2 * D + 8)
+    res.append({"kernel": "k_siso_local_ent_codes<16> (int8 out)", "ms": t * 1e3, "GB_s": byts / t / 1e9,
+                "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": byts})
+    emb = torch.randn(64, device="cuda") * 0.02
+    relb = ops.global_relbias(emb, 1.0, 0.0, L)
+    t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th, ch),
+                    reps=3, inner=1)
+    fl = B * (L * L / 2) * (2 * R + 2 * D)
+    res.append({"kernel": "k_siso_global_ent (SIMT fp32)", "ms": t * 1e3, "TFLOPS": fl / t / 1e12,
+                "note": "causal half counted; tensor-core version not built"})
+    return res
+
+
+def run_cfg4(args, peaks):
+    """TESMMIMO_Optimized layer forward, batch 4 x 16384, d_model 2048, 16 heads,
+    d_state 64, ent_rank 48, mimo_rank 4, window 16, bf16 activations, random init seed 0."""
+    import torch
+    from tesm_b200 import ops
+    from tesm_b200.modules import TESMMIMO_Optimized
+    torch.manual_seed(0)
+    B, L = 4, 16384
+    with torch.device("cuda"):
+        m = TESMMIMO_Optimized(d_model=2048, n_heads=16, d_state=64, entanglement_window=16, max_seq_len=L,
+                               kernel_backend="b200").eval()
+    x = torch.randn(B, L, 2048, device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        t = _graph_time(lambda i: m(x), reps=5, inner=2)
+        H, D, R, RM, Dm = 16, 64, 48, 4, 2048
+        proj = torch.randn(B * L, 2 * Dm + 3 * H * D + 2 * H * R, device="cuda").to(torch.bfloat16)
+        states = torch.empty(B * L, RM, H * D, device="cuda")
+        f32 = torch.empty(B, H * D, device="cuda")
+        f64 = torch.empty(B, H * D, device="cuda", dtype=torch.float64)
+        ts = _graph_time(lambda i: ops.mimo_scan(proj, B, L, Dm, H, D, R, RM, m.decay_bias.float().contiguous(),
+                                                   m.mimo_x.float().contiguous(), states, f32, f64), inner=2)
+        th = torch.empty(B * L, H * D, device="cuda", dtype=torch.bfloat16)
+        ch = torch.empty_like(th)
+        bias = m.local_entanglement_bias.float().contiguous()
+        mo = m.mimo_o.float().contiguous()
+        te = _graph_time(lambda i: ops.mimo_local_ent(proj, B, L, Dm, H, D, R, RM, 16, bias, mo, states, 0.5, 0.2, 1e4,
+                                                        True, th, ch), inner=2)
+    E = B * L * H * D
+    return [{"workload": "cfg4 MIMO layer", "tokens_per_s": B * L / t, "ms": t * 1e3},
+            {"kernel": "k_scan (MIMO, 4 ranks)", "ms": ts * 1e3, "GB_s": E * (6 + 16) / ts / 1e9,
+             "hbm_frac": E * (6 + 16) / ts / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": E * 22},
+            {"kernel": "k_mimo_local_ent<16,4>", "ms": te * 1e3, "GB_s": (E * (16 + 4) + B * L * H * R * 4) / te / 1e9,
+             "hbm_frac": (E * (16 + 4) + B * L * H * R * 4) / te / 1e9 / peaks["hbm_gbs"],
+             "algorithmic_bytes": E * 20 + B * L * H * R * 4}]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg4"],
+                    help="supplementary measurements of BASELINE configs 2-4 (one JSON line per measurement)")
     ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
     ap.add_argument("--kernel", default=None, choices=["gemm", "decode"], help="run a small ncu case")
     args = ap.parse_args()
+    if args.workload:
+        peaks, _ = load_peaks()
+        fn = {"cfg2": run_cfg2, "cfg3": run_cfg3, "cfg4": run_cfg4}[args.workload]
+        for rec in fn(args, peaks):
+            print(json.dumps(rec), flush=True)
+        return 0
     if args.kernel == "decode":
         return run_decode_case(args)
     if args.kernel:
