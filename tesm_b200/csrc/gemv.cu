@@ -65,6 +65,24 @@ __global__ void __launch_bounds__(256) k_gemv_int2(GemvParams p) {
   const int nsteps = max(s_end - s_begin, 0);
   const int act_stride = nsteps * 256 + 64;  // +64: rows of one 8-lane phase hit different banks
 
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int row0 = blockIdx.x * 128 + warp * 16;
+  const int rA = min(row0 + g, p.N - 1), rB = min(row0 + g + 8, p.N - 1);
+  const uint8_t *wA = p.packed + (int64_t)rA * p.ld_packed + tig * 16;
+  const uint8_t *wB = p.packed + (int64_t)rB * p.ld_packed + tig * 16;
+
+  // weight prefetch first: it does not depend on the activations
+  constexpr int PF = 4;  // prefetch depth in steps (2 x 16 B per step per thread)
+  uint4 bufA[PF], bufB[PF];
+#pragma unroll
+  for (int i = 0; i < PF; ++i) {
+    if (i < nsteps) {
+      bufA[i] = ldg_nc_v4(wA + (int64_t)(s_begin + i) * 64);
+      bufB[i] = ldg_nc_v4(wB + (int64_t)(s_begin + i) * 64);
+    }
+  }
+
   // ---- stage this CTA's K-slice of the activation codes in shared memory
   {
     const int chunks = nsteps * 16;  // 16-byte chunks per token row
@@ -78,26 +96,10 @@ __global__ void __launch_bounds__(256) k_gemv_int2(GemvParams p) {
   }
   __syncthreads();
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tig = lane & 3;
-  const int row0 = blockIdx.x * 128 + warp * 16;
-  const int rA = min(row0 + g, p.N - 1), rB = min(row0 + g + 8, p.N - 1);
-  const uint8_t *wA = p.packed + (int64_t)rA * p.ld_packed + tig * 16;
-  const uint8_t *wB = p.packed + (int64_t)rB * p.ld_packed + tig * 16;
-
   int acc[NT][4];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
 
-  constexpr int PF = 4;  // prefetch depth in steps (2 x 16 B per step per thread)
-  uint4 bufA[PF], bufB[PF];
-#pragma unroll
-  for (int i = 0; i < PF; ++i) {
-    if (i < nsteps) {
-      bufA[i] = ldg_nc_v4(wA + (int64_t)(s_begin + i) * 64);
-      bufB[i] = ldg_nc_v4(wB + (int64_t)(s_begin + i) * 64);
-    }
-  }
   for (int s0 = 0; s0 < nsteps; s0 += PF) {
 #pragma unroll
     for (int i = 0; i < PF; ++i) {

@@ -28,40 +28,27 @@ __global__ void k_mimo_local_ent(MimoEntParams p) {
   float *qs = sm;
   float *ks = qs + T * RP;
   float *tw = ks + (T + W - 1) * RP;
+  float *invf = tw + T * W;
   const int h = blockIdx.y, b = blockIdx.z;
   const int t0 = blockIdx.x * T;
   const int64_t row0 = (int64_t)b * p.L;
   const int nt = min(T, p.L - t0);
   const int C = p.H * p.D;
   const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < R / 2; i += blockDim.x) invf[i] = rope_inv_freq(i, R, p.rope_base);
+  __syncthreads();
   for (int r = warp; r < nt; r += nwarp)
-    load_rope_row(qs + r * RP, p.pc, p.pc.c_q + h * R, row0 + t0 + r, R, t0 + r, p.rope_base, nullptr, lane, 32);
+    load_rope_row_tab(qs + r * RP, p.pc, p.pc.c_q + h * R, row0 + t0 + r, R, t0 + r, invf, nullptr, lane, 32);
   for (int r = warp; r < nt + W - 1; r += nwarp) {
     const int pos = t0 - (W - 1) + r;
     if (pos < 0) continue;
-    load_rope_row(ks + r * RP, p.pc, p.pc.c_k + h * R, row0 + pos, R, pos, p.rope_base, nullptr, lane, 32);
+    load_rope_row_tab(ks + r * RP, p.pc, p.pc.c_k + h * R, row0 + pos, R, pos, invf, nullptr, lane, 32);
   }
   __syncthreads();
-  for (int t = warp; t < nt; t += nwarp) {
-    const int gt = t0 + t;
-    float tern_o = 0.f, cnt = 0.f;
-    for (int o = 0; o < W; ++o) {
-      const int j = gt - o;
-      const bool valid = j >= 0 && (!p.quirk || o >= W - 1 - gt);
-      float part = 0.f;
-      if (valid) {
-        const float *qr = qs + t * RP;
-        const float *kr = ks + (t + W - 1 - o) * RP;
-        for (int i = lane; i < R; i += 32) part = fmaf(qr[i], kr[i], part);
-      }
-      part = warp_sum(part);
-      float tv = 0.f;
-      if (valid) tv = ternary_of(__fdiv_rn(part, p.sqrt_r) + p.bias[h * W + (W - 1 - o)], p.thr);
-      if (lane == o) tern_o = tv;
-      cnt += fabsf(tv);
-    }
-    if (lane < W) tw[t * W + lane] = tern_o / fmaxf(cnt, 1.f);
-  }
+  const int quirk = p.quirk;
+  window_scores<W>(qs, ks, RP, R, nt, t0, p.bias + h * W, p.sqrt_r, p.thr, tw, [quirk](int gt, int o) {
+    return gt - o >= 0 && (!quirk || o >= W - 1 - gt);
+  });
   __syncthreads();
   for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
     const int c = h * p.D + d;
@@ -77,31 +64,45 @@ __global__ void k_mimo_local_ent(MimoEntParams p) {
 #pragma unroll
       for (int r = 0; r < RM; ++r) win[r][o - 1] = j >= 0 ? p.states[((row0 + j) * RM + r) * C + c] : 0.f;
     }
-    for (int t = 0; t < nt; ++t) {
-      const int64_t row = row0 + t0 + t;
-      float ent = 0.f, chg = 0.f;
+    constexpr int PF = 4;  // timesteps prefetched per batch (x RM loads)
+    for (int tb = 0; tb < nt; tb += PF) {
+      float sv[PF][RM];
 #pragma unroll
-      for (int r = 0; r < RM; ++r) {
+      for (int j = 0; j < PF; ++j)
 #pragma unroll
-        for (int o = W - 1; o > 0; --o) win[r][o] = win[r][o - 1];
-        const float s = p.states[(row * RM + r) * C + c];
-        win[r][0] = s;
-        float avg = 0.f;
+        for (int r = 0; r < RM; ++r)
+          sv[j][r] = tb + j < nt ? p.states[((row0 + t0 + tb + j) * RM + r) * C + c] : 0.f;
 #pragma unroll
-        for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[r][o], avg);
-        const float e_r = s + p.es * (avg - s);
-        ent = fmaf(mo[r], e_r, ent);
-        chg = fmaf(mo[r], e_r - s, chg);
+      for (int j = 0; j < PF; ++j) {
+        if (tb + j < nt) {
+          const int t = tb + j;
+          const int64_t row = row0 + t0 + t;
+          float ent = 0.f, chg = 0.f;
+#pragma unroll
+          for (int r = 0; r < RM; ++r) {
+#pragma unroll
+            for (int o = W - 1; o > 0; --o) win[r][o] = win[r][o - 1];
+            const float s = sv[j][r];
+            win[r][0] = s;
+            float avg = 0.f;
+#pragma unroll
+            for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[r][o], avg);
+            const float e_r = s + p.es * (avg - s);
+            ent = fmaf(mo[r], e_r, ent);
+            chg = fmaf(mo[r], e_r - s, chg);
+          }
+          store_f(p.out_tanh, p.out_dtype, row * C + c, tanhf(ent));
+          store_f(p.out_chg, p.out_dtype, row * C + c, chg);
+        }
       }
-      store_f(p.out_tanh, p.out_dtype, row * C + c, tanhf(ent));
-      store_f(p.out_chg, p.out_dtype, row * C + c, chg);
     }
   }
 }
 
 template <int W, int RM>
 static int launch_mimo_ent(MimoEntParams &p, cudaStream_t st) {
-  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W);
+  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
+                                       p.R / 2);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_mimo_local_ent<W, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);

@@ -35,30 +35,86 @@ struct ScanParams {
   int *ticket;
 };
 
-template <int RM, bool MIMO>
-__device__ __forceinline__ void scan_inputs(const ScanParams &p, int64_t row, int c, float db, const float (&mx)[RM],
-                                            float &a, float (&u)[RM]) {
-  const int64_t base = row * p.pc.ld;
-  const float dr = load_f(p.pc.proj, p.pc.dtype, base + p.pc.c_decay + c);
-  const float wr = load_f(p.pc.proj, p.pc.dtype, base + p.pc.c_write + c);
-  const float vr = load_f(p.pc.proj, p.pc.dtype, base + p.pc.c_value + c);
-  a = sigmoidf_(dr + db);
-  const float w = sigmoidf_(wr), v = tanhf(vr);
-  if (MIMO) {
-#pragma unroll
-    for (int r = 0; r < RM; ++r) u[r] = __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r]));
-  } else {
-    u[0] = w * v;
-  }
-}
-
 template <bool MIMO>
 __device__ __forceinline__ float step(float a, float h, float u) {
   return MIMO ? __fadd_rn(__fmul_rn(a, h), u) : fmaf(a, h, u);
 }
 
+// Stage the chunk's inputs in shared memory: sa[t][c] = a, and for SISO su[t][c] = u,
+// for MIMO sw / sv = sigmoid(write) / tanh(value) (the ranks are formed on the fly).  The tile
+// is read once from HBM with 16-byte loads when rows and column offsets are aligned.
+template <bool MIMO>
+__device__ __forceinline__ void stage_inputs(const ScanParams &p, int64_t row0, int t0, int nt, int c0, int S,
+                                             float *sa, float *s1, float *s2, int vec) {
+  const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4;
+  const uint8_t *base = reinterpret_cast<const uint8_t *>(p.pc.proj);
+  if (vec) {
+    const int VPT = 16 / esz;  // channels per 16-byte vector
+    const int groups = S / VPT;
+    for (int i = threadIdx.x; i < nt * groups; i += blockDim.x) {
+      const int t = i / groups, cg = (i - t * groups) * VPT;
+      const int c = c0 + cg;
+      if (c >= p.C) continue;
+      const uint8_t *rowp = base + ((row0 + t0 + t) * p.pc.ld) * esz;
+      float dv[8], wv[8], vv[8];
+      const uint4 d4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_decay + c) * esz);
+      const uint4 w4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_write + c) * esz);
+      const uint4 v4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_value + c) * esz);
+      if (esz == 2) {
+        const __nv_bfloat16 *dh = reinterpret_cast<const __nv_bfloat16 *>(&d4);
+        const __nv_bfloat16 *wh = reinterpret_cast<const __nv_bfloat16 *>(&w4);
+        const __nv_bfloat16 *vh = reinterpret_cast<const __nv_bfloat16 *>(&v4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          dv[j] = __bfloat162float(dh[j]);
+          wv[j] = __bfloat162float(wh[j]);
+          vv[j] = __bfloat162float(vh[j]);
+        }
+      } else {
+        const float *df = reinterpret_cast<const float *>(&d4);
+        const float *wf = reinterpret_cast<const float *>(&w4);
+        const float *vf = reinterpret_cast<const float *>(&v4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          dv[j] = df[j];
+          wv[j] = wf[j];
+          vv[j] = vf[j];
+        }
+      }
+      for (int j = 0; j < VPT; ++j) {
+        const int o = t * S + cg + j;
+        sa[o] = sigmoidf_(dv[j] + p.decay_bias[c + j]);
+        const float w = sigmoidf_(wv[j]), v = tanhf(vv[j]);
+        if (MIMO) {
+          s1[o] = w;
+          s2[o] = v;
+        } else {
+          s1[o] = w * v;
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < nt * S; i += blockDim.x) {
+      const int t = i / S, cl = i - t * S, c = c0 + cl;
+      if (c >= p.C) continue;
+      const int64_t rb = (row0 + t0 + t) * p.pc.ld;
+      const float dr = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_decay + c);
+      const float w = sigmoidf_(load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_write + c));
+      const float v = tanhf(load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_value + c));
+      sa[i] = sigmoidf_(dr + p.decay_bias[c]);
+      if (MIMO) {
+        s1[i] = w;
+        s2[i] = v;
+      } else {
+        s1[i] = w * v;
+      }
+    }
+  }
+}
+
 template <int RM, bool MIMO>
-__global__ void k_scan(ScanParams p) {
+__global__ void k_scan(ScanParams p, int vec) {
+  extern __shared__ float sm_scan[];
   __shared__ int s_tile, s_flag;
   if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1);
   __syncthreads();
@@ -67,10 +123,14 @@ __global__ void k_scan(ScanParams p) {
   const int chunk = tile / per_chunk;
   const int bs = tile - chunk * per_chunk;
   const int b = bs / p.nslices, slice = bs - b * p.nslices;
-  const int c = slice * blockDim.x + threadIdx.x;
+  const int S = blockDim.x;
+  const int c0 = slice * S;
+  const int c = c0 + threadIdx.x;
   const bool active = c < p.C;
-  const int t0 = chunk * p.T, t1 = min(t0 + p.T, p.L);
-  const float db = active ? p.decay_bias[c] : 0.f;
+  const int t0 = chunk * p.T, t1 = min(t0 + p.T, p.L), nt = t1 - t0;
+  float *sa = sm_scan, *s1 = sa + p.T * S, *s2 = s1 + p.T * S;
+  const int64_t row0 = (int64_t)b * p.L;
+  stage_inputs<MIMO>(p, row0, t0, nt, c0, S, sa, s1, s2, vec);
   float mx[RM];
 #pragma unroll
   for (int r = 0; r < RM; ++r) mx[r] = 0.f;
@@ -79,18 +139,22 @@ __global__ void k_scan(ScanParams p) {
 #pragma unroll
     for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
   }
-  const int64_t row0 = (int64_t)b * p.L;
+  __syncthreads();
 
   // pass 1: aggregate affine map of this chunk (A shared by the ranks)
   float A = 1.f, U[RM];
 #pragma unroll
   for (int r = 0; r < RM; ++r) U[r] = 0.f;
   if (active) {
-    for (int t = t0; t < t1; ++t) {
-      float a, u[RM];
-      scan_inputs<RM, MIMO>(p, row0 + t, c, db, mx, a, u);
+    for (int t = 0; t < nt; ++t) {
+      const float a = sa[t * S + threadIdx.x];
+      if (MIMO) {
+        const float w = s1[t * S + threadIdx.x], v = s2[t * S + threadIdx.x];
 #pragma unroll
-      for (int r = 0; r < RM; ++r) U[r] = step<MIMO>(a, U[r], u[r]);
+        for (int r = 0; r < RM; ++r) U[r] = step<true>(a, U[r], __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r])));
+      } else {
+        U[0] = step<false>(a, U[0], s1[t * S + threadIdx.x]);
+      }
       A *= a;
     }
   }
@@ -162,13 +226,19 @@ __global__ void k_scan(ScanParams p) {
   }
   // pass 2: states of this chunk from the carry
   if (active) {
-    for (int t = t0; t < t1; ++t) {
-      float a, u[RM];
-      scan_inputs<RM, MIMO>(p, row0 + t, c, db, mx, a, u);
+    for (int t = 0; t < nt; ++t) {
+      const float a = sa[t * S + threadIdx.x];
+      const int64_t orow = (row0 + t0 + t) * RM;
+      if (MIMO) {
+        const float w = s1[t * S + threadIdx.x], v = s2[t * S + threadIdx.x];
 #pragma unroll
-      for (int r = 0; r < RM; ++r) {
-        h[r] = step<MIMO>(a, h[r], u[r]);
-        p.states[((row0 + t) * RM + r) * p.C + c] = h[r];
+        for (int r = 0; r < RM; ++r) {
+          h[r] = step<true>(a, h[r], __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r])));
+          p.states[(orow + r) * p.C + c] = h[r];
+        }
+      } else {
+        h[0] = step<false>(a, h[0], s1[t * S + threadIdx.x]);
+        p.states[orow * p.C + c] = h[0];
       }
     }
     if (t1 == p.L) {
@@ -200,7 +270,16 @@ static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
 template <int RM, bool MIMO>
 static int launch_scan(ScanParams &p, cudaStream_t st, int slice) {
   const int64_t grid = (int64_t)p.nchunks * p.B * p.nslices;
-  k_scan<RM, MIMO><<<(unsigned)grid, slice, 0, st>>>(p);
+  const size_t smem = sizeof(float) * (size_t)p.T * slice * (MIMO ? 3 : 2);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_scan<RM, MIMO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    attr = true;
+  }
+  const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4, vpt = 16 / esz;
+  const int vec = ((uintptr_t)p.pc.proj % 16 == 0) && ((p.pc.ld * esz) % 16 == 0) && (p.pc.c_decay % vpt == 0) &&
+                  (p.pc.c_write % vpt == 0) && (p.pc.c_value % vpt == 0) && (p.C % vpt == 0) && (slice % vpt == 0);
+  k_scan<RM, MIMO><<<(unsigned)grid, slice, smem, st>>>(p, vec);
   return check_launch("scan");
 }
 

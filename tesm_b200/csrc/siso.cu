@@ -27,80 +27,85 @@ struct LocalEntParams {
   int out_dtype;
 };
 
+// Shared front half of the local-entanglement kernels: RoPE'd q (+ cross bias) and k rows of
+// the tile (k with a W-1 halo) in shared memory, then the normalised ternary window weights.
 template <int W>
-__global__ void k_siso_local_ent(LocalEntParams p) {
-  extern __shared__ float sm[];
-  const int R = p.R, T = p.T;
-  const int RP = R + 1;
-  float *qs = sm;                    // T x RP
-  float *ks = qs + T * RP;           // (T + W - 1) x RP
-  float *tw = ks + (T + W - 1) * RP; // T x W ternary / norm
-  const int b = blockIdx.y;
-  const int t0 = blockIdx.x * T;
-  const int64_t row0 = (int64_t)b * p.L;
-  const int nt = min(T, p.L - t0);
-  // q rows (+ cross-layer bias), k rows with halo
+__device__ __forceinline__ void local_front(const LocalEntParams &p, float *qs, float *ks, float *tw, float *invf,
+                                            int64_t row0, int t0, int nt) {
+  const int R = p.R, RP = R + 1;
+  for (int i = threadIdx.x; i < R / 2; i += blockDim.x) invf[i] = rope_inv_freq(i, R, p.rope_base);
+  __syncthreads();
   const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int r = warp; r < nt; r += nwarp) {
     const int64_t row = row0 + t0 + r;
-    load_rope_row(qs + r * RP, p.pc, p.pc.c_q, row, R, t0 + r, p.rope_base,
-                  p.cross ? p.cross + row * R : nullptr, lane, 32);
+    load_rope_row_tab(qs + r * RP, p.pc, p.pc.c_q, row, R, t0 + r, invf, p.cross ? p.cross + row * R : nullptr,
+                      lane, 32);
   }
   for (int r = warp; r < nt + W - 1; r += nwarp) {
     const int pos = t0 - (W - 1) + r;
     if (pos < 0) continue;
-    load_rope_row(ks + r * RP, p.pc, p.pc.c_k, row0 + pos, R, pos, p.rope_base, nullptr, lane, 32);
+    load_rope_row_tab(ks + r * RP, p.pc, p.pc.c_k, row0 + pos, R, pos, invf, nullptr, lane, 32);
   }
   __syncthreads();
-  // scores -> ternary weights; one warp per query position
-  for (int t = warp; t < nt; t += nwarp) {
-    float tern_o = 0.f;
-    float cnt = 0.f;
-    for (int o = 0; o < W; ++o) {
-      const int j = t0 + t - o;
-      float part = 0.f;
-      if (j >= 0) {
-        const float *qr = qs + t * RP;
-        const float *kr = ks + (t + W - 1 - o) * RP;
-        for (int i = lane; i < R; i += 32) part = fmaf(qr[i], kr[i], part);
-      }
-      part = warp_sum(part);
-      float tv = 0.f;
-      if (j >= 0) {
-        const float sc = __fdiv_rn(part, p.sqrt_r) + p.bias[W - 1 - o];
-        tv = ternary_of(sc, p.thr);
-      }
-      if (lane == o) tern_o = tv;
-      cnt += fabsf(tv);
-    }
-    const float norm = fmaxf(cnt, 1.f);
-    if (lane < W) tw[t * W + lane] = tern_o / norm;
-  }
+  window_scores<W>(qs, ks, RP, R, nt, t0, p.bias, p.sqrt_r, p.thr, tw, [](int gt, int o) { return gt - o >= 0; });
   __syncthreads();
-  // per channel: sliding window of states in registers
-  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+}
+
+// Per channel: sliding window of states in registers, 8 timesteps prefetched at a time.
+// emit(t, d, tanh_ent, chg) consumes the outputs.
+template <int W, class Emit>
+__device__ __forceinline__ void local_channels(const LocalEntParams &p, const float *tw, int64_t row0, int t0, int nt,
+                                               Emit emit) {
+  const int D = p.D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
     // before the first shift win[o] holds states[t0 - 1 - o]; after it, win[o] = states[t - o]
     float win[W];
     win[W - 1] = 0.f;
 #pragma unroll
     for (int o = 1; o < W; ++o) {
       const int j = t0 - o;
-      win[o - 1] = j >= 0 ? p.states[(row0 + j) * p.D + d] : 0.f;
+      win[o - 1] = j >= 0 ? p.states[(row0 + j) * D + d] : 0.f;
     }
-    for (int t = 0; t < nt; ++t) {
+    for (int tb = 0; tb < nt; tb += 8) {
+      float sv[8];
 #pragma unroll
-      for (int o = W - 1; o > 0; --o) win[o] = win[o - 1];
-      const int64_t row = row0 + t0 + t;
-      const float s = p.states[row * p.D + d];
-      win[0] = s;
-      float avg = 0.f;
+      for (int j = 0; j < 8; ++j) sv[j] = tb + j < nt ? p.states[(row0 + t0 + tb + j) * D + d] : 0.f;
 #pragma unroll
-      for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[o], avg);
-      const float ent = s + p.es * (avg - s);
-      store_f(p.out_tanh, p.out_dtype, row * p.D + d, tanhf(ent));
-      store_f(p.out_chg, p.out_dtype, row * p.D + d, ent - s);
+      for (int j = 0; j < 8; ++j) {
+        if (tb + j < nt) {
+          const int t = tb + j;
+#pragma unroll
+          for (int o = W - 1; o > 0; --o) win[o] = win[o - 1];
+          const float s = sv[j];
+          win[0] = s;
+          float avg = 0.f;
+#pragma unroll
+          for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[o], avg);
+          const float ent = s + p.es * (avg - s);
+          emit(t, d, tanhf(ent), ent - s);
+        }
+      }
     }
   }
+}
+
+template <int W>
+__global__ void k_siso_local_ent(LocalEntParams p) {
+  extern __shared__ float sm[];
+  const int R = p.R, T = p.T, RP = R + 1;
+  float *qs = sm;                    // T x RP
+  float *ks = qs + T * RP;           // (T + W - 1) x RP
+  float *tw = ks + (T + W - 1) * RP; // T x W ternary / norm
+  float *invf = tw + T * W;          // R / 2
+  const int b = blockIdx.y, t0 = blockIdx.x * T;
+  const int64_t row0 = (int64_t)b * p.L;
+  const int nt = min(T, p.L - t0);
+  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt);
+  local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
+    const int64_t o = (row0 + t0 + t) * p.D + d;
+    store_f(p.out_tanh, p.out_dtype, o, th);
+    store_f(p.out_chg, p.out_dtype, o, ch);
+  });
 }
 
 // Same computation, but the two outputs go straight to int8: the per-token codes of tanh(ent)
@@ -127,64 +132,18 @@ __global__ void k_siso_local_ent_codes(LocalEntCodesParams pp) {
   float *qs = sm;
   float *ks = qs + T * RP;
   float *tw = ks + (T + W - 1) * RP;
-  float *oT = tw + T * W;      // T x (D+1)
+  float *invf = tw + T * W;
+  float *oT = invf + R / 2;    // T x (D+1)
   float *oC = oT + T * DP1;    // T x (D+1)
-  const int b = blockIdx.y;
-  const int t0 = blockIdx.x * T;
+  const int b = blockIdx.y, t0 = blockIdx.x * T;
   const int64_t row0 = (int64_t)b * p.L;
   const int nt = min(T, p.L - t0);
   const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < nt; r += nwarp) {
-    const int64_t row = row0 + t0 + r;
-    load_rope_row(qs + r * RP, p.pc, p.pc.c_q, row, R, t0 + r, p.rope_base, p.cross ? p.cross + row * R : nullptr,
-                  lane, 32);
-  }
-  for (int r = warp; r < nt + W - 1; r += nwarp) {
-    const int pos = t0 - (W - 1) + r;
-    if (pos < 0) continue;
-    load_rope_row(ks + r * RP, p.pc, p.pc.c_k, row0 + pos, R, pos, p.rope_base, nullptr, lane, 32);
-  }
-  __syncthreads();
-  for (int t = warp; t < nt; t += nwarp) {
-    float tern_o = 0.f, cnt = 0.f;
-    for (int o = 0; o < W; ++o) {
-      const int j = t0 + t - o;
-      float part = 0.f;
-      if (j >= 0) {
-        const float *qr = qs + t * RP;
-        const float *kr = ks + (t + W - 1 - o) * RP;
-        for (int i = lane; i < R; i += 32) part = fmaf(qr[i], kr[i], part);
-      }
-      part = warp_sum(part);
-      float tv = 0.f;
-      if (j >= 0) tv = ternary_of(__fdiv_rn(part, p.sqrt_r) + p.bias[W - 1 - o], p.thr);
-      if (lane == o) tern_o = tv;
-      cnt += fabsf(tv);
-    }
-    if (lane < W) tw[t * W + lane] = tern_o / fmaxf(cnt, 1.f);
-  }
-  __syncthreads();
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float win[W];
-    win[W - 1] = 0.f;
-#pragma unroll
-    for (int o = 1; o < W; ++o) {
-      const int j = t0 - o;
-      win[o - 1] = j >= 0 ? p.states[(row0 + j) * D + d] : 0.f;
-    }
-    for (int t = 0; t < nt; ++t) {
-#pragma unroll
-      for (int o = W - 1; o > 0; --o) win[o] = win[o - 1];
-      const float s = p.states[(row0 + t0 + t) * D + d];
-      win[0] = s;
-      float avg = 0.f;
-#pragma unroll
-      for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[o], avg);
-      const float ent = s + p.es * (avg - s);
-      oT[t * DP1 + d] = round_to(pp.act_dtype, tanhf(ent));
-      oC[t * DP1 + d] = round_to(pp.act_dtype, ent - s);
-    }
-  }
+  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt);
+  local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
+    oT[t * DP1 + d] = round_to(pp.act_dtype, th);
+    oC[t * DP1 + d] = round_to(pp.act_dtype, ch);
+  });
   __syncthreads();
   // per-token quantisation: one warp per (row, output)
   for (int item = warp; item < 2 * nt; item += nwarp) {
@@ -371,7 +330,8 @@ using namespace tesm;
 
 template <int W>
 static int launch_local(LocalEntParams &p, cudaStream_t st) {
-  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W);
+  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
+                                       p.R / 2);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
@@ -423,7 +383,7 @@ template <int W>
 static int launch_local_codes(LocalEntCodesParams &pp, cudaStream_t st) {
   const LocalEntParams &p = pp.e;
   const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
-                                       2 * (size_t)p.T * (p.D + 1));
+                                       p.R / 2 + 2 * (size_t)p.T * (p.D + 1));
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
