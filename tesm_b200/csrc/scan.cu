@@ -40,82 +40,48 @@ __device__ __forceinline__ float step(float a, float h, float u) {
   return MIMO ? __fadd_rn(__fmul_rn(a, h), u) : fmaf(a, h, u);
 }
 
-// Stage the chunk's inputs in shared memory: sa[t][c] = a, and for SISO su[t][c] = u,
-// for MIMO sw / sv = sigmoid(write) / tanh(value) (the ranks are formed on the fly).  The tile
-// is read once from HBM with 16-byte loads when rows and column offsets are aligned.
-template <bool MIMO>
-__device__ __forceinline__ void stage_inputs(const ScanParams &p, int64_t row0, int t0, int nt, int c0, int S,
-                                             float *sa, float *s1, float *s2, int vec) {
+// Stage the chunk's raw decay / write / value columns (slice of S channels, nt rows) in shared
+// memory in their storage dtype: read once from HBM with 16-byte loads when rows and column
+// offsets are aligned.  Layout: three planes [t][c] of the input element type.
+__device__ __forceinline__ void stage_raw(const ScanParams &p, int64_t row0, int t0, int nt, int c0, int S,
+                                          uint8_t *sraw, int vec) {
   const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4;
   const uint8_t *base = reinterpret_cast<const uint8_t *>(p.pc.proj);
+  const int cols[3] = {p.pc.c_decay, p.pc.c_write, p.pc.c_value};
+  const int plane = p.T * S * esz;
   if (vec) {
-    const int VPT = 16 / esz;  // channels per 16-byte vector
+    const int VPT = 16 / esz;
     const int groups = S / VPT;
-    for (int i = threadIdx.x; i < nt * groups; i += blockDim.x) {
-      const int t = i / groups, cg = (i - t * groups) * VPT;
-      const int c = c0 + cg;
-      if (c >= p.C) continue;
-      const uint8_t *rowp = base + ((row0 + t0 + t) * p.pc.ld) * esz;
-      float dv[8], wv[8], vv[8];
-      const uint4 d4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_decay + c) * esz);
-      const uint4 w4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_write + c) * esz);
-      const uint4 v4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_value + c) * esz);
-      if (esz == 2) {
-        const __nv_bfloat16 *dh = reinterpret_cast<const __nv_bfloat16 *>(&d4);
-        const __nv_bfloat16 *wh = reinterpret_cast<const __nv_bfloat16 *>(&w4);
-        const __nv_bfloat16 *vh = reinterpret_cast<const __nv_bfloat16 *>(&v4);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          dv[j] = __bfloat162float(dh[j]);
-          wv[j] = __bfloat162float(wh[j]);
-          vv[j] = __bfloat162float(vh[j]);
-        }
-      } else {
-        const float *df = reinterpret_cast<const float *>(&d4);
-        const float *wf = reinterpret_cast<const float *>(&w4);
-        const float *vf = reinterpret_cast<const float *>(&v4);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          dv[j] = df[j];
-          wv[j] = wf[j];
-          vv[j] = vf[j];
-        }
-      }
-      for (int j = 0; j < VPT; ++j) {
-        const int o = t * S + cg + j;
-        sa[o] = sigmoidf_(dv[j] + p.decay_bias[c + j]);
-        const float w = sigmoidf_(wv[j]), v = tanhf(vv[j]);
-        if (MIMO) {
-          s1[o] = w;
-          s2[o] = v;
-        } else {
-          s1[o] = w * v;
-        }
-      }
+    for (int i = threadIdx.x; i < 3 * nt * groups; i += blockDim.x) {
+      const int pl = i / (nt * groups), rem = i - pl * nt * groups;
+      const int t = rem / groups, cg = (rem - t * groups) * VPT;
+      if (c0 + cg >= p.C) continue;
+      const uint4 v = *reinterpret_cast<const uint4 *>(base + ((row0 + t0 + t) * p.pc.ld + cols[pl] + c0 + cg) * esz);
+      *reinterpret_cast<uint4 *>(sraw + pl * plane + (t * S + cg) * esz) = v;
     }
   } else {
-    for (int i = threadIdx.x; i < nt * S; i += blockDim.x) {
-      const int t = i / S, cl = i - t * S, c = c0 + cl;
-      if (c >= p.C) continue;
-      const int64_t rb = (row0 + t0 + t) * p.pc.ld;
-      const float dr = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_decay + c);
-      const float w = sigmoidf_(load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_write + c));
-      const float v = tanhf(load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_value + c));
-      sa[i] = sigmoidf_(dr + p.decay_bias[c]);
-      if (MIMO) {
-        s1[i] = w;
-        s2[i] = v;
-      } else {
-        s1[i] = w * v;
-      }
+    for (int i = threadIdx.x; i < 3 * nt * S; i += blockDim.x) {
+      const int pl = i / (nt * S), rem = i - pl * nt * S;
+      const int t = rem / S, cl = rem - t * S;
+      if (c0 + cl >= p.C) continue;
+      const float v = load_f(p.pc.proj, p.pc.dtype, (row0 + t0 + t) * p.pc.ld + cols[pl] + c0 + cl);
+      if (esz == 2)
+        reinterpret_cast<__nv_bfloat16 *>(sraw + pl * plane)[t * S + cl] = __float2bfloat16_rn(v);
+      else
+        reinterpret_cast<float *>(sraw + pl * plane)[t * S + cl] = v;
     }
   }
 }
 
+__device__ __forceinline__ float raw_at(const uint8_t *plane, int dtype, int i) {
+  return dtype == TESM_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(plane)[i])
+                            : reinterpret_cast<const float *>(plane)[i];
+}
+
 template <int RM, bool MIMO>
 __global__ void k_scan(ScanParams p, int vec) {
-  extern __shared__ float sm_scan[];
-  __shared__ int s_tile, s_flag;
+  extern __shared__ __align__(16) uint8_t sm_scan[];
+  __shared__ int s_tile, s_jinc;
   if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1);
   __syncthreads();
   const int tile = s_tile;
@@ -128,18 +94,35 @@ __global__ void k_scan(ScanParams p, int vec) {
   const int c = c0 + threadIdx.x;
   const bool active = c < p.C;
   const int t0 = chunk * p.T, t1 = min(t0 + p.T, p.L), nt = t1 - t0;
-  float *sa = sm_scan, *s1 = sa + p.T * S, *s2 = s1 + p.T * S;
+  const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4;
+  const int plane = p.T * S * esz;
+  const uint8_t *pd = sm_scan, *pw = sm_scan + plane, *pv = sm_scan + 2 * plane;
   const int64_t row0 = (int64_t)b * p.L;
-  stage_inputs<MIMO>(p, row0, t0, nt, c0, S, sa, s1, s2, vec);
+  stage_raw(p, row0, t0, nt, c0, S, sm_scan, vec);
   float mx[RM];
 #pragma unroll
   for (int r = 0; r < RM; ++r) mx[r] = 0.f;
-  if (MIMO && active) {
-    const int h = c / p.D, d = c - h * p.D;
+  float db = 0.f;
+  if (active) {
+    db = p.decay_bias[c];
+    if (MIMO) {
+      const int h = c / p.D, d = c - h * p.D;
 #pragma unroll
-    for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
+      for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
+    }
   }
   __syncthreads();
+  auto inputs = [&](int t, float &a, float (&u)[RM]) {
+    const int i = t * S + threadIdx.x;
+    a = sigmoidf_(raw_at(pd, p.pc.dtype, i) + db);
+    const float w = sigmoidf_(raw_at(pw, p.pc.dtype, i)), v = tanhf(raw_at(pv, p.pc.dtype, i));
+    if (MIMO) {
+#pragma unroll
+      for (int r = 0; r < RM; ++r) u[r] = __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r]));
+    } else {
+      u[0] = w * v;
+    }
+  };
 
   // pass 1: aggregate affine map of this chunk (A shared by the ranks)
   float A = 1.f, U[RM];
@@ -147,14 +130,10 @@ __global__ void k_scan(ScanParams p, int vec) {
   for (int r = 0; r < RM; ++r) U[r] = 0.f;
   if (active) {
     for (int t = 0; t < nt; ++t) {
-      const float a = sa[t * S + threadIdx.x];
-      if (MIMO) {
-        const float w = s1[t * S + threadIdx.x], v = s2[t * S + threadIdx.x];
+      float a, u[RM];
+      inputs(t, a, u);
 #pragma unroll
-        for (int r = 0; r < RM; ++r) U[r] = step<true>(a, U[r], __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r])));
-      } else {
-        U[0] = step<false>(a, U[0], s1[t * S + threadIdx.x]);
-      }
+      for (int r = 0; r < RM; ++r) U[r] = step<MIMO>(a, U[r], u[r]);
       A *= a;
     }
   }
@@ -170,48 +149,52 @@ __global__ void k_scan(ScanParams p, int vec) {
     __syncthreads();
     if (threadIdx.x == 0) st_release(flag_row + chunk, 1);
   }
-  // look-back for the carry entering this chunk
+  // look-back for the carry entering this chunk: warp 0 scans 32 predecessor flags per round
+  // trip and finds the nearest inclusive chunk j with every chunk in (j, chunk) published;
+  // then every thread folds the inclusive state and those aggregates forward.
   float h[RM];
 #pragma unroll
   for (int r = 0; r < RM; ++r) h[r] = 0.f;
   if (active && p.h0) h[0] = (float)p.h0[(int64_t)b * p.C + c];
   if (chunk > 0) {
-    float Ar = 1.f, Ur[RM];
-#pragma unroll
-    for (int r = 0; r < RM; ++r) Ur[r] = 0.f;
-    int j = chunk - 1;
-    while (true) {
-      if (threadIdx.x == 0) {
-        const long long start = clock64();
-        int f;
-        while ((f = ld_acquire(flag_row + j)) == 0) {
-          if (clock64() - start > kSpinLimit * 64) {
-            flag_timeout();
-            f = -1;
-            break;
-          }
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      int base = chunk - 1, jinc = -1;
+      const long long start = clock64();
+      while (true) {
+        const int j = base - lane;
+        const int f = j >= 0 ? ld_acquire(flag_row + j) : 2;
+        const unsigned b2 = __ballot_sync(0xffffffffu, f == 2);
+        const unsigned b0 = __ballot_sync(0xffffffffu, f == 0);
+        const int first2 = b2 ? __ffs(b2) - 1 : 32, first0 = b0 ? __ffs(b0) - 1 : 32;
+        if (first2 < 32 && first2 < first0) {
+          jinc = base - first2;
+          break;
         }
-        s_flag = f;
-      }
-      __syncthreads();
-      const int f = s_flag;
-      __syncthreads();
-      if (f < 0) break;
-      const int64_t jidx = (int64_t)b * p.nchunks + j;
-      if (f == 2) {
-        if (active) {
-#pragma unroll
-          for (int r = 0; r < RM; ++r) h[r] = fmaf(Ar, p.incl[(jidx * RM + r) * p.C + c], Ur[r]);
+        if (first0 == 32) {  // 32 published aggregates, no inclusive yet: look further back
+          base -= 32;
+          continue;
         }
-        break;
+        if (clock64() - start > kSpinLimit * 64) {
+          if (lane == 0) flag_timeout();
+          jinc = -2;
+          break;
+        }
       }
-      if (active) {
-        const float gA = p.aggA[jidx * p.C + c];
+      if (lane == 0) s_jinc = jinc;
+    }
+    __syncthreads();
+    const int jinc = s_jinc;
+    if (active && jinc >= 0) {
+      const int64_t ji = (int64_t)b * p.nchunks + jinc;
 #pragma unroll
-        for (int r = 0; r < RM; ++r) Ur[r] = fmaf(Ar, p.aggU[(jidx * RM + r) * p.C + c], Ur[r]);
-        Ar *= gA;
+      for (int r = 0; r < RM; ++r) h[r] = p.incl[(ji * RM + r) * p.C + c];
+      for (int j = jinc + 1; j < chunk; ++j) {
+        const int64_t jj = (int64_t)b * p.nchunks + j;
+        const float gA = p.aggA[jj * p.C + c];
+#pragma unroll
+        for (int r = 0; r < RM; ++r) h[r] = fmaf(gA, h[r], p.aggU[(jj * RM + r) * p.C + c]);
       }
-      --j;  // chunk 0 always publishes an inclusive value, so j stays >= 0
     }
   }
   // publish the inclusive states for successors
@@ -227,18 +210,13 @@ __global__ void k_scan(ScanParams p, int vec) {
   // pass 2: states of this chunk from the carry
   if (active) {
     for (int t = 0; t < nt; ++t) {
-      const float a = sa[t * S + threadIdx.x];
+      float a, u[RM];
+      inputs(t, a, u);
       const int64_t orow = (row0 + t0 + t) * RM;
-      if (MIMO) {
-        const float w = s1[t * S + threadIdx.x], v = s2[t * S + threadIdx.x];
 #pragma unroll
-        for (int r = 0; r < RM; ++r) {
-          h[r] = step<true>(a, h[r], __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r])));
-          p.states[(orow + r) * p.C + c] = h[r];
-        }
-      } else {
-        h[0] = step<false>(a, h[0], s1[t * S + threadIdx.x]);
-        p.states[orow * p.C + c] = h[0];
+      for (int r = 0; r < RM; ++r) {
+        h[r] = step<MIMO>(a, h[r], u[r]);
+        p.states[(orow + r) * p.C + c] = h[r];
       }
     }
     if (t1 == p.L) {
@@ -255,8 +233,8 @@ struct ScanLayout {
 
 static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
   ScanLayout s;
-  s.T = 64;
-  s.slice = C < 128 ? (int)round_up(C, 32) : 128;
+  s.T = 32;
+  s.slice = C < 256 ? (int)round_up(C, 32) : 256;
   s.nchunks = (int)ceil_div(L, s.T);
   s.nslices = (int)ceil_div(C, s.slice);
   const int64_t nA = B * s.nchunks * C;
@@ -270,7 +248,7 @@ static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
 template <int RM, bool MIMO>
 static int launch_scan(ScanParams &p, cudaStream_t st, int slice) {
   const int64_t grid = (int64_t)p.nchunks * p.B * p.nslices;
-  const size_t smem = sizeof(float) * (size_t)p.T * slice * (MIMO ? 3 : 2);
+  const size_t smem = (size_t)3 * p.T * slice * (p.pc.dtype == TESM_BF16 ? 2 : 4);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_scan<RM, MIMO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
