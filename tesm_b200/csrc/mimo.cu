@@ -22,7 +22,7 @@ struct MimoEntParams {
 };
 
 template <int W, int RM>
-__global__ void k_mimo_local_ent(MimoEntParams p) {
+__global__ void __launch_bounds__(128, 3) k_mimo_local_ent(MimoEntParams p) {
   extern __shared__ float sm[];
   const int R = p.R, T = p.T, RP = R + 1;
   float *qs = sm;
@@ -106,6 +106,7 @@ static int launch_mimo_ent(MimoEntParams &p, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_mimo_local_ent<W, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(k_mimo_local_ent<W, RM>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr = true;
   }
   if (smem > 160 * 1024) return fail(TESM_EUNSUPPORTED, "mimo_local_ent: ent_rank too large");

@@ -79,7 +79,7 @@ __device__ __forceinline__ float raw_at(const uint8_t *plane, int dtype, int i) 
 }
 
 template <int RM, bool MIMO>
-__global__ void k_scan(ScanParams p, int vec) {
+__global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
   extern __shared__ __align__(16) uint8_t sm_scan[];
   __shared__ int s_tile, s_jinc;
   if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1);
@@ -252,6 +252,7 @@ static int launch_scan(ScanParams &p, cudaStream_t st, int slice) {
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_scan<RM, MIMO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(k_scan<RM, MIMO>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr = true;
   }
   const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4, vpt = 16 / esz;

@@ -90,7 +90,7 @@ __device__ __forceinline__ void local_channels(const LocalEntParams &p, const fl
 }
 
 template <int W>
-__global__ void k_siso_local_ent(LocalEntParams p) {
+__global__ void __launch_bounds__(256, 2) k_siso_local_ent(LocalEntParams p) {
   extern __shared__ float sm[];
   const int R = p.R, T = p.T, RP = R + 1;
   float *qs = sm;                    // T x RP
@@ -124,7 +124,7 @@ struct LocalEntCodesParams {
 };
 
 template <int W>
-__global__ void k_siso_local_ent_codes(LocalEntCodesParams pp) {
+__global__ void __launch_bounds__(256, 2) k_siso_local_ent_codes(LocalEntCodesParams pp) {
   extern __shared__ float sm[];
   const LocalEntParams &p = pp.e;
   const int R = p.R, T = p.T, D = p.D, DP1 = D + 1;
@@ -335,6 +335,7 @@ static int launch_local(LocalEntParams &p, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr = true;
   }
   if (smem > 160 * 1024) return fail(TESM_EUNSUPPORTED, "local_ent: ent_rank too large");
@@ -387,6 +388,7 @@ static int launch_local_codes(LocalEntCodesParams &pp, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr = true;
   }
   if (smem > 200 * 1024) return fail(TESM_EUNSUPPORTED, "local_ent_codes: d_state / ent_rank too large");
