@@ -189,11 +189,22 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
       const int64_t ji = (int64_t)b * p.nchunks + jinc;
 #pragma unroll
       for (int r = 0; r < RM; ++r) h[r] = p.incl[(ji * RM + r) * p.C + c];
-      for (int j = jinc + 1; j < chunk; ++j) {
-        const int64_t jj = (int64_t)b * p.nchunks + j;
-        const float gA = p.aggA[jj * p.C + c];
+      // fold forward, FB aggregates per batch with all their loads issued first
+      constexpr int FB = RM >= 4 ? 2 : (RM == 2 ? 4 : 8);
+      for (int j0 = jinc + 1; j0 < chunk; j0 += FB) {
+        float gA[FB], gU[FB][RM];
 #pragma unroll
-        for (int r = 0; r < RM; ++r) h[r] = fmaf(gA, h[r], p.aggU[(jj * RM + r) * p.C + c]);
+        for (int k = 0; k < FB; ++k) {
+          const int j = j0 + k;
+          const int64_t jj = (int64_t)b * p.nchunks + (j < chunk ? j : jinc);
+          gA[k] = j < chunk ? p.aggA[jj * p.C + c] : 1.f;
+#pragma unroll
+          for (int r = 0; r < RM; ++r) gU[k][r] = j < chunk ? p.aggU[(jj * RM + r) * p.C + c] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < FB; ++k)
+#pragma unroll
+          for (int r = 0; r < RM; ++r) h[r] = fmaf(gA[k], h[r], gU[k][r]);
       }
     }
   }

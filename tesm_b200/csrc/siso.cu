@@ -51,39 +51,34 @@ __device__ __forceinline__ void local_front(const LocalEntParams &p, float *qs, 
   __syncthreads();
 }
 
-// Per channel: sliding window of states in registers, 8 timesteps prefetched at a time.
-// emit(t, d, tanh_ent, chg) consumes the outputs.
+// Output (t, d) depends only on states[t-W+1..t][d] and the weights of row t (no recurrence
+// over t), so the work is split into independent items of TB consecutive timesteps x one
+// channel: each item loads its TB + W - 1 states at once (all in flight together) and emits
+// TB outputs.  emit(t, d, tanh_ent, chg) consumes them.
 template <int W, class Emit>
 __device__ __forceinline__ void local_channels(const LocalEntParams &p, const float *tw, int64_t row0, int t0, int nt,
                                                Emit emit) {
+  constexpr int TB = 8;
   const int D = p.D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    // before the first shift win[o] holds states[t0 - 1 - o]; after it, win[o] = states[t - o]
-    float win[W];
-    win[W - 1] = 0.f;
+  const int nblk = (nt + TB - 1) / TB;
+  for (int item = threadIdx.x; item < nblk * D; item += blockDim.x) {
+    const int tb = (item / D) * TB, d = item - (item / D) * D;
+    float win[TB + W - 1];  // win[i] = states[t0 + tb - (W-1) + i]
 #pragma unroll
-    for (int o = 1; o < W; ++o) {
-      const int j = t0 - o;
-      win[o - 1] = j >= 0 ? p.states[(row0 + j) * D + d] : 0.f;
+    for (int i = 0; i < TB + W - 1; ++i) {
+      const int j = t0 + tb - (W - 1) + i;
+      win[i] = (j >= 0 && j < t0 + nt) ? p.states[(row0 + j) * D + d] : 0.f;
     }
-    for (int tb = 0; tb < nt; tb += 8) {
-      float sv[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) sv[j] = tb + j < nt ? p.states[(row0 + t0 + tb + j) * D + d] : 0.f;
+    for (int k = 0; k < TB; ++k) {
+      const int t = tb + k;
+      if (t < nt) {
+        const float s = win[k + W - 1];
+        float avg = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (tb + j < nt) {
-          const int t = tb + j;
-#pragma unroll
-          for (int o = W - 1; o > 0; --o) win[o] = win[o - 1];
-          const float s = sv[j];
-          win[0] = s;
-          float avg = 0.f;
-#pragma unroll
-          for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[o], avg);
-          const float ent = s + p.es * (avg - s);
-          emit(t, d, tanhf(ent), ent - s);
-        }
+        for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[k + W - 1 - o], avg);
+        const float ent = s + p.es * (avg - s);
+        emit(t, d, tanhf(ent), ent - s);
       }
     }
   }
