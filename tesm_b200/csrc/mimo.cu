@@ -50,42 +50,50 @@ __global__ void __launch_bounds__(128, 3) k_mimo_local_ent(MimoEntParams p) {
     return gt - o >= 0 && (!quirk || o >= W - 1 - gt);
   });
   __syncthreads();
-  // independent items of TB timesteps x one channel (no recurrence over t); ranks in turn
-  constexpr int TB = 4;
-  const int nblk = (nt + TB - 1) / TB;
-  for (int item = threadIdx.x; item < nblk * p.D; item += blockDim.x) {
-    const int tb = (item / p.D) * TB, d = item - (item / p.D) * p.D;
+  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
     const int c = h * p.D + d;
-    float ent[TB], chg[TB];
+    float mo[RM];
 #pragma unroll
-    for (int k = 0; k < TB; ++k) ent[k] = chg[k] = 0.f;
+    for (int r = 0; r < RM; ++r) mo[r] = p.mimo_o[((int64_t)h * RM + r) * p.D + d];
+    float win[RM][W];  // before the first shift win[r][o] = states_r[t0 - 1 - o]
 #pragma unroll
-    for (int r = 0; r < RM; ++r) {
-      const float mo = p.mimo_o[((int64_t)h * RM + r) * p.D + d];
-      float win[TB + W - 1];
+    for (int r = 0; r < RM; ++r) win[r][W - 1] = 0.f;
 #pragma unroll
-      for (int i = 0; i < TB + W - 1; ++i) {
-        const int j = t0 + tb - (W - 1) + i;
-        win[i] = (j >= 0 && j < t0 + nt) ? p.states[((row0 + j) * RM + r) * C + c] : 0.f;
-      }
+    for (int o = 1; o < W; ++o) {
+      const int j = t0 - o;
 #pragma unroll
-      for (int k = 0; k < TB; ++k) {
-        const int t = tb + k < nt ? tb + k : nt - 1;
-        const float s = win[k + W - 1];
-        float avg = 0.f;
-#pragma unroll
-        for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[k + W - 1 - o], avg);
-        const float e_r = s + p.es * (avg - s);
-        ent[k] = fmaf(mo, e_r, ent[k]);
-        chg[k] = fmaf(mo, e_r - s, chg[k]);
-      }
+      for (int r = 0; r < RM; ++r) win[r][o - 1] = j >= 0 ? p.states[((row0 + j) * RM + r) * C + c] : 0.f;
     }
+    constexpr int PF = 4;  // timesteps prefetched per batch (x RM loads)
+    for (int tb = 0; tb < nt; tb += PF) {
+      float sv[PF][RM];
 #pragma unroll
-    for (int k = 0; k < TB; ++k) {
-      if (tb + k < nt) {
-        const int64_t row = row0 + t0 + tb + k;
-        store_f(p.out_tanh, p.out_dtype, row * C + c, tanhf(ent[k]));
-        store_f(p.out_chg, p.out_dtype, row * C + c, chg[k]);
+      for (int j = 0; j < PF; ++j)
+#pragma unroll
+        for (int r = 0; r < RM; ++r)
+          sv[j][r] = tb + j < nt ? p.states[((row0 + t0 + tb + j) * RM + r) * C + c] : 0.f;
+#pragma unroll
+      for (int j = 0; j < PF; ++j) {
+        if (tb + j < nt) {
+          const int t = tb + j;
+          const int64_t row = row0 + t0 + t;
+          float ent = 0.f, chg = 0.f;
+#pragma unroll
+          for (int r = 0; r < RM; ++r) {
+#pragma unroll
+            for (int o = W - 1; o > 0; --o) win[r][o] = win[r][o - 1];
+            const float s = sv[j][r];
+            win[r][0] = s;
+            float avg = 0.f;
+#pragma unroll
+            for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[r][o], avg);
+            const float e_r = s + p.es * (avg - s);
+            ent = fmaf(mo[r], e_r, ent);
+            chg = fmaf(mo[r], e_r - s, chg);
+          }
+          store_f(p.out_tanh, p.out_dtype, row * C + c, tanhf(ent));
+          store_f(p.out_chg, p.out_dtype, row * C + c, chg);
+        }
       }
     }
   }

@@ -40,42 +40,68 @@ __device__ __forceinline__ float step(float a, float h, float u) {
   return MIMO ? __fadd_rn(__fmul_rn(a, h), u) : fmaf(a, h, u);
 }
 
-// Stage the chunk's raw decay / write / value columns (slice of S channels, nt rows) in shared
-// memory in their storage dtype: read once from HBM with 16-byte loads when rows and column
-// offsets are aligned.  Layout: three planes [t][c] of the input element type.
-__device__ __forceinline__ void stage_raw(const ScanParams &p, int64_t row0, int t0, int nt, int c0, int S,
-                                          uint8_t *sraw, int vec) {
+__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.f + __expf(-x)); }
+
+// Stage the chunk's inputs in shared memory, transformed once: plane 0 = a = sigmoid(decay +
+// decay_bias); SISO plane 1 = u = sigmoid(write) * tanh(value); MIMO planes 1, 2 = sigmoid(write),
+// tanh(value) (the ranks are formed on the fly).  Rows are read once with 16-byte loads when
+// rows and column offsets are aligned.  (sigmoid with __expf: relative error ~1e-7.)
+template <bool MIMO>
+__device__ __forceinline__ void stage_inputs(const ScanParams &p, int64_t row0, int t0, int nt, int c0, int S,
+                                             float *s0, float *s1, float *s2, int vec) {
   const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4;
   const uint8_t *base = reinterpret_cast<const uint8_t *>(p.pc.proj);
-  const int cols[3] = {p.pc.c_decay, p.pc.c_write, p.pc.c_value};
-  const int plane = p.T * S * esz;
-  if (vec) {
-    const int VPT = 16 / esz;
-    const int groups = S / VPT;
-    for (int i = threadIdx.x; i < 3 * nt * groups; i += blockDim.x) {
-      const int pl = i / (nt * groups), rem = i - pl * nt * groups;
-      const int t = rem / groups, cg = (rem - t * groups) * VPT;
-      if (c0 + cg >= p.C) continue;
-      const uint4 v = *reinterpret_cast<const uint4 *>(base + ((row0 + t0 + t) * p.pc.ld + cols[pl] + c0 + cg) * esz);
-      *reinterpret_cast<uint4 *>(sraw + pl * plane + (t * S + cg) * esz) = v;
+  const int VPT = vec ? 16 / esz : 1;
+  const int groups = S / VPT;
+  for (int i = threadIdx.x; i < nt * groups; i += blockDim.x) {
+    const int t = i / groups, cg = (i - t * groups) * VPT;
+    const int c = c0 + cg;
+    if (c >= p.C) continue;
+    const uint8_t *rowp = base + ((row0 + t0 + t) * p.pc.ld) * esz;
+    float dv[8], wv[8], vv[8];
+    if (vec) {
+      const uint4 d4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_decay + c) * esz);
+      const uint4 w4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_write + c) * esz);
+      const uint4 v4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_value + c) * esz);
+      if (esz == 2) {
+        const __nv_bfloat16 *dh = reinterpret_cast<const __nv_bfloat16 *>(&d4);
+        const __nv_bfloat16 *wh = reinterpret_cast<const __nv_bfloat16 *>(&w4);
+        const __nv_bfloat16 *vh = reinterpret_cast<const __nv_bfloat16 *>(&v4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          dv[j] = __bfloat162float(dh[j]);
+          wv[j] = __bfloat162float(wh[j]);
+          vv[j] = __bfloat162float(vh[j]);
+        }
+      } else {
+        const float *df = reinterpret_cast<const float *>(&d4);
+        const float *wf = reinterpret_cast<const float *>(&w4);
+        const float *vf = reinterpret_cast<const float *>(&v4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          dv[j] = df[j];
+          wv[j] = wf[j];
+          vv[j] = vf[j];
+        }
+      }
+    } else {
+      const int64_t rb = (row0 + t0 + t) * p.pc.ld;
+      dv[0] = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_decay + c);
+      wv[0] = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_write + c);
+      vv[0] = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_value + c);
     }
-  } else {
-    for (int i = threadIdx.x; i < 3 * nt * S; i += blockDim.x) {
-      const int pl = i / (nt * S), rem = i - pl * nt * S;
-      const int t = rem / S, cl = rem - t * S;
-      if (c0 + cl >= p.C) continue;
-      const float v = load_f(p.pc.proj, p.pc.dtype, (row0 + t0 + t) * p.pc.ld + cols[pl] + c0 + cl);
-      if (esz == 2)
-        reinterpret_cast<__nv_bfloat16 *>(sraw + pl * plane)[t * S + cl] = __float2bfloat16_rn(v);
-      else
-        reinterpret_cast<float *>(sraw + pl * plane)[t * S + cl] = v;
+    for (int j = 0; j < VPT; ++j) {
+      const int o = t * S + cg + j;
+      s0[o] = fast_sigmoid(dv[j] + p.decay_bias[c + j]);
+      const float w = fast_sigmoid(wv[j]), v = tanhf(vv[j]);
+      if (MIMO) {
+        s1[o] = w;
+        s2[o] = v;
+      } else {
+        s1[o] = w * v;
+      }
     }
   }
-}
-
-__device__ __forceinline__ float raw_at(const uint8_t *plane, int dtype, int i) {
-  return dtype == TESM_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(plane)[i])
-                            : reinterpret_cast<const float *>(plane)[i];
 }
 
 template <int RM, bool MIMO>
@@ -94,33 +120,27 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
   const int c = c0 + threadIdx.x;
   const bool active = c < p.C;
   const int t0 = chunk * p.T, t1 = min(t0 + p.T, p.L), nt = t1 - t0;
-  const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4;
-  const int plane = p.T * S * esz;
-  const uint8_t *pd = sm_scan, *pw = sm_scan + plane, *pv = sm_scan + 2 * plane;
+  float *s0 = reinterpret_cast<float *>(sm_scan), *s1 = s0 + p.T * S, *s2 = s1 + p.T * S;
   const int64_t row0 = (int64_t)b * p.L;
-  stage_raw(p, row0, t0, nt, c0, S, sm_scan, vec);
+  stage_inputs<MIMO>(p, row0, t0, nt, c0, S, s0, s1, s2, vec);
   float mx[RM];
 #pragma unroll
   for (int r = 0; r < RM; ++r) mx[r] = 0.f;
-  float db = 0.f;
-  if (active) {
-    db = p.decay_bias[c];
-    if (MIMO) {
-      const int h = c / p.D, d = c - h * p.D;
+  if (active && MIMO) {
+    const int h = c / p.D, d = c - h * p.D;
 #pragma unroll
-      for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
-    }
+    for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
   }
   __syncthreads();
   auto inputs = [&](int t, float &a, float (&u)[RM]) {
     const int i = t * S + threadIdx.x;
-    a = sigmoidf_(raw_at(pd, p.pc.dtype, i) + db);
-    const float w = sigmoidf_(raw_at(pw, p.pc.dtype, i)), v = tanhf(raw_at(pv, p.pc.dtype, i));
+    a = s0[i];
     if (MIMO) {
+      const float w = s1[i], v = s2[i];
 #pragma unroll
       for (int r = 0; r < RM; ++r) u[r] = __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r]));
     } else {
-      u[0] = w * v;
+      u[0] = s1[i];
     }
   };
 
@@ -259,7 +279,7 @@ static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
 template <int RM, bool MIMO>
 static int launch_scan(ScanParams &p, cudaStream_t st, int slice) {
   const int64_t grid = (int64_t)p.nchunks * p.B * p.nslices;
-  const size_t smem = (size_t)3 * p.T * slice * (p.pc.dtype == TESM_BF16 ? 2 : 4);
+  const size_t smem = sizeof(float) * (size_t)(MIMO ? 3 : 2) * p.T * slice;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_scan<RM, MIMO>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
