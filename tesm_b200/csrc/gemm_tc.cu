@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -621,6 +622,13 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   cudaStream_t st = (cudaStream_t)stream;
   if (M <= 256) {  // decode-sized batches: skinny tiles, enough CTAs, weights streamed once
+    static const int forced = [] {
+      const char *e = getenv("TESM_SKINNY_BN");  // tuning override: 32, 64 or 128
+      return e ? atoi(e) : 0;
+    }();
+    if (forced == 128) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
+    if (forced == 64) return tc::launch<64, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
+    if (forced == 32) return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     // every CTA re-reads the 256-row activation tile from L2, so wider N tiles cut L2 traffic;
     // narrower ones keep enough CTAs in flight when N is small
     if (N >= 8192) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
