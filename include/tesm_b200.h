@@ -87,9 +87,10 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
  * TMEM accumulators, TMA-staged operands); same contract as tesm_b200_gemv_int2 but the
  * activation codes are row-major (TESM_LAYOUT_ROWMAJOR, ld_codes multiple of 16) and the
  * weights are the int8 ternary matrix from tesm_b200_pack_ternary (ld_tern multiple of 16).
- * splitk_ws (nullable, >= M*N int32, zero-filled before its first use and left zeroed by every
- * call): when there are fewer output tiles than SMs (decode batches), K is split across CTAs and
- * the int32 partials are summed atomically into it -- exact, so the result is deterministic. */
+ * splitk_ws (nullable, caller-owned scratch of ws_bytes): when there are fewer output tiles than
+ * SMs (decode batches), K is split across up to 8 CTAs per tile; each split stores its int32
+ * partial tile into its own M*N slice of the workspace and a finalize kernel sums the slices in a
+ * fixed order (exact integers, deterministic).  The split count is capped so S*M*N*4 <= ws_bytes. */
 /* state_proj + ent_proj + output combine in one tcgen05 GEMM (tesm.py:1256-1260): two TMEM
  * accumulators, acc1 over the first Kh columns (codes of tanh(ent) x state_proj ternary weights),
  * acc2 over the next Kh (codes of ent - s x ent_proj weights); the epilogue writes

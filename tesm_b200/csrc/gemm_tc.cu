@@ -59,6 +59,7 @@ struct Params {
   // (exact, so the result does not depend on the order), a finalize kernel scales them
   int splits;
   int32_t *ws;
+  int64_t ws_bytes;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -269,16 +270,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int row = (mt * MT + sub) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
       if (!DUAL && p.splits > 1) {
+        const int c_lo = MT == 2 ? 0 : half * (BN / 64), c_hi = MT == 2 ? BN / 32 : (half + 1) * (BN / 64);
 #pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        for (int c = c_lo; c < c_hi; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, r);
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + sub * BN + c * 32, r);
           const int n0 = nt * BN + c * 32;
           if (!row_ok || n0 >= p.N) continue;
-          int32_t *wrow = p.ws + (int64_t)row * p.N + n0;
+          // each split owns its slice of the workspace: plain stores, summed by the finalize kernel
+          int32_t *wrow = p.ws + ((int64_t)(u % p.splits) * p.M + row) * p.N + n0;
+          if (n0 + 32 <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) atomicAdd(wrow + j, (int32_t)r[j]);
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<int4 *>(wrow)[j] = make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2],
+                                                            (int)r[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) wrow[j] = (int32_t)r[j];
+          }
         }
         fence_before();
         __syncwarp();
@@ -426,29 +435,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-// Split-K finalize: scale the int32 sums (optionally the SiLU gate over 128-row interleaved
-// gate/up blocks), write the output, and zero the workspace for its next use.
-__global__ void k_splitk_finalize(int32_t *ws, int M, int N, const float *inv_scale, const float *w_deq, int per_row,
-                                  int swiglu, void *out, int out_dtype, int64_t ldo, int32_t *acc_out,
-                                  int64_t ld_acc) {
+// Split-K finalize: sum the per-split int32 partials, scale (optionally apply the SiLU gate over
+// 128-row interleaved gate/up blocks) and write the output.
+__global__ void k_splitk_finalize(const int32_t *ws, int splits, int M, int N, const float *inv_scale,
+                                  const float *w_deq, int per_row, int swiglu, void *out, int out_dtype, int64_t ldo,
+                                  int32_t *acc_out, int64_t ld_acc) {
   const int nout = swiglu ? N / 2 : N;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * nout) return;
   const int m = (int)(i / nout), n = (int)(i - (int64_t)m * nout);
   const float xs = inv_scale[m];
+  const int64_t slice = (int64_t)M * N;
   if (swiglu) {
     const int b = n >> 7, j = n & 127;
     const int ng = b * 256 + j, nu = ng + 128;
-    int32_t *wr = ws + (int64_t)m * N;
-    const float g = (float)wr[ng] * xs * w_deq[ng];
-    const float u = (float)wr[nu] * xs * w_deq[nu];
-    wr[ng] = 0;
-    wr[nu] = 0;
+    int32_t ag = 0, au = 0;
+    for (int s = 0; s < splits; ++s) {
+      ag += ws[s * slice + (int64_t)m * N + ng];
+      au += ws[s * slice + (int64_t)m * N + nu];
+    }
+    const float g = (float)ag * xs * w_deq[ng];
+    const float u = (float)au * xs * w_deq[nu];
     store_f(out, out_dtype, (int64_t)m * ldo + n, (g / (1.f + expf(-g))) * u);
   } else {
-    int32_t *w = ws + (int64_t)m * N + n;
-    const int32_t a = *w;
-    *w = 0;
+    int32_t a = 0;
+    for (int s = 0; s < splits; ++s) a += ws[s * slice + (int64_t)m * N + n];
     const float wd = per_row ? w_deq[n] : w_deq[0];
     store_f(out, out_dtype, (int64_t)m * ldo + n, (float)a * xs * wd);
     if (acc_out) acc_out[(int64_t)m * ld_acc + n] = a;
@@ -504,10 +515,11 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   p.group_m = 16;
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   p.splits = 1;
-  if (!DUAL && MT == 1 && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
+  if (!DUAL && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
     int s = (int)ceil_div(sm_count(), tiles);
     if (s > 8) s = 8;
     if (s > p.num_k_blocks / 4) s = p.num_k_blocks / 4;
+    while (s >= 2 && (int64_t)s * p.M * p.N * 4 > p.ws_bytes) --s;
     if (s >= 2) p.splits = s;
   }
   const int total = tiles * p.splits;
@@ -516,9 +528,9 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   int rc2 = check_launch("gemm_i8");
   if (rc2 || p.splits == 1) return rc2;
   const int64_t n = (int64_t)p.M * (p.swiglu ? p.N / 2 : p.N);
-  k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(p.ws, p.M, p.N, p.inv_scale, p.w_deq, p.per_row,
-                                                                p.swiglu, p.out, p.out_dtype, p.ldo, p.acc_out,
-                                                                p.ld_acc);
+  k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(p.ws, p.splits, p.M, p.N, p.inv_scale, p.w_deq,
+                                                                p.per_row, p.swiglu, p.out, p.out_dtype, p.ldo,
+                                                                p.acc_out, p.ld_acc);
   return check_launch("gemm_i8 split-K finalize");
 }
 
@@ -549,7 +561,10 @@ extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, c
   p.out_dtype = out_dtype;
   p.ldo = ldo;
   p.swiglu = 1;
-  if (splitk_ws && ws_bytes >= M * 2 * F * 4 && ((uintptr_t)splitk_ws & 15) == 0) p.ws = splitk_ws;
+  if (splitk_ws && ((uintptr_t)splitk_ws & 15) == 0) {
+    p.ws = splitk_ws;
+    p.ws_bytes = ws_bytes;
+  }
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
@@ -617,7 +632,10 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
   p.ldo = ldo;
   p.acc_out = acc_out;
   p.ld_acc = ld_acc;
-  if (splitk_ws && ws_bytes >= M * N * 4 && ((uintptr_t)splitk_ws & 15) == 0) p.ws = splitk_ws;
+  if (splitk_ws && ((uintptr_t)splitk_ws & 15) == 0) {
+    p.ws = splitk_ws;
+    p.ws_bytes = ws_bytes;
+  }
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   cudaStream_t st = (cudaStream_t)stream;
@@ -631,7 +649,9 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
     if (forced == 32) return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     // every CTA re-reads the 256-row activation tile from L2, so wider N tiles cut L2 traffic;
     // narrower ones keep enough CTAs in flight when N is small
-    if (N >= 8192) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
+    // with a split-K workspace, wide tiles + K splits give each CTA a K-slice of the activations;
+    // without one, narrower tiles keep enough CTAs in flight
+    if (p.ws || N >= 8192) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     if (N >= 2048) return tc::launch<64, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
   }

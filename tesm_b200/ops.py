@@ -128,15 +128,16 @@ SPLITK_MAX_M = 1024
 
 
 def splitk_workspace(M: int, N: int, device):
-    """Zero-filled int32 split-K workspace shared by the small-M tensor-core GEMMs of a device
-    (every GEMM call leaves it zeroed).  None for large M, where split-K is never chosen."""
+    """int32 split-K scratch shared by the small-M tensor-core GEMMs of a device (room for 8
+    partial M x N slices; every split writes its slice before the finalize reads it, so no
+    initialisation is needed).  None for large M, where split-K is never chosen."""
     if M > SPLITK_MAX_M:
         return None
-    need = M * N
+    need = 8 * M * N
     key = torch.device(device).index
     buf = _SPLITK.get(key)
     if buf is None or buf.numel() < need:
-        buf = torch.zeros(max(need, 1 << 20), device=device, dtype=torch.int32)
+        buf = torch.empty(max(need, 1 << 20), device=device, dtype=torch.int32)
         _SPLITK[key] = buf
     return buf
 
