@@ -515,7 +515,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   p.group_m = 16;
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   p.splits = 1;
-  if (!DUAL && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
+  if (!DUAL && MT == 1 && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
     int s = (int)ceil_div(sm_count(), tiles);
     if (s > 8) s = 8;
     if (s > p.num_k_blocks / 4) s = p.num_k_blocks / 4;
@@ -649,9 +649,8 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
     if (forced == 32) return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     // every CTA re-reads the 256-row activation tile from L2, so wider N tiles cut L2 traffic;
     // narrower ones keep enough CTAs in flight when N is small
-    // with a split-K workspace, wide tiles + K splits give each CTA a K-slice of the activations;
-    // without one, narrower tiles keep enough CTAs in flight
-    if (p.ws || N >= 8192) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
+    // wide tiles cut the activation re-reads for large N; narrower ones keep CTAs in flight
+    if (N >= 8192) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     if (N >= 2048) return tc::launch<64, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
   }
