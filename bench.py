@@ -321,6 +321,35 @@ def run_gpu(args, rank, world, local_rank):
     return 0
 
 
+def run_combine_case(args):
+    """Config-5 shaped dual-accumulator combine GEMM (state_proj + ent_proj + output combine) on
+    M = 32768 tokens, d_state 256, d_model 4096, bf16 proj / output (for ncu captures)."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    M, D, Dm = 32768, 256, 4096
+    Np = 2 * Dm + 3 * D + 128
+    proj = torch.randn(M, Np, device="cuda").to(torch.bfloat16)
+    codes = torch.randint(-127, 127, (M, 2 * D), device="cuda", dtype=torch.int8)
+    inv1 = torch.rand(M, device="cuda") * 0.01
+    inv2 = torch.rand(M, device="cuda") * 0.01
+    tern = torch.randint(-1, 2, (Dm, 2 * D), device="cuda", dtype=torch.int8)
+    deq = torch.full((1,), 0.02, device="cuda")
+    y = torch.empty(M, Dm, device="cuda", dtype=torch.bfloat16)
+    for _ in range(args.warmup + args.steps):
+        ops.gemm_combine(codes, D, inv1, inv2, tern, deq, deq, proj, 0, Dm + 3 * D, M, Dm, y)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    ops.gemm_combine(codes, D, inv1, inv2, tern, deq, deq, proj, 0, Dm + 3 * D, M, Dm, y)
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / 1e3
+    byts = M * Dm * 2 * 3 + M * 2 * D
+    print(json.dumps({"kernel": "gemm_i8_combine", "M": M, "ms": t * 1e3, "GB_s": byts / t / 1e9}), flush=True)
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone case of the dominant kernel for ncu captures: one int8 tcgen05 GEMM
     of in_proj-like shape M=16384, N=11008, K=4096 (operands 109 MB + 360 MB output > L2)."""
@@ -514,7 +543,7 @@ def main():
     ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg4"],
                     help="supplementary measurements of BASELINE configs 2-4 (one JSON line per measurement)")
     ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
-    ap.add_argument("--kernel", default=None, choices=["gemm", "decode"], help="run a small ncu case")
+    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine"], help="run a small ncu case")
     args = ap.parse_args()
     if args.workload:
         peaks, _ = load_peaks()
@@ -524,6 +553,8 @@ def main():
         return 0
     if args.kernel == "decode":
         return run_decode_case(args)
+    if args.kernel == "combine":
+        return run_combine_case(args)
     if args.kernel:
         return run_kernel_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
