@@ -57,6 +57,10 @@ __device__ __forceinline__ void store_f(void *p, int dtype, int64_t i, float v) 
 // Round a float to the nearest bfloat16 value (ties to even) and return it as float.
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// Logistic sigmoid from the hardware exponential and an IEEE-rounded reciprocal: no
+// slow-path branches, so a thread can interleave many of them (relative error ~1e-6).
+__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.f + __expf(-x)); }
+
 // Round to the arithmetic precision of `dtype` (identity for fp32).
 __device__ __forceinline__ float round_to(int dtype, float v) { return dtype == TESM_BF16 ? round_bf16(v) : v; }
 

@@ -144,6 +144,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+__device__ __forceinline__ uint4 lds128(uint32_t saddr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
+  return v;
+}
+
+// int32 accumulator -> float without the conversion unit (shared with the transcendentals):
+// for |a| < 2^22, 1.5*2^23 + a is exact in fp32 and its bit pattern is 0x4B400000 + a.  The
+// combine GEMM guarantees the bound (|a| <= 128 * Kh with Kh <= 16384).
+__device__ __forceinline__ float acc_to_f(uint32_t a) {
+  return __int_as_float((int)a + 0x4B400000) - 12582912.f;
+}
+// Sigmoid for the combine epilogue: two transcendental-unit ops (exp2, approximate reciprocal),
+// relative error a few ulp; exp overflow gives 1/inf = 0, the correct limit.
+__device__ __forceinline__ float epi_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
 __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
   const int per_group = p.group_m * p.num_n_tiles;
   const int grp = t / per_group;
@@ -168,6 +189,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
   uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = bars + 2 * STAGES + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  // DUAL: per epilogue warp, its rows' bf16 local / gate operands of one tile, staged by cp.async
+  // ([chunk][array][lane][64 B], 16-byte units swizzled by lane so a warp's reads hit all banks)
+  uint8_t *sP = sB + STAGES * B_BYTES + 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : MT * BN;  // TMEM columns of one tile's accumulator(s)
@@ -260,10 +284,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp stores
     uint32_t tile_i = 0;
+    // DUAL with bf16 proj: the local / gate operands do not depend on the accumulators, so they
+    // are copied into shared memory asynchronously one tile ahead: chunk cc of the next tile is
+    // requested as soon as chunk cc of this one has been read.
+    constexpr int DCH = DUAL ? BN / 64 : 1;
+    const bool dual_pre = DUAL && p.proj_vec && p.proj_dtype == TESM_BF16;
+    const uint32_t sp_warp = smem_u32(sP) + (uint32_t)(warp - 2) * (DCH * 2 * 32 * 64);
+    auto sp_addr = [&](int cc, int arr, int j) -> uint32_t {
+      return sp_warp + (uint32_t)(((cc * 2 + arr) * 32 + lane) * 64 + ((j ^ ((lane >> 1) & 3)) * 16));
+    };
+    auto stage_proj = [&](int smt, int snt, int cc) {
+      const int prow_i = smt * BM + q * 32 + lane;
+      const int n0 = snt * BN + (half * DCH + cc) * 32;
+      if (prow_i < p.M && n0 + 32 <= p.N) {
+        const __nv_bfloat16 *prow = reinterpret_cast<const __nv_bfloat16 *>(p.proj) + (int64_t)prow_i * p.ldp;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          cp_async16(sp_addr(cc, 0, j), prow + p.c_local + n0 + 8 * j);
+          cp_async16(sp_addr(cc, 1, j), prow + p.c_gate + n0 + 8 * j);
+        }
+      }
+    };
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++tile_i) {
       int mt, nt;
       tile_coords(p, u / p.splits, mt, nt);
       const uint32_t buf = tile_i & 1, use = tile_i >> 1;
+      if (dual_pre && tile_i == 0) {
+#pragma unroll
+        for (int cc = 0; cc < DCH; ++cc) stage_proj(mt, nt, cc);
+        cp_async_commit();
+      }
       if (!mbar_wait(&tfull[buf], use & 1)) break;
       fence_after();
       const int sub = MT == 2 ? half : 0;  // skinny tiles: each warp half owns one M sub-tile
@@ -301,26 +351,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float s1 = xs * wd0, s2 = xs2 * p.w_deq2[0];
         const int esz = p.proj_dtype == TESM_BF16 ? 2 : 4;
         const uint8_t *prow = reinterpret_cast<const uint8_t *>(p.proj) + (int64_t)(row_ok ? row : 0) * p.ldp * esz;
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          uint32_t r1[32], r2[32];
+#pragma unroll
+        for (int cc = 0; cc < DCH; ++cc) {
+          const int c = half * DCH + cc;
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + c * 32;
-          tmem_ld32(tbase, r1);
-          tmem_ld32(tbase + BN, r2);
           const int n0 = nt * BN + c * 32;
-          if (!row_ok || n0 >= p.N) continue;
-          float v[32];
           const bool full = p.proj_vec && n0 + 32 <= p.N;
+          float v[32];
+          uint32_t r[32];
+          tmem_ld32(tbase, r);  // acc1 (state_proj); TMEM loads are warp-collective: before any exit
+          uint4 pl[4], pg[4];
+          if (dual_pre) {
+            if (cc == 0) cp_async_wait_all();
+            if (row_ok && full) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float loc[16], gt[16];
-            load16(prow + (int64_t)p.c_local * esz, p.proj_dtype, n0 + 16 * h, p.N, full, loc);
-            load16(prow + (int64_t)p.c_gate * esz, p.proj_dtype, n0 + 16 * h, p.N, full, gt);
+              for (int j = 0; j < 4; ++j) {
+                pl[j] = lds128(sp_addr(cc, 0, j));
+                pg[j] = lds128(sp_addr(cc, 1, j));
+              }
+            }
+            // the next tile's chunk cc goes into the slots just read
+            const int un = u + gridDim.x;
+            if (un < total) {
+              int mtn, ntn;
+              tile_coords(p, un / p.splits, mtn, ntn);
+              stage_proj(mtn, ntn, cc);
+            }
+            if (cc == DCH - 1) cp_async_commit();
+          }
+          if (dual_pre && full) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int jj = 16 * h + j;
-              const float sig = 1.f / (1.f + expf(-gt[j]));
-              v[jj] = loc[j] + sig * ((float)(int32_t)r1[jj] * s1) + (float)(int32_t)r2[jj] * s2;
+            for (int j = 0; j < 4; ++j) {
+              const __nv_bfloat162 *hl = reinterpret_cast<const __nv_bfloat162 *>(&pl[j]);
+              const __nv_bfloat162 *hg = reinterpret_cast<const __nv_bfloat162 *>(&pg[j]);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 fl = __bfloat1622float2(hl[e]), fg = __bfloat1622float2(hg[e]);
+                const int jj = 8 * j + 2 * e;
+                v[jj] = fl.x + epi_sigmoid(fg.x) * (acc_to_f(r[jj]) * s1);
+                v[jj + 1] = fl.y + epi_sigmoid(fg.y) * (acc_to_f(r[jj + 1]) * s1);
+              }
+            }
+            tmem_ld32(tbase + BN, r);  // acc2 (ent_proj)
+            if (!row_ok || n0 >= p.N) continue;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += acc_to_f(r[j]) * s2;
+          } else {
+            uint32_t r2[32];
+            tmem_ld32(tbase + BN, r2);
+            if (!row_ok || n0 >= p.N) continue;
+            const uint32_t(&r1)[32] = r;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float loc[16], gt[16];
+              load16(prow + (int64_t)p.c_local * esz, p.proj_dtype, n0 + 16 * h, p.N, full, loc);
+              load16(prow + (int64_t)p.c_gate * esz, p.proj_dtype, n0 + 16 * h, p.N, full, gt);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int jj = 16 * h + j;
+                v[jj] = loc[j] + epi_sigmoid(gt[j]) * (acc_to_f(r1[jj]) * s1) + acc_to_f(r2[jj]) * s2;
+              }
             }
           }
           const bool vs = p.vec_store && n0 + 32 <= p.N;
@@ -503,7 +593,8 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   if (rc) return rc;
   rc = make_map(&mb, B, p.K, p.N, ldb, BN);
   if (rc) return rc;
-  const size_t smem = 1024 + (size_t)STAGES * (MT * BM * BK + BN * BK) + 256;
+  const size_t smem = 1024 + (size_t)STAGES * (MT * BM * BK + BN * BK) + 256 +
+                      (DUAL ? (size_t)EPI_WARPS * (BN / 64) * 2 * 32 * 64 : 0);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_gemm_i8<BN, DUAL, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -577,6 +668,7 @@ extern "C" int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, 
                                          int out_dtype, int64_t ldo, tesm_stream_t stream) {
   TESM_REQUIRE(codes && inv1 && inv2 && tern && deq1 && deq2 && proj && out, "gemm_i8_combine: null pointer");
   TESM_REQUIRE(M >= 0 && N > 0 && Kh > 0 && Kh % 128 == 0 && M < (1ll << 31), "gemm_i8_combine: need Kh % 128 == 0");
+  TESM_REQUIRE(Kh <= 16384, "gemm_i8_combine: d_state above 16384");
   if (M == 0) return TESM_OK;
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_combine: out dtype");
   if (proj_dtype != TESM_F32 && proj_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_combine: proj dtype");

@@ -40,7 +40,6 @@ __device__ __forceinline__ float step(float a, float h, float u) {
   return MIMO ? __fadd_rn(__fmul_rn(a, h), u) : fmaf(a, h, u);
 }
 
-__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.f + __expf(-x)); }
 
 // Stage the chunk's inputs in shared memory, transformed once: plane 0 = a = sigmoid(decay +
 // decay_bias); SISO plane 1 = u = sigmoid(write) * tanh(value); MIMO planes 1, 2 = sigmoid(write),
