@@ -55,6 +55,7 @@ struct Params {
   int64_t ldp;
   int c_local, c_gate;
   int proj_vec;
+  int dual_tma;  // bf16 proj and output, 16-byte aligned: local/gate via TMA loads, output via TMA store
   // split-K (small M): work unit = (tile, split); int32 partials are added atomically into ws
   // (exact, so the result does not depend on the order), a finalize kernel scales them
   int splits;
@@ -144,11 +145,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
+// TMA store of a shared-memory tile (bulk-group completion), and the group waits.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to a following TMA (async proxy) read
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
 __device__ __forceinline__ uint4 lds128(uint32_t saddr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
@@ -177,7 +189,9 @@ __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int
 
 template <int BN, bool DUAL, int MT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmG,
+              const __grid_constant__ CUtensorMap tmO, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // MT = 2 ("skinny", decode batches): one CTA covers 256 token rows as two M=128 MMAs sharing
@@ -189,9 +203,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
   uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = bars + 2 * STAGES + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
-  // DUAL: per epilogue warp, its rows' bf16 local / gate operands of one tile, staged by cp.async
-  // ([chunk][array][lane][64 B], 16-byte units swizzled by lane so a warp's reads hit all banks)
-  uint8_t *sP = sB + STAGES * B_BYTES + 256;
+  // DUAL with bf16 proj and output (p.dual_tma): per epilogue warp and 32-column chunk, the
+  // 32x32 bf16 local and gate tiles (TMA loads, one mbarrier each) and the output tile (TMA
+  // store), all with the 64-byte swizzle so lane-per-row accesses hit distinct banks.
+  constexpr int DCH = DUAL ? BN / 64 : 1;  // 32-column chunks per epilogue warp
+  uint64_t *pbar = bars + 2 * STAGES + 6;  // EPI_WARPS * DCH barriers
+  uint8_t *sP = sB + STAGES * B_BYTES + 1024;  // 1024-aligned (swizzled TMA boxes)
+  uint8_t *sO = sP + EPI_WARPS * DCH * 2 * 2048;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : MT * BN;  // TMEM columns of one tile's accumulator(s)
@@ -206,6 +224,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], EPI_WARPS);
     }
+    if (DUAL)
+      for (int i = 0; i < EPI_WARPS * DCH; ++i) mbar_init(&pbar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
@@ -284,35 +304,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp stores
     uint32_t tile_i = 0;
-    // DUAL with bf16 proj: the local / gate operands do not depend on the accumulators, so they
-    // are copied into shared memory asynchronously one tile ahead: chunk cc of the next tile is
-    // requested as soon as chunk cc of this one has been read.
-    constexpr int DCH = DUAL ? BN / 64 : 1;
-    const bool dual_pre = DUAL && p.proj_vec && p.proj_dtype == TESM_BF16;
-    const uint32_t sp_warp = smem_u32(sP) + (uint32_t)(warp - 2) * (DCH * 2 * 32 * 64);
-    auto sp_addr = [&](int cc, int arr, int j) -> uint32_t {
-      return sp_warp + (uint32_t)(((cc * 2 + arr) * 32 + lane) * 64 + ((j ^ ((lane >> 1) & 3)) * 16));
-    };
-    auto stage_proj = [&](int smt, int snt, int cc) {
-      const int prow_i = smt * BM + q * 32 + lane;
-      const int n0 = snt * BN + (half * DCH + cc) * 32;
-      if (prow_i < p.M && n0 + 32 <= p.N) {
-        const __nv_bfloat16 *prow = reinterpret_cast<const __nv_bfloat16 *>(p.proj) + (int64_t)prow_i * p.ldp;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          cp_async16(sp_addr(cc, 0, j), prow + p.c_local + n0 + 8 * j);
-          cp_async16(sp_addr(cc, 1, j), prow + p.c_gate + n0 + 8 * j);
-        }
+    // DUAL with TMA: the local / gate operands do not depend on the accumulators, so each
+    // chunk's tiles are requested one tile ahead, as soon as this tile's chunk has been read.
+    const int ew = warp - 2;
+    const bool dual_tma = DUAL && p.dual_tma;
+    // A chunk's tiles are loaded (and its barrier completes a phase) only when the chunk has
+    // columns below N and rows below M; the consumer tests the same condition and keeps its own
+    // per-chunk phase bit, so skipped chunks never desynchronise the parity.
+    auto issue_in = [&](int smt, int snt, int cc) {
+      const int x = snt * BN + (half * DCH + cc) * 32;
+      if (lane == 0 && x < p.N && smt * BM + q * 32 < p.M) {
+        uint64_t *bar = &pbar[ew * DCH + cc];
+        mbar_expect_tx(bar, 2 * 2048);
+        uint8_t *dst = sP + (ew * DCH + cc) * 2 * 2048;
+        tma_load_2d(dst, &tmL, bar, x, smt * BM + q * 32);
+        tma_load_2d(dst + 2048, &tmG, bar, x, smt * BM + q * 32);
       }
     };
+    // byte offset of 16-byte unit j of row r in a 32 x 64 B tile with the 64-byte swizzle
+    auto sw64 = [](int r, int j) -> uint32_t { return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); };
+    bool epi_ok = true;
+    uint32_t in_phase = 0;  // bit cc: parity of chunk cc's next barrier phase
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++tile_i) {
       int mt, nt;
       tile_coords(p, u / p.splits, mt, nt);
       const uint32_t buf = tile_i & 1, use = tile_i >> 1;
-      if (dual_pre && tile_i == 0) {
+      if (dual_tma && tile_i == 0) {
 #pragma unroll
-        for (int cc = 0; cc < DCH; ++cc) stage_proj(mt, nt, cc);
-        cp_async_commit();
+        for (int cc = 0; cc < DCH; ++cc) issue_in(mt, nt, cc);
       }
       if (!mbar_wait(&tfull[buf], use & 1)) break;
       fence_after();
@@ -346,57 +365,88 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const float xs = row_ok ? p.inv_scale[row] : 0.f;
       const float wd0 = p.w_deq[0];
-      if (DUAL) {
-        const float xs2 = row_ok ? p.inv_scale2[row] : 0.f;
-        const float s1 = xs * wd0, s2 = xs2 * p.w_deq2[0];
-        const int esz = p.proj_dtype == TESM_BF16 ? 2 : 4;
-        const uint8_t *prow = reinterpret_cast<const uint8_t *>(p.proj) + (int64_t)(row_ok ? row : 0) * p.ldp * esz;
+      if (DUAL && dual_tma) {
+        const float s1 = xs * wd0, s2 = (row_ok ? p.inv_scale2[row] : 0.f) * p.w_deq2[0];
+        int mtn = 0, ntn = 0;
+        const int un = u + gridDim.x;
+        if (un < total) tile_coords(p, un / p.splits, mtn, ntn);
 #pragma unroll
         for (int cc = 0; cc < DCH; ++cc) {
           const int c = half * DCH + cc;
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + c * 32;
           const int n0 = nt * BN + c * 32;
+          uint32_t r[32];
+          float v[32];
+          tmem_ld32(tbase, r);  // acc1 (state_proj)
+          uint4 pl[4], pg[4];
+          const bool have = n0 < p.N && mt * BM + q * 32 < p.M;
+          if (have) {
+            if (!mbar_wait(&pbar[ew * DCH + cc], (in_phase >> cc) & 1)) epi_ok = false;
+            in_phase ^= 1u << cc;
+          }
+          const uint32_t sin = smem_u32(sP + (ew * DCH + cc) * 2 * 2048);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            pl[j] = lds128(sin + sw64(lane, j));
+            pg[j] = lds128(sin + 2048 + sw64(lane, j));
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 *hl = reinterpret_cast<const __nv_bfloat162 *>(&pl[j]);
+            const __nv_bfloat162 *hg = reinterpret_cast<const __nv_bfloat162 *>(&pg[j]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 fl = __bfloat1622float2(hl[e]), fg = __bfloat1622float2(hg[e]);
+              const int jj = 8 * j + 2 * e;
+              v[jj] = fl.x + epi_sigmoid(fg.x) * (acc_to_f(r[jj]) * s1);
+              v[jj + 1] = fl.y + epi_sigmoid(fg.y) * (acc_to_f(r[jj + 1]) * s1);
+            }
+          }
+          // every lane has consumed its slot values (register dependencies above): refill the
+          // chunk's slots with the next tile's tiles
+          __syncwarp();
+          if (un < total && epi_ok) issue_in(mtn, ntn, cc);
+          tmem_ld32(tbase + BN, r);  // acc2 (ent_proj)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += acc_to_f(r[j]) * s2;
+          // the output slot of this chunk was last used DCH store groups ago
+          if (lane == 0) bulk_wait_read<DCH - 1>();
+          __syncwarp();
+          uint8_t *so = sO + (ew * DCH + cc) * 2048;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+            *reinterpret_cast<uint4 *>(so + sw64(lane, j)) = *reinterpret_cast<uint4 *>(h);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (have) tma_store_2d(&tmO, so, n0, mt * BM + q * 32);  // rows >= M, cols >= N are clipped
+            bulk_commit();
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        if (!epi_ok) break;
+        continue;
+      }
+      if (DUAL) {
+        const float xs2 = row_ok ? p.inv_scale2[row] : 0.f;
+        const float s1 = xs * wd0, s2 = xs2 * p.w_deq2[0];
+        const int esz = p.proj_dtype == TESM_BF16 ? 2 : 4;
+        const uint8_t *prow = reinterpret_cast<const uint8_t *>(p.proj) + (int64_t)(row_ok ? row : 0) * p.ldp * esz;
+#pragma unroll 1
+        for (int c = half * DCH; c < (half + 1) * DCH; ++c) {
+          const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + c * 32;
+          const int n0 = nt * BN + c * 32;
           const bool full = p.proj_vec && n0 + 32 <= p.N;
           float v[32];
           uint32_t r[32];
-          tmem_ld32(tbase, r);  // acc1 (state_proj); TMEM loads are warp-collective: before any exit
-          uint4 pl[4], pg[4];
-          if (dual_pre) {
-            if (cc == 0) cp_async_wait_all();
-            if (row_ok && full) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                pl[j] = lds128(sp_addr(cc, 0, j));
-                pg[j] = lds128(sp_addr(cc, 1, j));
-              }
-            }
-            // the next tile's chunk cc goes into the slots just read
-            const int un = u + gridDim.x;
-            if (un < total) {
-              int mtn, ntn;
-              tile_coords(p, un / p.splits, mtn, ntn);
-              stage_proj(mtn, ntn, cc);
-            }
-            if (cc == DCH - 1) cp_async_commit();
-          }
-          if (dual_pre && full) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const __nv_bfloat162 *hl = reinterpret_cast<const __nv_bfloat162 *>(&pl[j]);
-              const __nv_bfloat162 *hg = reinterpret_cast<const __nv_bfloat162 *>(&pg[j]);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 fl = __bfloat1622float2(hl[e]), fg = __bfloat1622float2(hg[e]);
-                const int jj = 8 * j + 2 * e;
-                v[jj] = fl.x + epi_sigmoid(fg.x) * (acc_to_f(r[jj]) * s1);
-                v[jj + 1] = fl.y + epi_sigmoid(fg.y) * (acc_to_f(r[jj + 1]) * s1);
-              }
-            }
-            tmem_ld32(tbase + BN, r);  // acc2 (ent_proj)
-            if (!row_ok || n0 >= p.N) continue;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += acc_to_f(r[j]) * s2;
-          } else {
+          tmem_ld32(tbase, r);
+          {
             uint32_t r2[32];
             tmem_ld32(tbase + BN, r2);
             if (!row_ok || n0 >= p.N) continue;
@@ -515,6 +565,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
+    // TMA stores still reading this warp's output slots must finish before the CTA exits
+    if (dual_tma && lane == 0) bulk_wait_all();
   }
 
   fence_before();
@@ -586,15 +638,38 @@ static int make_map(CUtensorMap *map, const void *ptr, int64_t inner, int64_t ou
   return TESM_OK;
 }
 
+// bf16 matrix (inner columns, outer rows, row pitch ld elements) in 32 x 32 boxes with the
+// 64-byte swizzle: the combine epilogue's local / gate / output tiles.
+static int make_map_bf16_32(CUtensorMap *map, const void *ptr, int64_t inner, int64_t outer, int64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return fail(TESM_ELAUNCH, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TESM_EINVAL, "cuTensorMapEncodeTiled (bf16) failed (" + std::to_string((int)r) + ")");
+  return TESM_OK;
+}
+
 template <int BN, bool DUAL = false, int MT = 1>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, ml, mg, mo;
   int rc = make_map(&ma, A, p.K, p.M, lda, BM * MT);
   if (rc) return rc;
   rc = make_map(&mb, B, p.K, p.N, ldb, BN);
   if (rc) return rc;
-  const size_t smem = 1024 + (size_t)STAGES * (MT * BM * BK + BN * BK) + 256 +
-                      (DUAL ? (size_t)EPI_WARPS * (BN / 64) * 2 * 32 * 64 : 0);
+  ml = mg = mo = ma;  // unused unless dual_tma
+  if (DUAL && p.dual_tma) {
+    const __nv_bfloat16 *pr = reinterpret_cast<const __nv_bfloat16 *>(p.proj);
+    if ((rc = make_map_bf16_32(&ml, pr + p.c_local, p.N, p.M, p.ldp))) return rc;
+    if ((rc = make_map_bf16_32(&mg, pr + p.c_gate, p.N, p.M, p.ldp))) return rc;
+    if ((rc = make_map_bf16_32(&mo, p.out, p.N, p.M, p.ldo))) return rc;
+  }
+  const size_t smem = 1024 + (size_t)STAGES * (MT * BM * BK + BN * BK) +
+                      (DUAL ? 1024 + (size_t)EPI_WARPS * (BN / 64) * 3 * 2048 : 256);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_gemm_i8<BN, DUAL, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -615,7 +690,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   }
   const int total = tiles * p.splits;
   const int grid = total < sm_count() ? total : sm_count();
-  k_gemm_i8<BN, DUAL, MT><<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
+  k_gemm_i8<BN, DUAL, MT><<<grid, NUM_THREADS, smem, st>>>(ma, mb, ml, mg, mo, p);
   int rc2 = check_launch("gemm_i8");
   if (rc2 || p.splits == 1) return rc2;
   const int64_t n = (int64_t)p.M * (p.swiglu ? p.N / 2 : p.N);
@@ -696,6 +771,7 @@ extern "C" int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, 
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   p.proj_vec = ((uintptr_t)proj % 16 == 0) && ((ldp * psz) % 16 == 0) && ((c_local * psz) % 16 == 0) &&
                ((c_gate * psz) % 16 == 0);
+  p.dual_tma = p.proj_vec && p.vec_store && proj_dtype == TESM_BF16 && out_dtype == TESM_BF16;
   return tc::launch<128, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
 }
 

@@ -183,3 +183,36 @@ def test_ffn_swiglu_interleaved(lib, M, Dm):
         y = ffn(x.cuda()).cpu().numpy()
     assert tie.mean() < 0.2
     assert max_rel(y[~tie], ref[~tie]) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("MNK", [(4133, 4096, 256), (200, 200, 128), (50, 96, 256), (1000, 1000, 384)])
+def test_gemm_combine_epilogue(ops, dtype, MNK):
+    """Dual-accumulator GEMM with the combine epilogue (tesm.py:1256-1260):
+    out = local + sigmoid(gate) * acc1 * inv1 * deq1 + acc2 * inv2 * deq2, against the exact
+    int accumulators in fp64.  bf16 runs the TMA-staged epilogue (ragged M and N, row quarters
+    of the last tile past M), fp32 the register path."""
+    M, N, Kh = MNK
+    g = torch.Generator().manual_seed(M + N)
+    codes = torch.randint(-128, 128, (M, 2 * Kh), generator=g, dtype=torch.int8)
+    tern = torch.randint(-1, 2, (N, 2 * Kh), generator=g, dtype=torch.int8)
+    inv1 = torch.rand(M, generator=g) * 1e-2
+    inv2 = torch.rand(M, generator=g) * 1e-2
+    deq1, deq2 = torch.tensor([0.03]), torch.tensor([0.05])
+    c_local, c_gate = 8, 16 + N  # columns inside a wider proj row, 16-byte aligned offsets
+    ldp = c_gate + N + 24
+    proj = (torch.randn(M, ldp, generator=g) * 2).to(DT[dtype])
+    out = torch.full((M, N), float("nan"), dtype=DT[dtype], device="cuda")
+    ops.gemm_combine(codes.cuda(), Kh, inv1.cuda(), inv2.cuda(), tern.cuda(), deq1.cuda(), deq2.cuda(), proj.cuda(),
+                     c_local, c_gate, M, N, out)
+    c64, t64 = codes.double(), tern.double()
+    a1 = c64[:, :Kh] @ t64[:, :Kh].T
+    a2 = c64[:, Kh:] @ t64[:, Kh:].T
+    pf = proj.double()
+    loc, gate = pf[:, c_local:c_local + N], pf[:, c_gate:c_gate + N]
+    ref = loc + torch.sigmoid(gate) * a1 * (inv1.double()[:, None] * 0.03) + a2 * (inv2.double()[:, None] * 0.05)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    tol = 1e-5 if dtype == "float32" else 8e-3
+    err = ((got - ref).abs() / (ref.abs() + 1.0)).max().item()
+    assert err <= tol, err
