@@ -106,15 +106,45 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// ---- CTA pairs (cta_group::2): one M=256 MMA over two SMs, each holding half of A and B ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// address of the same shared-memory variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;\n" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on the pair leader's
+// barrier (bar_cluster: a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];\n" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(bar_cluster) : "memory");
+}
+
 // K-major operand tile with 128-byte swizzle: 8-row atoms 1024 B apart (SBO), version 1.
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void *p) {
   const uint64_t addr = smem_u32(p);
   return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// kind::i8 instruction descriptor: D s32, A/B signed int8, both K-major, M=128, N=BN.
-__host__ __device__ constexpr uint32_t idesc_i8(int n) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// kind::i8 instruction descriptor: D s32, A/B signed int8, both K-major, M=m (128, or 256 for
+// a CTA pair), N=n.
+__host__ __device__ constexpr uint32_t idesc_i8(int n, int m = BM) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -123,6 +153,23 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Completion of the pair's MMAs signalled on the barrier at this offset in both CTAs.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -187,7 +234,7 @@ __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int
   mt = first_m + (r - nt * gm);
 }
 
-template <int BN, bool DUAL, int MT>
+template <int BN, bool DUAL, int MT, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmG,
@@ -196,33 +243,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // MT = 2 ("skinny", decode batches): one CTA covers 256 token rows as two M=128 MMAs sharing
   // each weight tile, so a narrow N tile still reads every weight byte once
+  // PAIR: a cluster of two CTAs computes a 256-row tile with M=256 MMAs issued by the even CTA
+  // (the leader); each CTA stages its own 128 rows of A and half (BN/2 rows) of the weight tile,
+  // and holds its 128 accumulator rows in its own TMEM.
+  static_assert(!PAIR || (MT == 1 && !DUAL), "CTA pairs: plain tiles only");
+  constexpr int NST = PAIR ? 6 : STAGES;
   constexpr int A_BYTES = MT * BM * BK;
-  constexpr int B_BYTES = BN * BK;
+  constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;
   uint8_t *sA = smem;
-  uint8_t *sB = smem + STAGES * A_BYTES;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
-  uint64_t *full = bars, *empty = bars + STAGES, *tfull = bars + 2 * STAGES, *tempty = bars + 2 * STAGES + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  uint8_t *sB = smem + NST * A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + NST * B_BYTES);
+  uint64_t *full = bars, *empty = bars + NST, *tfull = bars + 2 * NST, *tempty = bars + 2 * NST + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NST + 4);
   // DUAL with bf16 proj and output (p.dual_tma): per epilogue warp and 32-column chunk, the
   // 32x32 bf16 local and gate tiles (TMA loads, one mbarrier each) and the output tile (TMA
   // store), all with the 64-byte swizzle so lane-per-row accesses hit distinct banks.
   constexpr int DCH = DUAL ? BN / 64 : 1;  // 32-column chunks per epilogue warp
-  uint64_t *pbar = bars + 2 * STAGES + 6;  // EPI_WARPS * DCH barriers
-  uint8_t *sP = sB + STAGES * B_BYTES + 1024;  // 1024-aligned (swizzled TMA boxes)
+  uint64_t *pbar = bars + 2 * NST + 6;  // EPI_WARPS * DCH barriers
+  uint8_t *sP = sB + NST * B_BYTES + 1024;  // 1024-aligned (swizzled TMA boxes)
   uint8_t *sO = sP + EPI_WARPS * DCH * 2 * 2048;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = PAIR ? cluster_rank() : 0;  // 0: the pair leader
+  // persistent loop over work units: per CTA, or per CTA pair
+  const int ustart = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : MT * BN;  // TMEM columns of one tile's accumulator(s)
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < NST; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], EPI_WARPS);
+      mbar_init(&tempty[i], PAIR ? 2 * EPI_WARPS : EPI_WARPS);  // pair: both CTAs' epilogues
     }
     if (DUAL)
       for (int i = 0; i < EPI_WARPS * DCH; ++i) mbar_init(&pbar[i], 1);
@@ -231,12 +287,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tmB) : "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+    if (PAIR) {  // both CTAs of the pair allocate together
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+    }
   }
   fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // the peer's barriers are initialised before any remote arrive
+  else
+    __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -247,29 +314,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      for (int u = ustart; u < total && ok; u += ustride) {
         int mt, nt;
         const int t = u / p.splits, sp = u - t * p.splits;
         tile_coords(p, t, mt, nt);
         const int kb_lo = sp * nk_all / p.splits, kb_hi = (sp + 1) * nk_all / p.splits;
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
-          const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
+          const uint32_t stage = it % NST, phase = (it / NST) & 1;
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM * MT);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+          if (PAIR) {
+            // the leader's barrier counts both CTAs' bytes; each CTA loads its own halves
+            if (crank == 0) mbar_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(sA + stage * A_BYTES, &tmA, fb, kb * BK, (mt * 2 + (int)crank) * BM);
+            tma_load_2d_pair(sB + stage * B_BYTES, &tmB, fb, kb * BK, nt * BN + (int)crank * (BN / 2));
+          } else {
+            mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM * MT);
+            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(BN);
+    if (lane == 0 && crank == 0) {  // pair: the leader issues the MMAs for both CTAs
+      constexpr uint32_t idesc = idesc_i8(BN, PAIR ? 2 * BM : BM);
       uint32_t it = 0, tile_i = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++tile_i) {
+      for (int u = ustart; u < total && ok; u += ustride, ++tile_i) {
         const uint32_t buf = tile_i & 1, use = tile_i >> 1;
         const int sp = u % p.splits;
         const int kb_lo = sp * nk_all / p.splits, kb_hi = (sp + 1) * nk_all / p.splits;
@@ -279,7 +354,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const bool second = DUAL && kb >= p.ksplit;
           const uint32_t d_tmem = tmem_base + buf * ACC_COLS + (second ? BN : 0);
           const int kb0 = second ? kb - p.ksplit : kb - kb_lo;
-          const uint32_t stage = it % STAGES, phase = (it / STAGES) & 1;
+          const uint32_t stage = it % NST, phase = (it / NST) & 1;
           if (!mbar_wait(&full[stage], phase)) {
             ok = false;
             break;
@@ -290,13 +365,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             // advance 32 bytes along K inside the swizzle atom: +2 in 16-byte units
+            if (PAIR) {
+              mma_i8_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
+            } else {
 #pragma unroll
-            for (int s = 0; s < MT; ++s)  // second M sub-tile: +16 KB = +1024 in 16-byte units
-              mma_i8(d_tmem + s * BN, adesc + 2 * kk + s * (BM * BK / 16), bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
+              for (int s = 0; s < MT; ++s)  // second M sub-tile: +16 KB = +1024 in 16-byte units
+                mma_i8(d_tmem + s * BN, adesc + 2 * kk + s * (BM * BK / 16), bdesc + 2 * kk, idesc,
+                       (kb0 | kk) != 0);
+            }
           }
-          mma_commit(&empty[stage]);
+          if (PAIR)
+            mma_commit_pair(&empty[stage]);
+          else
+            mma_commit(&empty[stage]);
         }
-        if (ok) mma_commit(&tfull[buf]);
+        if (ok) {
+          if (PAIR)
+            mma_commit_pair(&tfull[buf]);
+          else
+            mma_commit(&tfull[buf]);
+        }
       }
     }
   } else {
@@ -325,7 +413,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     auto sw64 = [](int r, int j) -> uint32_t { return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); };
     bool epi_ok = true;
     uint32_t in_phase = 0;  // bit cc: parity of chunk cc's next barrier phase
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++tile_i) {
+    // release of a TMEM buffer: to this CTA's barrier, or the pair leader's
+    auto release = [&](uint32_t b) {
+      if (lane != 0) return;
+      if (PAIR)
+        mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+      else
+        mbar_arrive(&tempty[b]);
+    };
+    for (int u = ustart; u < total; u += ustride, ++tile_i) {
       int mt, nt;
       tile_coords(p, u / p.splits, mt, nt);
       const uint32_t buf = tile_i & 1, use = tile_i >> 1;
@@ -336,7 +432,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull[buf], use & 1)) break;
       fence_after();
       const int sub = MT == 2 ? half : 0;  // skinny tiles: each warp half owns one M sub-tile
-      const int row = (mt * MT + sub) * BM + q * 32 + lane;
+      const int row = (PAIR ? mt * 2 + (int)crank : mt * MT + sub) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
       if (!DUAL && p.splits > 1) {
         const int c_lo = MT == 2 ? 0 : half * (BN / 64), c_hi = MT == 2 ? BN / 32 : (half + 1) * (BN / 64);
@@ -360,7 +456,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+        release(buf);
         continue;
       }
       const float xs = row_ok ? p.inv_scale[row] : 0.f;
@@ -368,7 +464,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (DUAL && dual_tma) {
         const float s1 = xs * wd0, s2 = (row_ok ? p.inv_scale2[row] : 0.f) * p.w_deq2[0];
         int mtn = 0, ntn = 0;
-        const int un = u + gridDim.x;
+        const int un = u + ustride;
         if (un < total) tile_coords(p, un / p.splits, mtn, ntn);
 #pragma unroll
         for (int cc = 0; cc < DCH; ++cc) {
@@ -429,7 +525,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+        release(buf);
         if (!epi_ok) break;
         continue;
       }
@@ -475,7 +571,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+        release(buf);
         continue;
       }
       if (BN == 256 && MT == 1 && p.swiglu) {
@@ -519,7 +615,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+        release(buf);
         continue;
       }
       const int c_lo = MT == 2 ? 0 : half * (BN / 64), c_hi = MT == 2 ? BN / 32 : (half + 1) * (BN / 64);
@@ -563,17 +659,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
+      release(buf);
     }
     // TMA stores still reading this warp's output slots must finish before the CTA exits
     if (dual_tma && lane == 0) bulk_wait_all();
   }
 
   fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // the leader's MMAs into this CTA's TMEM are complete
+  else
+    __syncthreads();
   if (warp == 1) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "r"(TMEM_COLS));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "r"(TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "r"(TMEM_COLS));
   }
 }
 
@@ -654,12 +756,12 @@ static int make_map_bf16_32(CUtensorMap *map, const void *ptr, int64_t inner, in
   return TESM_OK;
 }
 
-template <int BN, bool DUAL = false, int MT = 1>
+template <int BN, bool DUAL = false, int MT = 1, bool PAIR = false>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
   CUtensorMap ma, mb, ml, mg, mo;
   int rc = make_map(&ma, A, p.K, p.M, lda, BM * MT);
   if (rc) return rc;
-  rc = make_map(&mb, B, p.K, p.N, ldb, BN);
+  rc = make_map(&mb, B, p.K, p.N, ldb, PAIR ? BN / 2 : BN);
   if (rc) return rc;
   ml = mg = mo = ma;  // unused unless dual_tma
   if (DUAL && p.dual_tma) {
@@ -668,20 +770,23 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
     if ((rc = make_map_bf16_32(&mg, pr + p.c_gate, p.N, p.M, p.ldp))) return rc;
     if ((rc = make_map_bf16_32(&mo, p.out, p.N, p.M, p.ldo))) return rc;
   }
-  const size_t smem = 1024 + (size_t)STAGES * (MT * BM * BK + BN * BK) +
+  constexpr int NST = PAIR ? 6 : STAGES;
+  const size_t smem = 1024 + (size_t)NST * (MT * BM * BK + (PAIR ? BN / 2 : BN) * BK) +
                       (DUAL ? 1024 + (size_t)EPI_WARPS * (BN / 64) * 3 * 2048 : 256);
+  auto kern = k_gemm_i8<BN, DUAL, MT, PAIR>;
   static bool attr = false;
+  static int max_clusters = 0;
   if (!attr) {
-    cudaFuncSetAttribute(k_gemm_i8<BN, DUAL, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = true;
   }
-  p.num_m_tiles = (int)ceil_div(p.M, BM * MT);
+  p.num_m_tiles = (int)ceil_div(p.M, BM * MT * (PAIR ? 2 : 1));
   p.num_n_tiles = (int)ceil_div(p.N, BN);
   p.num_k_blocks = (int)ceil_div(p.K, BK);
-  p.group_m = 16;
+  p.group_m = PAIR ? 8 : 16;
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   p.splits = 1;
-  if (!DUAL && MT == 1 && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
+  if (!PAIR && !DUAL && MT == 1 && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
     int s = (int)ceil_div(sm_count(), tiles);
     if (s > 8) s = 8;
     if (s > p.num_k_blocks / 4) s = p.num_k_blocks / 4;
@@ -689,8 +794,35 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
     if (s >= 2) p.splits = s;
   }
   const int total = tiles * p.splits;
+  if (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (!max_clusters) {
+      cfg.gridDim = dim3(2 * (sm_count() / 2));
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      max_clusters = n;
+    }
+    const int clusters = total < max_clusters ? total : max_clusters;
+    cfg.gridDim = dim3(2 * clusters);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, ml, mg, mo, p);
+    if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemm_i8 (CTA pairs): ") + cudaGetErrorString(e));
+    return check_launch("gemm_i8 (CTA pairs)");
+  }
   const int grid = total < sm_count() ? total : sm_count();
-  k_gemm_i8<BN, DUAL, MT><<<grid, NUM_THREADS, smem, st>>>(ma, mb, ml, mg, mo, p);
+  kern<<<grid, NUM_THREADS, smem, st>>>(ma, mb, ml, mg, mo, p);
   int rc2 = check_launch("gemm_i8");
   if (rc2 || p.splits == 1) return rc2;
   const int64_t n = (int64_t)p.M * (p.swiglu ? p.N / 2 : p.N);
@@ -698,6 +830,18 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
                                                                 p.per_row, p.swiglu, p.out, p.out_dtype, p.ldo,
                                                                 p.acc_out, p.ld_acc);
   return check_launch("gemm_i8 split-K finalize");
+}
+
+// CTA pairs for large plain / SwiGLU GEMMs: enough 256 x 256 tiles to fill every SM pair.
+// TESM_GEMM_PAIR=0 / 1 forces the choice (tuning and tests).
+static bool use_pairs(int64_t M, int64_t N) {
+  static int force = -2;
+  if (force == -2) {
+    const char *e = getenv("TESM_GEMM_PAIR");
+    force = e ? atoi(e) : -1;
+  }
+  if (force >= 0) return force > 0;
+  return ceil_div(M, 256) * ceil_div(N, 256) >= 2 * (sm_count() / 2);
 }
 
 }  // namespace tc
@@ -733,6 +877,7 @@ extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, c
   }
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
+  if (tc::use_pairs(M, 2 * F)) return tc::launch<256, false, 1, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
 }
 
@@ -823,5 +968,6 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
     return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
   }
   if (N <= 128) return tc::launch<128>(codes, ld_codes, tern, ld_tern, p, st);
+  if (tc::use_pairs(M, N)) return tc::launch<256, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, st);
 }

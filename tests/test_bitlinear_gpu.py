@@ -107,8 +107,10 @@ def test_gemv_exact(ops, MNK):
 
 
 GEMM_SHAPES = [(65, 80, 96), (128, 256, 256), (300, 1000, 520), (1000, 11008, 4096), (256, 4096, 11008),
-               (77, 130, 37), (4096, 512, 2048), (128, 4096, 4096), (200, 300, 2048), (300, 1000, 2048)]
-# M <= 256 runs the skinny-tile kernel; (300, 1000, 2048) has fewer tiles than SMs -> split-K
+               (77, 130, 37), (4096, 512, 2048), (128, 4096, 4096), (200, 300, 2048), (300, 1000, 2048),
+               (4500, 8000, 1000)]
+# M <= 256 runs the skinny-tile kernel; (300, 1000, 2048) has fewer tiles than SMs -> split-K;
+# (4500, 8000, 1000) has enough 256 x 256 tiles for CTA pairs (ragged M, N and K)
 
 
 @pytest.mark.parametrize("MNK", GEMM_SHAPES, ids=lambda s: "x".join(map(str, s)))
@@ -156,7 +158,7 @@ def test_module_forward(lib):
         lay(randn(c["xshape"], 1).cuda())
 
 
-@pytest.mark.parametrize("M,Dm", [(20, 256), (300, 256), (200, 2048), (300, 2048)])
+@pytest.mark.parametrize("M,Dm", [(20, 256), (300, 256), (200, 2048), (300, 2048), (13000, 256)])
 def test_ffn_swiglu_interleaved(lib, M, Dm):
     """FeedForward with d_intermediate % 128 == 0: gate/up rows interleaved in 128-blocks; the
     tensor-core path applies silu(gate)*up in the GEMM epilogue, the GEMV path in a kernel."""
