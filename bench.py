@@ -218,8 +218,9 @@ def run_gpu(args, rank, world, local_rank):
         barrier()
         t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
 
-        # roofline of the dominant kernel (the tcgen05 int8 GEMM): events around each of its
-        # launches in one extra instrumented step, on the launching (current) stream
+        # roofline of the dominant kernel (the tcgen05 int8 GEMM: in_proj, out_proj, the SwiGLU
+        # gate/up GEMM and down_proj): events around each of its launches in one extra
+        # instrumented step, on the launching (current) stream
         rec = []
         orig = ops.gemm
 
@@ -231,13 +232,25 @@ def run_gpu(args, rank, world, local_rank):
             rec.append((a, b, 2.0 * M * pw.N * pw.K, M * pw.K + pw.N * pw.K + M * pw.N * 2))
             return r
 
-        ops.gemm = timed_gemm
+        orig_sw = ops.gemm_swiglu
+
+        def timed_swiglu(q, pw, out_dtype, out=None):
+            if q.M <= 256:  # decode-size batches route through ops.gemm (timed there)
+                return orig_sw(q, pw, out_dtype, out)
+            a, b = ev(), ev()
+            a.record()
+            r = orig_sw(q, pw, out_dtype, out)
+            b.record()
+            rec.append((a, b, 2.0 * q.M * pw.N * pw.K, q.M * pw.K + pw.N * pw.K + q.M * (pw.N // 2) * 2))
+            return r
+
+        ops.gemm, ops.gemm_swiglu = timed_gemm, timed_swiglu
         s0, s1 = ev(), ev()
         s0.record()
         model(ids, logits_to_keep=1)
         s1.record()
         torch.cuda.synchronize()
-        ops.gemm = orig
+        ops.gemm, ops.gemm_swiglu = orig, orig_sw
         g_ms = sum(a.elapsed_time(b) for a, b, _, _ in rec)
         g_ops = sum(o for _, _, o, _ in rec)
         g_bytes = sum(bb for _, _, _, bb in rec)
