@@ -158,6 +158,16 @@ int tesm_b200_siso_global_ent(const void *proj, int dtype, int64_t ldp, int64_t 
                               float thr, float es, float rope_base, void *out_tanh, void *out_chg, int out_dtype,
                               tesm_stream_t stream);
 
+/* Tensor-core version of tesm_b200_siso_global_ent (same reference code, same outputs): q.k in
+ * three fp16 hi/lo MMAs (fp32 accumulation), ternary weights and states as fp16 MMA operands.
+ * Needs ent_rank <= 64 (even) and d_state <= 256 (else status 5).  The caller provides a device
+ * workspace of tesm_b200_global_ent_tc_workspace() bytes, 1024-byte aligned. */
+int tesm_b200_global_ent_tc_workspace(int64_t B, int64_t L, int64_t D, int64_t R, int64_t *bytes);
+int tesm_b200_siso_global_ent_tc(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
+                                 int64_t D, int64_t R, const float *cross, const float *relb, const float *states,
+                                 float thr, float es, float rope_base, void *out_tanh, void *out_chg, int out_dtype,
+                                 void *workspace, int64_t ws_bytes, tesm_stream_t stream);
+
 /* MIMO global entanglement with the rank merge (replaces _compute_global_entanglement_mimo's torch
  * rung, tesm_mimo.py:590-687, as used per rank at :1007-1017): scores over all heads' flattened
  * q.k / sqrt(H*R) (RoPE per head) + relative bias, ternary, causal; per rank avg_r = (tern/norm) @

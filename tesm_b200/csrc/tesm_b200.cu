@@ -6,6 +6,7 @@
 #include "gemm_tc.cu"
 #include "scan.cu"
 #include "siso.cu"
+#include "global_tc.cu"
 #include "mimo.cu"
 #include "decode.cu"
 #include "model.cu"

@@ -249,7 +249,24 @@ def global_relbias(embed, scale, bias0, L):
     return out
 
 
-def siso_global_ent(proj, B, L, Dm, D, R, cross, relb, states, thr, es, base, out_tanh, out_chg):
+def global_ent_tc_ok(D, R):
+    return R <= 64 and R % 2 == 0 and D <= 256
+
+
+def siso_global_ent(proj, B, L, Dm, D, R, cross, relb, states, thr, es, base, out_tanh, out_chg, force=None):
+    """Causal global entanglement: tensor-core kernel when ent_rank <= 64 and d_state <= 256
+    (force="tc" / "simt" picks one for tests), else the fp32 SIMT kernel."""
+    path = force or ("tc" if global_ent_tc_ok(D, R) else "simt")
+    if path == "tc":
+        n = ctypes.c_int64(0)
+        _lib.call("tesm_b200_global_ent_tc_workspace", B, L, D, R, ctypes.addressof(n))
+        raw = torch.empty(n.value + 1024, device=proj.device, dtype=torch.uint8)
+        off = (-raw.data_ptr()) % 1024  # 1024-byte aligned start
+        _lib.call("tesm_b200_siso_global_ent_tc", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm,
+                  D, R, _ptr(cross), relb.data_ptr(), states.data_ptr(), float(thr), float(es), float(base),
+                  out_tanh.data_ptr(), out_chg.data_ptr(), dtype_code(out_tanh.dtype), raw.data_ptr() + off,
+                  n.value, _stream())
+        return
     _lib.call("tesm_b200_siso_global_ent", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, D, R,
               _ptr(cross), relb.data_ptr(), states.data_ptr(), float(thr), float(es), float(base),
               out_tanh.data_ptr(), out_chg.data_ptr(), dtype_code(out_tanh.dtype), _stream())
