@@ -503,11 +503,17 @@ def run_cfg3(args, peaks):
                 "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": byts})
     emb = torch.randn(64, device="cuda") * 0.02
     relb = ops.global_relbias(emb, 1.0, 0.0, L)
-    t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th, ch),
-                    reps=3, inner=1)
-    fl = B * (L * L / 2) * (2 * R + 2 * D)
-    res.append({"kernel": "k_siso_global_ent (SIMT fp32)", "ms": t * 1e3, "TFLOPS": fl / t / 1e12,
-                "note": "causal half counted; tensor-core version not built"})
+    fl = B * (L * L / 2) * (2 * R + 2 * D)  # algorithmic: causal half, q.k and t.v once each
+    t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th, ch,
+                                                  force="tc"), reps=5, inner=2)
+    res.append({"kernel": "k_global_ent_tc (tcgen05 kind::f16, incl. prep kernels)", "ms": t * 1e3,
+                "TFLOPS": fl / t / 1e12, "tensor_frac": fl / t / 1e12 / peaks["bf16_tflops"],
+                "note": "causal half counted once; the kernel issues 3 q.k (hi/lo) and 2 t.v (hi/lo) MMAs, "
+                        "2.2x the algorithmic flops at R=64, D=256"})
+    t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th, ch,
+                                                  force="simt"), reps=3, inner=1)
+    res.append({"kernel": "k_siso_global_ent (SIMT fp32, fallback for ent_rank > 64 / d_state > 256)",
+                "ms": t * 1e3, "TFLOPS": fl / t / 1e12})
     return res
 
 

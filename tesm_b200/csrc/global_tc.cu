@@ -14,12 +14,14 @@
 // fp32 torch path only for scores within ~1e-6 of the threshold.  t is exact in fp16 and t.v is
 // two MMAs (t.v_hi + t.v_lo), so avg carries ~2^-22 relative rounding, like fp32.
 //
-// Kernel: one CTA per (batch, 128-query tile), heaviest tiles first.  Warp 0 streams the k and
-// v^T tiles of 64 keys through a 2-stage TMA ring, warp 1 issues the MMAs, warps 2..9 (two per
-// TMEM lane quarter, one half of the 64 key columns each) turn scores into ternaries written
-// straight into the shared-memory A operand of the t.v^T MMA, then run the epilogue.  Scores are
-// double-buffered in TMEM (2 x 64 columns) next to the (128 x DS) fp32 accumulator, so the
-// score MMA of block j+1 overlaps the ternary pass of block j.  Every wait is bounded.
+// Kernel: one CTA per (batch, 128-query tile), heaviest tiles first, blocks of 64 keys.  Warp 0
+// streams k tiles (hi + lo) and warp 18 v^T tiles (hi + lo, 4x larger) through 2-stage TMA
+// rings; warp 1 issues the MMAs; warps 2..17 (four per TMEM lane quarter, 16 key columns each)
+// turn scores into ternaries written straight into the shared-memory A operand of the t.v^T MMA,
+// then run the epilogue.  Scores are triple-buffered in TMEM (3 x 64 columns next to the 128 x DS
+// fp32 accumulator) and ternary tiles double-buffered in shared memory; the MMA warp issues the
+// score MMAs of block j+2 before the t.v^T MMAs of block j, so the ternary warps never wait for
+// scores and the tensor pipe never waits for more than one ternary pass.  Every wait is bounded.
 
 #include "layer_common.cuh"
 
@@ -42,14 +44,29 @@ using tc::tmem_ld32;
 constexpr int QT = 128;  // query rows per CTA (TMEM lanes)
 constexpr int KB = 64;   // keys per block
 constexpr int RP = 64;   // padded ent_rank (one 128-byte swizzle atom of fp16)
-constexpr int NS = 2;    // k / v^T ring stages
-constexpr int NUM_THREADS = 64 + 256;
+constexpr int NSK = 2;   // k ring stages
+constexpr int NSV = 2;   // v^T ring stages
+constexpr int TW = 16;   // ternary / epilogue warps: 4 per TMEM lane quarter, 16 key columns each
+constexpr int NUM_THREADS = 32 * (3 + TW);  // + TMA k producer, MMA issuer, TMA v producer
+
+#ifdef TESM_GTC_TRACE
+// Development-only timeline of CTA 0 (heaviest tile): clock64 at 8 points for each key block.
+__device__ unsigned long long g_gtc_trace[8 * 256];
+#define GTC_MARK(pt, j) \
+  do {                  \
+    if (blockIdx.x == 0 && (j) < 256) g_gtc_trace[(pt) * 256 + (j)] = clock64(); \
+  } while (0)
+#else
+#define GTC_MARK(pt, j) \
+  do {                  \
+  } while (0)
+#endif
 
 struct Params {
   int B, L, D, DS, nqt, nkb_max;
   const float *relb;    // (2L - 1), index i - j + L - 1
   const float *states;  // (B*L, D) fp32
-  float thr, es, sqrt_r;
+  float thr, es, inv_sqrt_r;  // scores use q.k * fp32(1/sqrt(R)): within an ulp of q.k / sqrt(R)
   void *out_tanh, *out_chg;
   int out_dtype;
 };
@@ -72,6 +89,15 @@ __device__ __forceinline__ void commit(uint64_t *bar) {
                : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_global_ent_tc(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                     const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
@@ -83,14 +109,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int T_BYTES = QT * KB * 2;   // 16 KB
   const int V_BYTES = p.DS * KB * 2;     // <= 32 KB per hi / lo
   uint8_t *sQ = smem;                         // [hi | lo]
-  uint8_t *sK = sQ + 2 * Q_BYTES;             // NS x [hi | lo]
-  uint8_t *sT = sK + NS * 2 * K_BYTES;        // 2 x T
-  uint8_t *sV = sT + 2 * T_BYTES;             // NS x [hi | lo]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + NS * 2 * V_BYTES);
-  uint64_t *qfull = bars, *kvfull = bars + 1, *kvempty = kvfull + NS, *sfull = kvempty + NS, *tready = sfull + 2,
-           *tfree = tready + 2, *ofull = tfree + 2;
+  uint8_t *sK = sQ + 2 * Q_BYTES;             // NSK x [hi | lo]
+  uint8_t *sV = sK + NSK * 2 * K_BYTES;       // NSV x [hi | lo]
+  uint8_t *sT = sV + NSV * 2 * V_BYTES;       // 2 x (128 x 64) ternary tiles
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sT + 2 * T_BYTES);
+  uint64_t *qfull = bars, *kfull = bars + 1, *kempty = kfull + NSK, *vfull = kempty + NSK, *vempty = vfull + NSV,
+           *sfull = vempty + NSV, *tready = sfull + 3, *tfree = tready + 2, *ofull = tfree + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ofull + 1);
-  float *cnt_s = reinterpret_cast<float *>(tmem_slot + 4);  // [2][QT]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.nqt - 1 - (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
@@ -100,13 +125,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(qfull, 1);
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&kvfull[i], 1);
-      mbar_init(&kvempty[i], 1);
+    for (int i = 0; i < NSK; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&kempty[i], 1);
     }
+    for (int i = 0; i < NSV; ++i) {
+      mbar_init(&vfull[i], 1);
+      mbar_init(&vempty[i], 1);
+    }
+    for (int i = 0; i < 3; ++i) mbar_init(&sfull[i], 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sfull[i], 1);
-      mbar_init(&tready[i], 8);
+      mbar_init(&tready[i], TW);
       mbar_init(&tfree[i], 1);
     }
     mbar_init(ofull, 1);
@@ -120,22 +149,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tmem = *tmem_slot;  // S[0] cols 0..63, S[1] 64..127, O 128..128+DS
+  const uint32_t tmem = *tmem_slot;  // S[0..2] at cols 0, 64, 128; O at 192..192+DS
+  constexpr uint32_t O_COL = 3 * KB;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0) {  // q once, then the k ring
       mbar_expect_tx(qfull, 2 * Q_BYTES);
       tma_load_2d(sQ, &tmQh, qfull, 0, (int)(rowq + q0));
       tma_load_2d(sQ + Q_BYTES, &tmQl, qfull, 0, (int)(rowq + q0));
       for (int j = 0; j < nkb; ++j) {
-        const int s = j % NS;
-        if (!mbar_wait(&kvempty[s], ((j / NS) & 1) ^ 1)) break;
-        mbar_expect_tx(&kvfull[s], 2 * K_BYTES + 2 * V_BYTES);
+        const int s = j % NSK;
+        if (!mbar_wait(&kempty[s], ((j / NSK) & 1) ^ 1)) break;
+        mbar_expect_tx(&kfull[s], 2 * K_BYTES);
         uint8_t *k = sK + s * 2 * K_BYTES;
-        tma_load_2d(k, &tmKh, &kvfull[s], 0, (int)(rowq + j * KB));
-        tma_load_2d(k + K_BYTES, &tmKl, &kvfull[s], 0, (int)(rowq + j * KB));
-        tma_load_2d(sV + s * 2 * V_BYTES, &tmVh, &kvfull[s], j * KB, b * p.DS);
-        tma_load_2d(sV + s * 2 * V_BYTES + V_BYTES, &tmVl, &kvfull[s], j * KB, b * p.DS);
+        tma_load_2d(k, &tmKh, &kfull[s], 0, (int)(rowq + j * KB));
+        tma_load_2d(k + K_BYTES, &tmKl, &kfull[s], 0, (int)(rowq + j * KB));
+      }
+    }
+  } else if (warp == 2 + TW) {
+    if (lane == 0) {  // the v^T ring
+      for (int j = 0; j < nkb; ++j) {
+        const int s = j % NSV;
+        if (!mbar_wait(&vempty[s], ((j / NSV) & 1) ^ 1)) break;
+        mbar_expect_tx(&vfull[s], 2 * V_BYTES);
+        tma_load_2d(sV + s * 2 * V_BYTES, &tmVh, &vfull[s], j * KB, b * p.DS);
+        tma_load_2d(sV + s * 2 * V_BYTES + V_BYTES, &tmVl, &vfull[s], j * KB, b * p.DS);
       }
     }
   } else if (warp == 1) {
@@ -145,103 +183,136 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = mbar_wait(qfull, 0);
       fence_after();
       const uint64_t qh = smem_desc_sw128(sQ), ql = smem_desc_sw128(sQ + Q_BYTES);
-      for (int j = 0; ok && j <= nkb; ++j) {
-        if (j < nkb) {
-          const int s = j % NS;
-          if (!mbar_wait(&kvfull[s], (j / NS) & 1)) break;
-          fence_after();
-          const uint64_t kh = smem_desc_sw128(sK + s * 2 * K_BYTES), kl = smem_desc_sw128(sK + s * 2 * K_BYTES + K_BYTES);
-          const uint32_t dS = tmem + (j & 1) * KB;
+      // scores run two blocks ahead of t.v^T: order S(0), S(1), [S(j+2), O(j)] for j = 0, 1, ...
+      auto scores = [&](int jj) -> bool {
+        const int s = jj % NSK;
+        if (!mbar_wait(&kfull[s], (jj / NSK) & 1)) return false;
+        GTC_MARK(0, jj);
+        fence_after();
+        const uint64_t kh = smem_desc_sw128(sK + s * 2 * K_BYTES), kl = smem_desc_sw128(sK + s * 2 * K_BYTES + K_BYTES);
+        const uint32_t dS = tmem + (jj % 3) * KB;  // read by the ternary pass of block jj - 3, long done
 #pragma unroll
-          for (int kk = 0; kk < RP / 16; ++kk) {  // 16 fp16 = 32 bytes per K step: +2 in 16-byte units
-            mma_f16(dS, qh + 2 * kk, kh + 2 * kk, idS, kk > 0);
-            mma_f16(dS, qh + 2 * kk, kl + 2 * kk, idS, 1);
-            mma_f16(dS, ql + 2 * kk, kh + 2 * kk, idS, 1);
-          }
-          commit(&sfull[j & 1]);
+        for (int kk = 0; kk < RP / 16; ++kk) {  // 16 fp16 = 32 bytes per K step: +2 in 16-byte units
+          mma_f16(dS, qh + 2 * kk, kh + 2 * kk, idS, kk > 0);
+          mma_f16(dS, qh + 2 * kk, kl + 2 * kk, idS, 1);
+          mma_f16(dS, ql + 2 * kk, kh + 2 * kk, idS, 1);
         }
-        if (j >= 1) {
-          const int jp = j - 1, bp = jp & 1, sp = jp % NS;
-          if (!mbar_wait(&tready[bp], (jp >> 1) & 1)) break;
-          fence_after();
-          const uint64_t ta = smem_desc_sw128(sT + bp * T_BYTES), vh = smem_desc_sw128(sV + sp * 2 * V_BYTES),
-                         vl = smem_desc_sw128(sV + sp * 2 * V_BYTES + V_BYTES);
+        commit(&kempty[s]);
+        commit(&sfull[jj % 3]);
+        GTC_MARK(7, jj);
+        return true;
+      };
+      for (int jj = 0; ok && jj < 2 && jj < nkb; ++jj) ok = scores(jj);
+      for (int j = 0; ok && j < nkb; ++j) {
+        if (j + 2 < nkb && !scores(j + 2)) break;
+        const int sv = j % NSV, bt = j & 1;  // t.v^T of block j
+        if (!mbar_wait(&tready[bt], (j >> 1) & 1)) break;
+        GTC_MARK(1, j);
+        if (!mbar_wait(&vfull[sv], (j / NSV) & 1)) break;
+        GTC_MARK(2, j);
+        fence_after();
+        const uint64_t ta = smem_desc_sw128(sT + bt * T_BYTES), vh = smem_desc_sw128(sV + sv * 2 * V_BYTES),
+                       vl = smem_desc_sw128(sV + sv * 2 * V_BYTES + V_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < KB / 16; ++kk) {
-            mma_f16(tmem + 2 * KB, ta + 2 * kk, vh + 2 * kk, idO, (jp | kk) != 0);
-            mma_f16(tmem + 2 * KB, ta + 2 * kk, vl + 2 * kk, idO, 1);
-          }
-          commit(&kvempty[sp]);
-          commit(&tfree[bp]);
+        for (int kk = 0; kk < KB / 16; ++kk) {
+          mma_f16(tmem + O_COL, ta + 2 * kk, vh + 2 * kk, idO, (j | kk) != 0);
+          mma_f16(tmem + O_COL, ta + 2 * kk, vl + 2 * kk, idO, 1);
         }
+        commit(&vempty[sv]);
+        commit(&tfree[bt]);
       }
       commit(ofull);
     }
   } else {
-    // ternary warps: TMEM lane quarter q, key columns [half*32, half*32+32) of each block
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    // ternary warps 2 .. 2+TW-1: a warp reaches only TMEM lanes 32*(warp % 4) .. +31, so its lane
+    // quarter is q = warp % 4; part = which 16 of the block's 64 key columns it handles
+    const int tw = warp - 2, q = warp & 3, part = tw >> 2;
     const int rl = q * 32 + lane, i = q0 + rl;
     const bool row_ok = i < p.L;
     float cnt = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkb; ++j) {
-      const int buf = j & 1;
-      if (!mbar_wait(&sfull[buf], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      fence_after();
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * KB + half * 32, r);
-      if (j >= 2 && !mbar_wait(&tfree[buf], ((j - 2) >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      const int key0 = j * KB + half * 32;
-      uint32_t packed[16];
+    // relb[i - key + L - 1] for this lane's row and its 16 keys of a block: 16 consecutive
+    // entries (descending), loaded one block ahead; clamped indices are used only where
+    // key > i or i >= L, where the score is masked.
+    const int top = 2 * p.L - 2;
+    auto load_relb = [&](int jj, float (&rb)[16]) {
+      const int x0 = i - (jj * KB + part * 16) + p.L - 1;
 #pragma unroll
-      for (int c = 0; c < 32; c += 2) {
+      for (int c = 0; c < 16; ++c) rb[c] = __ldg(&p.relb[min(max(x0 - c, 0), top)]);
+    };
+    float rb[16], rbn[16];
+    load_relb(0, rbn);
+    const uint32_t sgn_one = 0x3f800000u;
+    for (int j = 0; j < nkb; ++j) {
+      const int sb = j % 3, bt = j & 1;
+      const int key0 = j * KB + part * 16;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) rb[c] = rbn[c];
+      if (j + 1 < nkb) load_relb(j + 1, rbn);
+      if (!mbar_wait(&sfull[sb], (j / 3) & 1)) {
+        ok = false;
+        break;
+      }
+      if (tw == 0 && lane == 0) GTC_MARK(3, j);
+      fence_after();
+      uint32_t r[16];
+      tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + sb * KB + part * 16, r);
+      // whole warp strictly below the diagonal and inside the sequence: no per-score mask
+      const bool dense = key0 + 15 <= q0 + q * 32 && q0 + q * 32 + 31 < p.L;
+      uint32_t packed[8];
+#pragma unroll
+      for (int c = 0; c < 16; c += 2) {
         float tv[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int key = key0 + c + e;
-          float t = 0.f;
-          if (row_ok && key <= i) {
-            const float sc = __fdiv_rn(__uint_as_float(r[c + e]), p.sqrt_r) + __ldg(&p.relb[i - key + p.L - 1]);
-            t = ternary_of(sc, p.thr);
-          }
-          cnt += fabsf(t);
+          const float sc = fmaf(__uint_as_float(r[c + e]), p.inv_sqrt_r, rb[c + e]);
+          // t = sign(sc) where |sc| > thr, else 0
+          float t = fabsf(sc) > p.thr ? __uint_as_float((__float_as_uint(sc) & 0x80000000u) | sgn_one) : 0.f;
+          if (!dense && !(row_ok && key0 + c + e <= i)) t = 0.f;
+          cnt = fmaf(t, t, cnt);
           tv[e] = t;
         }
         const __half2 h = __floats2half2_rn(tv[0], tv[1]);
         packed[c >> 1] = *reinterpret_cast<const uint32_t *>(&h);
       }
+      if (tw == 0 && lane == 0) GTC_MARK(4, j);
+      // the t.v^T MMA of block j - 2 has finished reading this buffer
+      if (j >= 2 && !mbar_wait(&tfree[bt], ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (tw == 0 && lane == 0) GTC_MARK(5, j);
       // row rl of the 128 x 64 fp16 tile (128-byte rows, 128-byte swizzle): 16-byte chunk u of
-      // this half sits at chunk index (half*4 + u) ^ (rl & 7)
-      uint8_t *trow = sT + buf * T_BYTES + rl * 128;
+      // this part sits at chunk index (part*2 + u) ^ (rl & 7)
+      uint8_t *trow = sT + bt * T_BYTES + rl * 128;
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        *reinterpret_cast<uint4 *>(trow + (((half * 4 + u) ^ (rl & 7)) << 4)) =
+      for (int u = 0; u < 2; ++u)
+        *reinterpret_cast<uint4 *>(trow + (((part * 2 + u) ^ (rl & 7)) << 4)) =
             make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tready[buf]);
+      if (lane == 0) mbar_arrive(&tready[bt]);
+      if (tw == 0 && lane == 0) GTC_MARK(6, j);
     }
-    cnt_s[half * QT + rl] = cnt;
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");  // the eight ternary warps
-    const float denom = fmaxf(cnt_s[rl] + cnt_s[QT + rl], 1.f);
-    if (ok && mbar_wait(ofull, 0)) {
+    // the row's count is split over its 4 column parts; the ternary tiles are free once the
+    // accumulator is complete, so the partial counts go there
+    const bool o_ok = ok && mbar_wait(ofull, 0);
+    float *cnt_s = reinterpret_cast<float *>(sT);  // [4][QT]
+    cnt_s[part * QT + rl] = cnt;
+    asm volatile("bar.sync 1, %0;\n" ::"n"(32 * TW) : "memory");  // the ternary warps
+    const float denom = fmaxf(cnt_s[rl] + cnt_s[QT + rl] + cnt_s[2 * QT + rl] + cnt_s[3 * QT + rl], 1.f);
+    if (o_ok) {
       fence_after();
-      const int nch = (p.DS + 31) / 32;  // TMEM columns past DS are allocated, their values unused
+      const int nch = (p.DS + 15) / 16;  // 16-column chunks; TMEM columns past DS are allocated, unused
       const int64_t row = rowq + i;
-      for (int ch = half; ch < nch; ch += 2) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + 2 * KB + ch * 32, r);
+      for (int ch = part; ch < nch; ch += 4) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + O_COL + ch * 16, r);
         if (!row_ok) continue;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int d = ch * 32 + c;
+        for (int c = 0; c < 16; ++c) {
+          const int d = ch * 16 + c;
           if (d >= p.D) continue;
           const float s = p.states[row * p.D + d];
           const float avg = __uint_as_float(r[c]) / denom;
@@ -337,6 +408,12 @@ static Layout layout(int64_t B, int64_t L, int64_t D) {
 
 using namespace tesm;
 
+#ifdef TESM_GTC_TRACE
+extern "C" int tesm_b200_gtc_trace_read(unsigned long long *host) {
+  return cudaMemcpyFromSymbol(host, gtc::g_gtc_trace, sizeof(gtc::g_gtc_trace)) == cudaSuccess ? 0 : 3;
+}
+#endif
+
 extern "C" int tesm_b200_global_ent_tc_workspace(int64_t B, int64_t L, int64_t D, int64_t R, int64_t *bytes) {
   TESM_REQUIRE(bytes && B > 0 && L > 0 && D > 0 && R > 0, "global_ent_tc_workspace: bad argument");
   if (R > gtc::RP || D > 256 || R % 2)
@@ -394,13 +471,12 @@ extern "C" int tesm_b200_siso_global_ent_tc(const void *proj, int dtype, int64_t
   p.states = states;
   p.thr = thr;
   p.es = es;
-  p.sqrt_r = (float)sqrt((double)R);
+  p.inv_sqrt_r = (float)(1.0 / sqrt((double)R));
   p.out_tanh = out_tanh;
   p.out_chg = out_chg;
   p.out_dtype = out_dtype;
-  const size_t smem = 1024 + 2 * (size_t)gtc::QT * gtc::RP * 2 + gtc::NS * 2 * (size_t)gtc::KB * gtc::RP * 2 +
-                      2 * (size_t)gtc::QT * gtc::KB * 2 + gtc::NS * 2 * (size_t)lay.DS * gtc::KB * 2 + 256 +
-                      2 * gtc::QT * sizeof(float);
+  const size_t smem = 1024 + 2 * (size_t)gtc::QT * gtc::RP * 2 + gtc::NSK * 2 * (size_t)gtc::KB * gtc::RP * 2 +
+                      2 * (size_t)gtc::QT * gtc::KB * 2 + gtc::NSV * 2 * (size_t)lay.DS * gtc::KB * 2 + 256;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(gtc::k_global_ent_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
