@@ -14,7 +14,9 @@
 // fp32 torch path only for scores within ~1e-6 of the threshold.  t is exact in fp16 and t.v is
 // two MMAs (t.v_hi + t.v_lo), so avg carries ~2^-22 relative rounding, like fp32.
 //
-// Kernel: one CTA per (batch, 128-query tile), heaviest tiles first, blocks of 64 keys.  Warp 0
+// Kernel: one CTA per (batch, 128-query tile), heaviest tiles first, blocks of 64 keys.
+// (Warp roles below; the score MMAs and the t.v^T MMAs are issued by two separate warps, warps 1
+// and 19, so that neither waits behind the other's issue.)  Warp 0
 // streams k tiles (hi + lo) and warp 18 v^T tiles (hi + lo, 4x larger) through 2-stage TMA
 // rings; warp 1 issues the MMAs; warps 2..17 (four per TMEM lane quarter, 16 key columns each)
 // turn scores into ternaries written straight into the shared-memory A operand of the t.v^T MMA,
@@ -44,10 +46,10 @@ using tc::tmem_ld32;
 constexpr int QT = 128;  // query rows per CTA (TMEM lanes)
 constexpr int KB = 64;   // keys per block
 constexpr int RP = 64;   // padded ent_rank (one 128-byte swizzle atom of fp16)
-constexpr int NSK = 2;   // k ring stages
+constexpr int NSK = 3;   // k ring stages
 constexpr int NSV = 2;   // v^T ring stages
 constexpr int TW = 16;   // ternary / epilogue warps: 4 per TMEM lane quarter, 16 key columns each
-constexpr int NUM_THREADS = 32 * (3 + TW);  // + TMA k producer, MMA issuer, TMA v producer
+constexpr int NUM_THREADS = 32 * (4 + TW);  // + TMA k / v producers, score-MMA and t.v-MMA issuers
 
 #ifdef TESM_GTC_TRACE
 // Development-only timeline of CTA 0 (heaviest tile): clock64 at 8 points for each key block.
@@ -98,24 +100,40 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+// A operand from TMEM: [a_tmem] holds the M x 16 fp16 slice (lane = row, 8 columns of packed pairs).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+// TMEM columns: accumulator O, score buffers S0/S1, q hi / lo (A of the score MMAs), ternary
+// tiles T0/T1 (A of the t.v^T MMAs); fp16 operands pack two values per 32-bit column.
+constexpr uint32_t COL_O = 0, COL_S = 256, COL_QH = 384, COL_QL = 416, COL_T = 448;
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_global_ent_tc(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
-                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
-                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl, Params p) {
+    k_global_ent_tc(const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
+                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
+                    const __half *__restrict__ qh_g, const __half *__restrict__ ql_g, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  constexpr int Q_BYTES = QT * RP * 2;   // 16 KB per hi / lo
   constexpr int K_BYTES = KB * RP * 2;   // 8 KB per hi / lo
-  constexpr int T_BYTES = QT * KB * 2;   // 16 KB
   const int V_BYTES = p.DS * KB * 2;     // <= 32 KB per hi / lo
-  uint8_t *sQ = smem;                         // [hi | lo]
-  uint8_t *sK = sQ + 2 * Q_BYTES;             // NSK x [hi | lo]
+  uint8_t *sK = smem;                         // NSK x [hi | lo]
   uint8_t *sV = sK + NSK * 2 * K_BYTES;       // NSV x [hi | lo]
-  uint8_t *sT = sV + NSV * 2 * V_BYTES;       // 2 x (128 x 64) ternary tiles
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sT + 2 * T_BYTES);
-  uint64_t *qfull = bars, *kfull = bars + 1, *kempty = kfull + NSK, *vfull = kempty + NSK, *vempty = vfull + NSV,
-           *sfull = vempty + NSV, *tready = sfull + 3, *tfree = tready + 2, *ofull = tfree + 2;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + NSV * 2 * V_BYTES);
+  uint64_t *qready = bars, *kfull = bars + 1, *kempty = kfull + NSK, *vfull = kempty + NSK, *vempty = vfull + NSV,
+           *sfull = vempty + NSV, *sfree = sfull + 2, *tready = sfree + 2, *tfree = tready + 2, *ofull = tfree + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ofull + 1);
+  float *cnt_s = reinterpret_cast<float *>(bars + 32);  // [4][QT]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.nqt - 1 - (int)(blockIdx.x / p.B), b = (int)(blockIdx.x % p.B);
@@ -124,7 +142,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int64_t rowq = (int64_t)b * p.L;
 
   if (threadIdx.x == 0) {
-    mbar_init(qfull, 1);
+    mbar_init(qready, TW);
     for (int i = 0; i < NSK; ++i) {
       mbar_init(&kfull[i], 1);
       mbar_init(&kempty[i], 1);
@@ -133,8 +151,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&vfull[i], 1);
       mbar_init(&vempty[i], 1);
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&sfull[i], 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&sfree[i], TW);
       mbar_init(&tready[i], TW);
       mbar_init(&tfree[i], 1);
     }
@@ -149,14 +168,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tmem = *tmem_slot;  // S[0..2] at cols 0, 64, 128; O at 192..192+DS
-  constexpr uint32_t O_COL = 3 * KB;
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {  // q once, then the k ring
-      mbar_expect_tx(qfull, 2 * Q_BYTES);
-      tma_load_2d(sQ, &tmQh, qfull, 0, (int)(rowq + q0));
-      tma_load_2d(sQ + Q_BYTES, &tmQl, qfull, 0, (int)(rowq + q0));
+    if (lane == 0) {  // the k ring
       for (int j = 0; j < nkb; ++j) {
         const int s = j % NSK;
         if (!mbar_wait(&kempty[s], ((j / NSK) & 1) ^ 1)) break;
@@ -177,46 +192,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0) {  // score MMAs, running ahead of the ternary pass by one buffer
       constexpr uint32_t idS = idesc_f16(KB);
-      const uint32_t idO = idesc_f16(p.DS);
-      bool ok = mbar_wait(qfull, 0);
+      bool ok = mbar_wait(qready, 0);
       fence_after();
-      const uint64_t qh = smem_desc_sw128(sQ), ql = smem_desc_sw128(sQ + Q_BYTES);
-      // scores run two blocks ahead of t.v^T: order S(0), S(1), [S(j+2), O(j)] for j = 0, 1, ...
-      auto scores = [&](int jj) -> bool {
-        const int s = jj % NSK;
-        if (!mbar_wait(&kfull[s], (jj / NSK) & 1)) return false;
-        GTC_MARK(0, jj);
+      for (int j = 0; ok && j < nkb; ++j) {
+        const int s = j % NSK, bs = j & 1;
+        if (!mbar_wait(&kfull[s], (j / NSK) & 1)) break;
+        // S[bs] was read (tcgen05.ld) by the ternary pass of block j - 2
+        if (j >= 2 && !mbar_wait(&sfree[bs], ((j - 2) >> 1) & 1)) break;
+        GTC_MARK(0, j);
         fence_after();
         const uint64_t kh = smem_desc_sw128(sK + s * 2 * K_BYTES), kl = smem_desc_sw128(sK + s * 2 * K_BYTES + K_BYTES);
-        const uint32_t dS = tmem + (jj % 3) * KB;  // read by the ternary pass of block jj - 3, long done
+        const uint32_t dS = tmem + COL_S + bs * KB;
 #pragma unroll
-        for (int kk = 0; kk < RP / 16; ++kk) {  // 16 fp16 = 32 bytes per K step: +2 in 16-byte units
-          mma_f16(dS, qh + 2 * kk, kh + 2 * kk, idS, kk > 0);
-          mma_f16(dS, qh + 2 * kk, kl + 2 * kk, idS, 1);
-          mma_f16(dS, ql + 2 * kk, kh + 2 * kk, idS, 1);
+        for (int kk = 0; kk < RP / 16; ++kk) {  // 16 fp16 per K step: +8 TMEM columns, +2 descriptor units
+          mma_f16_ts(dS, tmem + COL_QH + 8 * kk, kh + 2 * kk, idS, kk > 0);
+          mma_f16_ts(dS, tmem + COL_QH + 8 * kk, kl + 2 * kk, idS, 1);
+          mma_f16_ts(dS, tmem + COL_QL + 8 * kk, kh + 2 * kk, idS, 1);
         }
         commit(&kempty[s]);
-        commit(&sfull[jj % 3]);
-        GTC_MARK(7, jj);
-        return true;
-      };
-      for (int jj = 0; ok && jj < 2 && jj < nkb; ++jj) ok = scores(jj);
-      for (int j = 0; ok && j < nkb; ++j) {
-        if (j + 2 < nkb && !scores(j + 2)) break;
-        const int sv = j % NSV, bt = j & 1;  // t.v^T of block j
+        commit(&sfull[bs]);
+        GTC_MARK(7, j);
+      }
+    }
+  } else if (warp == 3 + TW) {
+    if (lane == 0) {  // t.v^T MMAs into the accumulator
+      const uint32_t idO = idesc_f16(p.DS);
+      for (int j = 0; j < nkb; ++j) {
+        const int sv = j % NSV, bt = j & 1;
         if (!mbar_wait(&tready[bt], (j >> 1) & 1)) break;
         GTC_MARK(1, j);
         if (!mbar_wait(&vfull[sv], (j / NSV) & 1)) break;
         GTC_MARK(2, j);
         fence_after();
-        const uint64_t ta = smem_desc_sw128(sT + bt * T_BYTES), vh = smem_desc_sw128(sV + sv * 2 * V_BYTES),
-                       vl = smem_desc_sw128(sV + sv * 2 * V_BYTES + V_BYTES);
+        const uint64_t vh = smem_desc_sw128(sV + sv * 2 * V_BYTES), vl = smem_desc_sw128(sV + sv * 2 * V_BYTES + V_BYTES);
+        const uint32_t ta = tmem + COL_T + bt * (KB / 2);
 #pragma unroll
         for (int kk = 0; kk < KB / 16; ++kk) {
-          mma_f16(tmem + O_COL, ta + 2 * kk, vh + 2 * kk, idO, (j | kk) != 0);
-          mma_f16(tmem + O_COL, ta + 2 * kk, vl + 2 * kk, idO, 1);
+          mma_f16_ts(tmem + COL_O, ta + 8 * kk, vh + 2 * kk, idO, (j | kk) != 0);
+          mma_f16_ts(tmem + COL_O, ta + 8 * kk, vl + 2 * kk, idO, 1);
         }
         commit(&vempty[sv]);
         commit(&tfree[bt]);
@@ -224,13 +239,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       commit(ofull);
     }
   } else {
-    // ternary warps 2 .. 2+TW-1: a warp reaches only TMEM lanes 32*(warp % 4) .. +31, so its lane
+    // ternary warps 2 .. 2+TW-1 (warps 0, 1, 2+TW, 3+TW are the producers and MMA issuers): a warp reaches only TMEM lanes 32*(warp % 4) .. +31, so its lane
     // quarter is q = warp % 4; part = which 16 of the block's 64 key columns it handles
     const int tw = warp - 2, q = warp & 3, part = tw >> 2;
     const int rl = q * 32 + lane, i = q0 + rl;
     const bool row_ok = i < p.L;
-    float cnt = 0.f;
-    bool ok = true;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    {  // q hi / lo of this row into TMEM: this part's 16 of the 64 values (8 columns each)
+      uint32_t vh[8], vl[8];
+      const int64_t qrow = rowq + min(i, p.L - 1);
+      const uint4 *gh = reinterpret_cast<const uint4 *>(qh_g + qrow * RP + part * 16);
+      const uint4 *gl = reinterpret_cast<const uint4 *>(ql_g + qrow * RP + part * 16);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint4 h = gh[u], l = gl[u];
+        vh[4 * u] = h.x, vh[4 * u + 1] = h.y, vh[4 * u + 2] = h.z, vh[4 * u + 3] = h.w;
+        vl[4 * u] = l.x, vl[4 * u + 1] = l.y, vl[4 * u + 2] = l.z, vl[4 * u + 3] = l.w;
+      }
+      tmem_st8(lane_base + COL_QH + part * 8, vh);
+      tmem_st8(lane_base + COL_QL + part * 8, vl);
+      asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(qready);
+    }
     // relb[i - key + L - 1] for this lane's row and its 16 keys of a block: 16 consecutive
     // entries (descending), loaded one block ahead; clamped indices are used only where
     // key > i or i >= L, where the score is masked.
@@ -243,20 +275,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float rb[16], rbn[16];
     load_relb(0, rbn);
     const uint32_t sgn_one = 0x3f800000u;
+    float cnt = 0.f;
+    bool ok = true;
     for (int j = 0; j < nkb; ++j) {
-      const int sb = j % 3, bt = j & 1;
+      const int bt = j & 1;
       const int key0 = j * KB + part * 16;
 #pragma unroll
       for (int c = 0; c < 16; ++c) rb[c] = rbn[c];
       if (j + 1 < nkb) load_relb(j + 1, rbn);
-      if (!mbar_wait(&sfull[sb], (j / 3) & 1)) {
+      if (!mbar_wait(&sfull[bt], (j >> 1) & 1)) {
         ok = false;
         break;
       }
       if (tw == 0 && lane == 0) GTC_MARK(3, j);
       fence_after();
       uint32_t r[16];
-      tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + sb * KB + part * 16, r);
+      tmem_ld16(lane_base + COL_S + bt * KB + part * 16, r);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sfree[bt]);  // the score MMAs may refill this buffer
       // whole warp strictly below the diagonal and inside the sequence: no per-score mask
       const bool dense = key0 + 15 <= q0 + q * 32 && q0 + q * 32 + 31 < p.L;
       uint32_t packed[8];
@@ -282,33 +319,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       if (tw == 0 && lane == 0) GTC_MARK(5, j);
-      // row rl of the 128 x 64 fp16 tile (128-byte rows, 128-byte swizzle): 16-byte chunk u of
-      // this part sits at chunk index (part*2 + u) ^ (rl & 7)
-      uint8_t *trow = sT + bt * T_BYTES + rl * 128;
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
-        *reinterpret_cast<uint4 *>(trow + (((part * 2 + u) ^ (rl & 7)) << 4)) =
-            make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      fence_after();
+      tmem_st8(lane_base + COL_T + bt * (KB / 2) + part * 8, packed);
+      asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tready[bt]);
       if (tw == 0 && lane == 0) GTC_MARK(6, j);
     }
-    // the row's count is split over its 4 column parts; the ternary tiles are free once the
-    // accumulator is complete, so the partial counts go there
-    const bool o_ok = ok && mbar_wait(ofull, 0);
-    float *cnt_s = reinterpret_cast<float *>(sT);  // [4][QT]
+    // the row's count is split over its 4 column parts
     cnt_s[part * QT + rl] = cnt;
     asm volatile("bar.sync 1, %0;\n" ::"n"(32 * TW) : "memory");  // the ternary warps
     const float denom = fmaxf(cnt_s[rl] + cnt_s[QT + rl] + cnt_s[2 * QT + rl] + cnt_s[3 * QT + rl], 1.f);
-    if (o_ok) {
+    if (ok && mbar_wait(ofull, 0)) {
       fence_after();
       const int nch = (p.DS + 15) / 16;  // 16-column chunks; TMEM columns past DS are allocated, unused
       const int64_t row = rowq + i;
       for (int ch = part; ch < nch; ch += 4) {
         uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + O_COL + ch * 16, r);
+        tmem_ld16(lane_base + COL_O + ch * 16, r);
         if (!row_ok) continue;
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
@@ -452,9 +481,7 @@ extern "C" int tesm_b200_siso_global_ent_tc(const void *proj, int dtype, int64_t
   gtc::k_gtc_prep_v<<<gv, 256, 0, st>>>(states, (int)L, (int)D, lay.DS, lay.Lp, vth, vtl);
   if ((rc = check_launch("global_ent_tc prep v"))) return rc;
 
-  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
-  if ((rc = gtc::make_map_f16(&mqh, qh, gtc::RP, M, gtc::RP, gtc::QT))) return rc;
-  if ((rc = gtc::make_map_f16(&mql, ql, gtc::RP, M, gtc::RP, gtc::QT))) return rc;
+  CUtensorMap mkh, mkl, mvh, mvl;
   if ((rc = gtc::make_map_f16(&mkh, kh, gtc::RP, M, gtc::RP, gtc::KB))) return rc;
   if ((rc = gtc::make_map_f16(&mkl, kl, gtc::RP, M, gtc::RP, gtc::KB))) return rc;
   if ((rc = gtc::make_map_f16(&mvh, vth, lay.Lp, B * lay.DS, gtc::KB, lay.DS))) return rc;
@@ -475,14 +502,14 @@ extern "C" int tesm_b200_siso_global_ent_tc(const void *proj, int dtype, int64_t
   p.out_tanh = out_tanh;
   p.out_chg = out_chg;
   p.out_dtype = out_dtype;
-  const size_t smem = 1024 + 2 * (size_t)gtc::QT * gtc::RP * 2 + gtc::NSK * 2 * (size_t)gtc::KB * gtc::RP * 2 +
-                      2 * (size_t)gtc::QT * gtc::KB * 2 + gtc::NSV * 2 * (size_t)lay.DS * gtc::KB * 2 + 256;
+  const size_t smem = 1024 + gtc::NSK * 2 * (size_t)gtc::KB * gtc::RP * 2 + gtc::NSV * 2 * (size_t)lay.DS * gtc::KB * 2 +
+                      256 + 4 * gtc::QT * sizeof(float);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(gtc::k_global_ent_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     attr = true;
   }
   TESM_REQUIRE(smem <= 227 * 1024, "global_ent_tc: shared memory");
-  gtc::k_global_ent_tc<<<(unsigned)(B * p.nqt), gtc::NUM_THREADS, smem, st>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
+  gtc::k_global_ent_tc<<<(unsigned)(B * p.nqt), gtc::NUM_THREADS, smem, st>>>(mkh, mkl, mvh, mvl, qh, ql, p);
   return check_launch("global_ent_tc");
 }
