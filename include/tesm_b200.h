@@ -91,6 +91,24 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
  * SMs (decode batches), K is split across up to 8 CTAs per tile; each split stores its int32
  * partial tile into its own M*N slice of the workspace and a finalize kernel sums the slices in a
  * fixed order (exact integers, deterministic).  The split count is capped so S*M*N*4 <= ws_bytes. */
+/* Tensor-parallel pieces of the row-parallel BitLinear (down_proj / out_proj split along K over
+ * ranks; no counterpart in the reference, which runs on one device):
+ * tesm_b200_row_absmax: amax[m] = max_k |x[m,k]| of this rank's K-shard (the caller reduces it
+ *   with MAX across ranks);
+ * tesm_b200_quant_act_amax: tesm_b200_quant_act with the row maxima given (the global ones), so
+ *   every rank's codes equal the single-device codes of its columns;
+ * tesm_b200_gemm_i8 with out == NULL and acc_out set writes only the int32 partial accumulators
+ *   (summed exactly across ranks by the caller);
+ * tesm_b200_acc_scale: out[m,n] = acc[m,n] * inv_scale[m] * w_deq[n or 0] (acc is M x N, dense),
+ *   the same float operations as the GEMM epilogue, so the result is bit-identical to one device. */
+int tesm_b200_row_absmax(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float *amax,
+                         tesm_stream_t stream);
+int tesm_b200_quant_act_amax(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
+                             const float *amax, int8_t *codes, int64_t ld_codes, int layout, float *inv_scale,
+                             int32_t *rowsum, tesm_stream_t stream);
+int tesm_b200_acc_scale(const int32_t *acc, int64_t M, int64_t N, const float *inv_scale, const float *w_deq,
+                        int per_row, void *out, int out_dtype, int64_t ldo, tesm_stream_t stream);
+
 /* state_proj + ent_proj + output combine in one tcgen05 GEMM (tesm.py:1256-1260): two TMEM
  * accumulators, acc1 over the first Kh columns (codes of tanh(ent) x state_proj ternary weights),
  * acc2 over the next Kh (codes of ent - s x ent_proj weights); the epilogue writes

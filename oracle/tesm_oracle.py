@@ -94,15 +94,18 @@ def unpack_int2(packed, k=None):
     return v if k is None else v[:, :k]
 
 
-def quant_act(x, eps=1e-5, dtype="float32"):
+def quant_act(x, eps=1e-5, dtype="float32", amax=None):
     """int8 codes of ``BitLinear.quantized_input`` (tesm.py:206-209).
 
     s = 127 / max(max|x|, eps) in the input dtype -- torch evaluates ``127 / t`` as
     ``t.reciprocal() * 127`` (two roundings); c = clamp(round(x*s), -128, 127).
+    ``amax`` (optional, per row) replaces max|x|: the quantisation of a column slice of a wider
+    row with the full row's maximum (tensor-parallel shards).
     Returns (codes int8 (..., K), s float32 (...,)).
     """
     x = cast(x, dtype)
-    mx = cast(np.maximum(np.abs(x).max(axis=-1), F32(eps)).astype(F32), dtype)
+    ax = np.abs(x).max(axis=-1) if amax is None else np.asarray(amax, dtype=F32)
+    mx = cast(np.maximum(ax, F32(eps)).astype(F32), dtype)
     s = cast(cast(F32(1.0) / mx, dtype) * F32(127.0), dtype)
     prod = cast(x * s[..., None], dtype)
     c = np.clip(np.rint(prod), -128, 127).astype(np.int8)

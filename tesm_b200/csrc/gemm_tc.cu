@@ -637,6 +637,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int j = 0; j < 32; ++j)
             if (n0 + j < p.N) arow[n0 + j] = (int32_t)r[j];
         }
+        if (!p.out) continue;  // accumulator-only call (tensor-parallel partial sums)
         if (p.vec_store && n0 + 32 <= p.N) {
           if (p.out_dtype == TESM_BF16) {
             uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + (int64_t)row * p.ldo + n0);
@@ -705,7 +706,7 @@ __global__ void k_splitk_finalize(const int32_t *ws, int splits, int M, int N, c
     int32_t a = 0;
     for (int s = 0; s < splits; ++s) a += ws[s * slice + (int64_t)m * N + n];
     const float wd = per_row ? w_deq[n] : w_deq[0];
-    store_f(out, out_dtype, (int64_t)m * ldo + n, (float)a * xs * wd);
+    if (out) store_f(out, out_dtype, (int64_t)m * ldo + n, (float)a * xs * wd);
     if (acc_out) acc_out[(int64_t)m * ld_acc + n] = a;
   }
 }
@@ -924,7 +925,7 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
                                  int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K,
                                  void *out, int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc,
                                  int32_t *splitk_ws, int64_t ws_bytes, tesm_stream_t stream) {
-  TESM_REQUIRE(codes && inv_scale && tern && w_deq && out, "gemm_i8: null pointer");
+  TESM_REQUIRE(codes && inv_scale && tern && w_deq && (out || acc_out), "gemm_i8: null pointer");
   TESM_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31), "gemm_i8: bad shape");
   if (M == 0) return TESM_OK;
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8: out dtype");
@@ -970,4 +971,17 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
   if (N <= 128) return tc::launch<128>(codes, ld_codes, tern, ld_tern, p, st);
   if (tc::use_pairs(M, N)) return tc::launch<256, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, st);
+}
+
+extern "C" int tesm_b200_acc_scale(const int32_t *acc, int64_t M, int64_t N, const float *inv_scale,
+                                   const float *w_deq, int per_row, void *out, int out_dtype, int64_t ldo,
+                                   tesm_stream_t stream) {
+  TESM_REQUIRE(acc && inv_scale && w_deq && out, "acc_scale: null pointer");
+  TESM_REQUIRE(M >= 0 && N > 0 && ldo >= N && M * N < (1ll << 40), "acc_scale: bad shape");
+  if (M == 0) return TESM_OK;
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "acc_scale: out dtype");
+  const int64_t n = M * N;
+  tc::k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      acc, 1, (int)M, (int)N, inv_scale, w_deq, per_row, 0, out, out_dtype, ldo, nullptr, 0);
+  return check_launch("acc_scale");
 }

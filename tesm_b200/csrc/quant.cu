@@ -93,7 +93,8 @@ constexpr int kQuantGPT = 4;
 template <int GPT>
 __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, int64_t ldx, float eps,
                             int8_t *__restrict__ codes, int64_t ld_codes, int layout, int64_t groups_out,
-                            float *__restrict__ inv_scale, int32_t *__restrict__ rowsum, int vec) {
+                            float *__restrict__ inv_scale, int32_t *__restrict__ rowsum, int vec,
+                            const float *__restrict__ amax_in) {
   __shared__ float redf[32];
   __shared__ int redi[32];
   const int64_t row = blockIdx.x;
@@ -115,6 +116,7 @@ __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, in
     for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[j][e]));
   }
   amax = block_reduce(amax, redf, [](float a, float b) { return fmaxf(a, b); }, 0.f);
+  if (amax_in) amax = amax_in[row];  // the row's max |x| over all tensor-parallel shards
   const float s = act_scale(amax, eps, dtype);
   if (threadIdx.x == 0) inv_scale[row] = __frcp_rn(s);
   int csum = 0;
@@ -135,6 +137,23 @@ __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, in
     csum = block_reduce(csum, redi, [](int a, int b) { return a + b; }, 0);
     if (threadIdx.x == 0) rowsum[row] = csum;
   }
+}
+
+// max |x| of each row (tensor-parallel shards: reduced across ranks, then quantised with it).
+__global__ void k_row_absmax(const void *__restrict__ x, int dtype, int64_t K, int64_t ldx, int vec,
+                             float *__restrict__ amax_out) {
+  __shared__ float redf[32];
+  const int64_t row = blockIdx.x;
+  const void *xrow = reinterpret_cast<const uint8_t *>(x) + row * ldx * (dtype == TESM_BF16 ? 2 : 4);
+  float amax = 0.f;
+  for (int64_t g = threadIdx.x; g < (K + 15) / 16; g += blockDim.x) {
+    float v[16];
+    load16(xrow, dtype, g * 16, K, vec, v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
+  }
+  amax = block_reduce(amax, redf, [](float a, float b) { return fmaxf(a, b); }, 0.f);
+  if (threadIdx.x == 0) amax_out[row] = amax;
 }
 
 }  // namespace tesm
@@ -174,9 +193,9 @@ extern "C" int tesm_b200_pack_ternary(const void *w, int dtype, int64_t N, int64
   return check_launch("pack_ternary");
 }
 
-extern "C" int tesm_b200_quant_act(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
-                                   int8_t *codes, int64_t ld_codes, int layout, float *inv_scale, int32_t *rowsum,
-                                   tesm_stream_t stream) {
+static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
+                          const float *amax, int8_t *codes, int64_t ld_codes, int layout, float *inv_scale,
+                          int32_t *rowsum, tesm_stream_t stream) {
   TESM_REQUIRE(x && codes && inv_scale, "quant_act: null pointer");
   TESM_REQUIRE(M >= 0 && K > 0 && ldx >= K, "quant_act: bad shape");
   if (M == 0) return TESM_OK;
@@ -199,6 +218,30 @@ extern "C" int tesm_b200_quant_act(const void *x, int dtype, int64_t M, int64_t 
   const int esz = dtype == TESM_BF16 ? 2 : 4;
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
   k_quant_act<kQuantGPT><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-      x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec);
+      x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
   return check_launch("quant_act");
+}
+
+extern "C" int tesm_b200_quant_act(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
+                                   int8_t *codes, int64_t ld_codes, int layout, float *inv_scale, int32_t *rowsum,
+                                   tesm_stream_t stream) {
+  return quant_act_impl(x, dtype, M, K, ldx, eps, nullptr, codes, ld_codes, layout, inv_scale, rowsum, stream);
+}
+
+extern "C" int tesm_b200_quant_act_amax(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
+                                        const float *amax, int8_t *codes, int64_t ld_codes, int layout,
+                                        float *inv_scale, int32_t *rowsum, tesm_stream_t stream) {
+  TESM_REQUIRE(amax, "quant_act_amax: null amax");
+  return quant_act_impl(x, dtype, M, K, ldx, eps, amax, codes, ld_codes, layout, inv_scale, rowsum, stream);
+}
+
+extern "C" int tesm_b200_row_absmax(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float *amax,
+                                    tesm_stream_t stream) {
+  TESM_REQUIRE(x && amax && M >= 0 && K > 0 && ldx >= K, "row_absmax: bad argument");
+  if (M == 0) return TESM_OK;
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "row_absmax: dtype must be f32 or bf16");
+  const int esz = dtype == TESM_BF16 ? 2 : 4;
+  const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
+  k_row_absmax<<<(unsigned)M, 128, 0, (cudaStream_t)stream>>>(x, dtype, K, ldx, vec, amax);
+  return check_launch("row_absmax");
 }

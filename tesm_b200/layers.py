@@ -14,6 +14,7 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
+from . import parallel
 from ._lib import TesmError
 
 B200 = "b200"
@@ -164,6 +165,14 @@ def _as_quant(mod, u2d):
     return u2d if isinstance(u2d, ops.QuantAct) else ops.quantize(u2d, mod.in_proj.bit_eps)
 
 
+def _out_proj(mod, y, act_dtype):
+    """out_proj (tesm.py:1261); row-parallel across ranks when tensor parallelism is enabled."""
+    tp = parallel.get_tp(mod)
+    if tp is not None:
+        return parallel.out_proj_tp(mod, y, act_dtype, tp)
+    return linear(mod.out_proj, y, act_dtype)
+
+
 def _tail(mod, proj, M, C, Rc, tanh_e, chg, act_dtype):
     """state_proj / ent_proj, output combine and out_proj (tesm.py:1255-1261)."""
     Dm = mod.d_model
@@ -171,7 +180,7 @@ def _tail(mod, proj, M, C, Rc, tanh_e, chg, act_dtype):
     ep = linear(mod.ent_proj, chg, act_dtype)
     y = torch.empty(M, Dm, device=proj.device, dtype=act_dtype)
     ops.combine(proj, M, Dm, C, Rc, sp, ep, y)
-    return linear(mod.out_proj, y, act_dtype)
+    return _out_proj(mod, y, act_dtype)
 
 
 def combine_weight(mod):
@@ -235,7 +244,7 @@ def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, ac
         tern, deq1, deq2, _ = combine_weight(mod)
         y = torch.empty(M, Dm, device=dev, dtype=act_dtype)
         ops.gemm_combine(codes, Dp, inv1, inv2, tern, deq1, deq2, proj, 0, Dm + 3 * D, M, Dm, y)
-        out = linear(mod.out_proj, y, act_dtype)
+        out = _out_proj(mod, y, act_dtype)
     else:
         out = _tail(mod, proj, M, D, R, tanh_e, chg, act_dtype)
     mod.last_entanglement_map = None
@@ -422,6 +431,9 @@ def ffn_packed(ffn):
 
 def ffn_q(ffn, q: ops.QuantAct, act_dtype):
     """``FeedForward.forward`` on pre-quantised input (mixer_seq_simple.py:59-67)."""
+    tp = parallel.get_tp(ffn)
+    if tp is not None:
+        return parallel.ffn_q_tp(ffn, q, act_dtype, tp)
     pw, blk = ffn_packed(ffn)
     Fd = ffn.gate_proj.out_features
     if blk and q.layout == ops.LAYOUT_ROWMAJOR:

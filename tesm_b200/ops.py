@@ -154,6 +154,59 @@ def gemm(codes, inv, pw: PackedWeight, M: int, out_dtype: torch.dtype, out=None,
     return (out, accb) if acc else out
 
 
+def gemm_acc(codes, inv, pw: PackedWeight, M: int, acc: torch.Tensor):
+    """int32 accumulators only (no scaled output): the partial product of a row-parallel shard."""
+    ws = splitk_workspace(M, pw.N, codes.device)
+    _lib.call("tesm_b200_gemm_i8", codes.data_ptr(), codes.stride(0), inv.data_ptr(), pw.tern.data_ptr(),
+              pw.tern.stride(0), pw.deq.data_ptr(), int(pw.per_row), M, pw.N, pw.K, None, dtype_code(torch.float32),
+              pw.N, acc.data_ptr(), acc.stride(0), _ptr(ws), ws.numel() * 4 if ws is not None else 0, _stream())
+    return acc
+
+
+def acc_scale(acc, inv, pw: PackedWeight, out_dtype, out=None):
+    """out = acc * inv_scale[row] * deq (the GEMM epilogue's float operations, bit for bit)."""
+    M, N = acc.shape
+    out = out if out is not None else torch.empty(M, N, device=acc.device, dtype=out_dtype)
+    _lib.call("tesm_b200_acc_scale", acc.data_ptr(), M, N, inv.data_ptr(), pw.deq.data_ptr(), int(pw.per_row),
+              out.data_ptr(), dtype_code(out.dtype), out.stride(0), _stream())
+    return out
+
+
+def row_absmax(x2d: torch.Tensor, out=None):
+    M, K = x2d.shape
+    out = out if out is not None else torch.empty(M, device=x2d.device, dtype=torch.float32)
+    _lib.call("tesm_b200_row_absmax", x2d.data_ptr(), dtype_code(x2d.dtype), M, K, x2d.stride(0), out.data_ptr(),
+              _stream())
+    return out
+
+
+def quant_act_amax(x2d: torch.Tensor, eps: float, amax: torch.Tensor) -> "QuantAct":
+    """Row-major int8 codes of x with the row maxima given (global across tensor-parallel shards)."""
+    M, K = x2d.shape
+    ld = round_up(K, 16)
+    codes = torch.empty(M, ld, device=x2d.device, dtype=torch.int8)
+    inv = torch.empty(M, device=x2d.device, dtype=torch.float32)
+    _lib.call("tesm_b200_quant_act_amax", x2d.data_ptr(), dtype_code(x2d.dtype), M, K, x2d.stride(0), float(eps),
+              amax.data_ptr(), codes.data_ptr(), ld, LAYOUT_ROWMAJOR, inv.data_ptr(), None, _stream())
+    return QuantAct(codes, inv, None, LAYOUT_ROWMAJOR, M)
+
+
+def pack_shard(w_full: torch.Tensor, eps: float, rows=None, cols=None, per_row: bool = False) -> PackedWeight:
+    """Ternary pack of a row or column slice of a weight with the scale of the FULL weight (the
+    reference quantises each BitLinear as a whole, tesm.py:211-215)."""
+    scale, deq = weight_scale(w_full, eps, per_row)
+    w = w_full
+    if rows is not None:
+        w = w[rows[0]:rows[1]]
+        if per_row:
+            scale, deq = scale[rows[0]:rows[1]].contiguous(), deq[rows[0]:rows[1]].contiguous()
+    if cols is not None:
+        w = w[:, cols[0]:cols[1]]
+    pw = pack_weight(w, eps, per_row, with_tern=True, scale=scale)
+    pw.deq = deq
+    return pw
+
+
 def bitlinear_2d(x2d: torch.Tensor, pw: PackedWeight, eps: float, out_dtype=None, out=None, acc=False,
                  force: Optional[str] = None):
     """Quantise a (M, K) activation and multiply by a packed ternary weight."""
