@@ -281,6 +281,31 @@ def run_gpu(args, rank, world, local_rank):
                    "batch_per_gpu": Bd, "prompt": 16, "steps": args.decode_steps,
                    "ms_per_step": t_dec / args.decode_steps * 1e3, "cuda_graph": True, "sampling": "greedy argmax"}
             del dg, ip
+            if world > 1:
+                # tensor-parallel decode over all ranks (FFN column/row split, out_proj row split,
+                # NCCL all-reduces inside the captured graph): one batch of 256 shared by the ranks
+                from tesm_b200 import parallel
+                parallel.enable_tensor_parallel(model)
+                torch.cuda.empty_cache()
+                ip = {"state_cache": model.backbone.allocate_inference_cache(Bd, CFG["max_seq_len"])}
+                o, _ = model(prompt, inference_params=ip, logits_to_keep=1)
+                dg = DecodeGraph(model, ip, o.logits[:, -1, :].argmax(-1, keepdim=True))
+                for _ in range(3):
+                    dg.step()
+                n_tp = min(args.decode_steps, 128)
+                barrier()
+                d0, d1 = ev(), ev()
+                d0.record()
+                for _ in range(n_tp):
+                    dg.step()
+                d1.record()
+                barrier()
+                t_tp = max_over_ranks(d0.elapsed_time(d1) / 1e3)
+                dec["tensor_parallel"] = {"tp": world, "batch": Bd, "steps": n_tp, "value": Bd * n_tp / t_tp,
+                                          "unit": UNIT, "ms_per_step": t_tp / n_tp * 1e3,
+                                          "note": "whole job: one batch shared by all ranks; data-parallel "
+                                                  "replicas (the value above) are faster at this batch"}
+                del dg, ip
         status = ops.device_status()
 
     if rank != 0:
