@@ -263,7 +263,13 @@ struct ScanLayout {
 
 static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
   ScanLayout s;
-  s.T = 32;
+  s.T = RM > 1 ? 16 : 32;  // measured: MIMO (3 staged planes) prefers more, shorter chunks
+  static int force = -1;
+  if (force < 0) {
+    const char *e = getenv("TESM_SCAN_T");  // tuning override: positions per chunk
+    force = e ? atoi(e) : 0;
+  }
+  if (force > 0) s.T = force;
   s.slice = C < 256 ? (int)round_up(C, 32) : 256;
   s.nchunks = (int)ceil_div(L, s.T);
   s.nslices = (int)ceil_div(C, s.slice);
