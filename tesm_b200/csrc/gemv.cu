@@ -83,6 +83,11 @@ __global__ void __launch_bounds__(256) k_gemv_int2(GemvParams p) {
     }
   }
 
+  // Launched with programmatic stream serialization: the weight prefetch above overlaps the tail
+  // of the quantisation kernel that produces the codes; wait for that grid (and its memory)
+  // before touching them.  A no-op for an ordinary launch.
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+
   // ---- stage this CTA's K-slice of the activation codes in shared memory
   {
     const int chunks = nsteps * 16;  // 16-byte chunks per token row
@@ -197,13 +202,15 @@ static int launch_gemv(const GemvParams &p, cudaStream_t st) {
   cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = (unsigned)p.split;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddepcontrol.wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_int2<NT>, p);
   if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemv_int2 launch: ") + cudaGetErrorString(e));
   return TESM_OK;

@@ -97,6 +97,9 @@ __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, in
                             const float *__restrict__ amax_in) {
   __shared__ float redf[32];
   __shared__ int redi[32];
+  // let a programmatically serialized consumer (the GEMV) start its weight prefetch now; it
+  // still waits for this whole grid before reading the codes
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const int64_t row = blockIdx.x;
   const int64_t groups_in = (K + 15) / 16;
   const int esz = dtype == TESM_BF16 ? 2 : 4;

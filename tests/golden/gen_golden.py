@@ -1,7 +1,7 @@
 """Generate golden vectors by running the reference torch backend.
 
 Run where the reference package is importable (``TESM_REFERENCE`` points at the
-project root, default ``/root/reference``):
+project root; default: a ``reference`` directory beside this repository):
 
     python tests/golden/gen_golden.py
 
@@ -24,7 +24,8 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("TESM_REFERENCE", "/root/reference")
+REF = os.environ.get("TESM_REFERENCE") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))), "reference")
 sys.path.insert(0, REF)
 
 from tesm_ssm.modules.tesm import BitLinear, TESM_SISO  # noqa: E402
