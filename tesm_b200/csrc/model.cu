@@ -97,23 +97,32 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
 
 // out[m, f] = silu(gate[m, f]) * up[m, f]; gu holds [gate | up] halves (blk == 0) or
 // blocks of `blk` gate columns followed by the matching `blk` up columns.
-__global__ void k_silu_mul(const void *gu, int dtype, int64_t M, int F, void *out, int odtype, int blk) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * F) return;
-  const int64_t m = i / F;
-  const int f = (int)(i - m * F);
-  int64_t gi, ui;
+// Thread = 8 consecutive output columns of one row (grid.y strides over rows): 16-byte
+// bf16 / 32-byte fp32 vectors when aligned; blk is a multiple of 8, so a group never straddles
+// an interleave block.
+__global__ void k_silu_mul(const void *gu, int dtype, int64_t M, int F, void *out, int odtype, int blk, int vec) {
+  const int f0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (f0 >= F) return;
+  int gcol, ucol;
   if (blk) {
-    const int b = f / blk, j = f - b * blk;
-    gi = m * 2 * F + (int64_t)b * 2 * blk + j;
-    ui = gi + blk;
+    const int b = f0 / blk, j = f0 - b * blk;
+    gcol = b * 2 * blk + j;
+    ucol = gcol + blk;
   } else {
-    gi = m * 2 * F + f;
-    ui = gi + F;
+    gcol = f0;
+    ucol = f0 + F;
   }
-  const float g = load_f(gu, dtype, gi);
-  const float u = load_f(gu, dtype, ui);
-  store_f(out, odtype, i, (g * sigmoidf_(g)) * u);
+  const int gsz = dtype == TESM_BF16 ? 2 : 4, osz = odtype == TESM_BF16 ? 2 : 4;
+  for (int64_t m = blockIdx.y; m < M; m += gridDim.y) {
+    const uint8_t *row = reinterpret_cast<const uint8_t *>(gu) + m * 2 * (int64_t)F * gsz;
+    float g[8], u[8], o[8];
+    // columns past F only occur without an interleave (blk == 0, F % 8 != 0, scalar path)
+    load8(row, dtype, gcol, blk ? gcol + 8 : F, vec != 0, g);
+    load8(row, dtype, ucol, blk ? ucol + 8 : 2 * F, vec != 0, u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = (g[e] * sigmoidf_(g[e])) * u[e];
+    store8(reinterpret_cast<uint8_t *>(out) + m * (int64_t)F * osz, odtype, f0, F, vec != 0, o);
+  }
 }
 
 // Prefill -> cache (tesm.py:1235-1253): last min(L, W) positions of rope(k) and of the
@@ -169,15 +178,22 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
     }
     TESM_REQUIRE(ld_codes >= groups_out * 16, "add_rmsnorm_quant: ld_codes too small");
   }
-  int64_t threads = round_up(ceil_div(groups_out, 4), 32);
-  if (threads < 32) threads = 32;
-  TESM_REQUIRE(threads <= 1024, "add_rmsnorm_quant: K too large");
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && (!residual || (uintptr_t)residual % 16 == 0) &&
                   (!residual_out || (uintptr_t)residual_out % 16 == 0) && ((uintptr_t)weight % 16 == 0) &&
                   (!y_out || (uintptr_t)y_out % 16 == 0);
-  k_add_rmsnorm_quant<4><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-      x, xdtype, residual, residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale,
-      rowsum, y_out, ydtype, vec);
+  // few rows (decode): one 16-element group per thread, so each row's latency chain is short
+  const int gpt = M < 1024 && groups_out <= 1024 ? 1 : 4;
+  int64_t threads = round_up(ceil_div(groups_out, gpt), 32);
+  if (threads < 32) threads = 32;
+  TESM_REQUIRE(threads <= 1024, "add_rmsnorm_quant: K too large");
+  if (gpt == 1)
+    k_add_rmsnorm_quant<1><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
+        x, xdtype, residual, residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale,
+        rowsum, y_out, ydtype, vec);
+  else
+    k_add_rmsnorm_quant<4><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
+        x, xdtype, residual, residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale,
+        rowsum, y_out, ydtype, vec);
   return check_launch("add_rmsnorm_quant");
 }
 
@@ -186,9 +202,14 @@ extern "C" int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t 
   TESM_REQUIRE(blk == 0 || F % blk == 0, "silu_mul: F must be a multiple of the interleave block");
   TESM_REQUIRE(gu && out && M >= 0 && F > 0, "silu_mul: bad argument");
   if (M == 0) return TESM_OK;
-  const int64_t n = M * F;
-  k_silu_mul<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(gu, dtype, M, (int)F, out, odtype,
-                                                                             (int)blk);
+  TESM_REQUIRE(blk == 0 || blk % 8 == 0, "silu_mul: interleave block must be a multiple of 8");
+  const int gsz = dtype == TESM_BF16 ? 2 : 4, osz = odtype == TESM_BF16 ? 2 : 4;
+  const int vec = (F % 8 == 0) && ((uintptr_t)gu % 16 == 0) && ((uintptr_t)out % 16 == 0) && ((F * gsz) % 16 == 0) &&
+                  ((F * osz) % 16 == 0);
+  const int64_t groups = ceil_div(F, 8);
+  const int threads = groups >= 128 ? 128 : (int)round_up(groups, 32);
+  dim3 grid((unsigned)ceil_div(groups, threads), (unsigned)(M < 65535 ? M : 65535));
+  k_silu_mul<<<grid, threads, 0, (cudaStream_t)stream>>>(gu, dtype, M, (int)F, out, odtype, (int)blk, vec);
   return check_launch("silu_mul");
 }
 

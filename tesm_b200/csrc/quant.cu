@@ -215,13 +215,18 @@ static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_
   } else {
     return fail(TESM_EINVAL, "quant_act: unknown layout");
   }
-  int64_t threads = round_up(ceil_div(groups_out, kQuantGPT), 32);
+  const int gpt = M < 1024 && groups_out <= 1024 ? 1 : kQuantGPT;  // few rows: short per-row chains
+  int64_t threads = round_up(ceil_div(groups_out, gpt), 32);
   if (threads < 32) threads = 32;
   TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
   const int esz = dtype == TESM_BF16 ? 2 : 4;
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
-  k_quant_act<kQuantGPT><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-      x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
+  if (gpt == 1)
+    k_quant_act<1><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
+        x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
+  else
+    k_quant_act<kQuantGPT><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
+        x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
   return check_launch("quant_act");
 }
 

@@ -61,6 +61,49 @@ __device__ __forceinline__ void store16(void *row, int dtype, int64_t k0, int64_
   }
 }
 
+// 8 consecutive elements starting at column k0 (< K); `vec` promises 16-byte alignment of
+// row + k0 and k0 + 8 <= K.
+__device__ __forceinline__ void load8(const void *row, int dtype, int64_t k0, int64_t K, bool vec, float (&v)[8]) {
+  if (vec) {
+    if (dtype == TESM_BF16) {
+      const uint4 a = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(row) + k0);
+      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&a);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+      const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(row) + k0);
+      const float4 a = p[0], b = p[1];
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = k0 + e < K ? load_f(row, dtype, k0 + e) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void store8(void *row, int dtype, int64_t k0, int64_t K, bool vec, const float (&v)[8]) {
+  if (vec) {
+    if (dtype == TESM_BF16) {
+      __nv_bfloat162 h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      *reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(row) + k0) = *reinterpret_cast<uint4 *>(h);
+    } else {
+      float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(row) + k0);
+      p[0] = make_float4(v[0], v[1], v[2], v[3]);
+      p[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (k0 + e < K) store_f(row, dtype, k0 + e, v[e]);
+  }
+}
+
 // Codes of one 16-element group (already scaled and rounded) into row-major or GEMV layout.
 // GEMV layout: natural column k = s*256 + tig*64 + u*16 + 4*i + sw is stored at
 // s*256 + u*64 + tig*16 + sw*4 + i (consumer: gemv.cu).

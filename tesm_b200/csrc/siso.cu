@@ -307,16 +307,23 @@ static int launch_global(GlobalEntParams &p, cudaStream_t st) {
 
 // ---------------------------------------------------------------- combine
 // y = local + sigmoid(gate) * sp + ep   (tesm.py:1256-1260)
+// Thread = 8 consecutive columns of one row (grid.y strides over rows).
 __global__ void k_combine(ProjCols pc, const void *sp, const void *ep, int sdtype, int64_t M, int Dm, void *y,
-                          int ydtype) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * Dm) return;
-  const int64_t m = i / Dm;
-  const int c = (int)(i - m * Dm);
-  const float loc = load_f(pc.proj, pc.dtype, m * pc.ld + pc.c_local + c);
-  const float g = sigmoidf_(load_f(pc.proj, pc.dtype, m * pc.ld + pc.c_gate + c));
-  const float v = loc + g * load_f(sp, sdtype, i) + load_f(ep, sdtype, i);
-  store_f(y, ydtype, i, v);
+                          int ydtype, int vec) {
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= Dm) return;
+  const int psz = pc.dtype == TESM_BF16 ? 2 : 4, ssz = sdtype == TESM_BF16 ? 2 : 4, ysz = ydtype == TESM_BF16 ? 2 : 4;
+  for (int64_t m = blockIdx.y; m < M; m += gridDim.y) {
+    const uint8_t *prow = reinterpret_cast<const uint8_t *>(pc.proj) + m * pc.ld * psz;
+    float loc[8], gt[8], a[8], b[8], v[8];
+    load8(prow, pc.dtype, pc.c_local + c0, pc.c_local + Dm, vec != 0, loc);
+    load8(prow, pc.dtype, pc.c_gate + c0, pc.c_gate + Dm, vec != 0, gt);
+    load8(reinterpret_cast<const uint8_t *>(sp) + m * Dm * ssz, sdtype, c0, Dm, vec != 0, a);
+    load8(reinterpret_cast<const uint8_t *>(ep) + m * Dm * ssz, sdtype, c0, Dm, vec != 0, b);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = loc[e] + sigmoidf_(gt[e]) * a[e] + b[e];
+    store8(reinterpret_cast<uint8_t *>(y) + m * Dm * ysz, ydtype, c0, Dm, vec != 0, v);
+  }
 }
 
 }  // namespace tesm
@@ -528,6 +535,15 @@ extern "C" int tesm_b200_combine(const void *proj, int dtype, int64_t ldp, int64
   if (M == 0) return TESM_OK;
   ProjCols pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
   const int64_t n = M * Dm;
-  k_combine<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(pc, sp, ep, sdtype, M, (int)Dm, y, ydtype);
+  const int psz = dtype == TESM_BF16 ? 2 : 4, ssz = sdtype == TESM_BF16 ? 2 : 4, ysz = ydtype == TESM_BF16 ? 2 : 4;
+  const int vec = (Dm % 8 == 0) && ((uintptr_t)proj % 16 == 0) && ((ldp * psz) % 16 == 0) &&
+                  ((pc.c_local * psz) % 16 == 0) && ((pc.c_gate * psz) % 16 == 0) && ((uintptr_t)sp % 16 == 0) &&
+                  ((uintptr_t)ep % 16 == 0) && ((uintptr_t)y % 16 == 0) && ((Dm * ssz) % 16 == 0) &&
+                  ((Dm * ysz) % 16 == 0);
+  (void)n;
+  const int64_t groups = ceil_div(Dm, 8);
+  const int threads = groups >= 128 ? 128 : (int)round_up(groups, 32);
+  dim3 grid((unsigned)ceil_div(groups, threads), (unsigned)(M < 65535 ? M : 65535));
+  k_combine<<<grid, threads, 0, (cudaStream_t)stream>>>(pc, sp, ep, sdtype, M, (int)Dm, y, ydtype, vec);
   return check_launch("combine");
 }
