@@ -31,7 +31,7 @@ struct LocalEntParams {
 // the tile (k with a W-1 halo) in shared memory, then the normalised ternary window weights.
 template <int W>
 __device__ __forceinline__ void local_front(const LocalEntParams &p, float *qs, float *ks, float *tw, float *invf,
-                                            int64_t row0, int t0, int nt) {
+                                            int64_t row0, int t0, int nt, float2 *tw2 = nullptr) {
   const int R = p.R, RP = R + 1;
   for (int i = threadIdx.x; i < R / 2; i += blockDim.x) invf[i] = rope_inv_freq(i, R, p.rope_base);
   __syncthreads();
@@ -49,6 +49,47 @@ __device__ __forceinline__ void local_front(const LocalEntParams &p, float *qs, 
   __syncthreads();
   window_scores<W>(qs, ks, RP, R, nt, t0, p.bias, p.sqrt_r, p.thr, tw, [](int gt, int o) { return gt - o >= 0; });
   __syncthreads();
+  if (tw2) {  // each weight duplicated into both halves of a float2, for the packed FMAs
+    for (int i = threadIdx.x; i < nt * W; i += blockDim.x) tw2[i] = make_float2(tw[i], tw[i]);
+    __syncthreads();
+  }
+}
+
+// Two channels per thread (D even): the same sums as local_channels, in the same order, with
+// packed fp32 FMAs (FFMA2) on float2 state pairs and duplicated weights, so each weight load
+// and each instruction serves two channels.  emit(t, d2, ent.x, ent.y, s.x, s.y).
+template <int W, class Emit>
+__device__ __forceinline__ void local_channels2(const LocalEntParams &p, const float2 *tw2, int64_t row0, int t0,
+                                                int nt, Emit emit) {
+  constexpr int TB = 8;
+  const int D2 = p.D >> 1;
+  const int nblk = (nt + TB - 1) / TB;
+  const float2 *st2 = reinterpret_cast<const float2 *>(p.states);
+  for (int item = threadIdx.x; item < nblk * D2; item += blockDim.x) {
+    const int tbi = item / D2, d2 = item - tbi * D2, tb = tbi * TB;
+    float2 win[TB + W - 1];  // win[i] = states[t0 + tb - (W-1) + i][2*d2 .. 2*d2+1]
+#pragma unroll
+    for (int i = 0; i < TB + W - 1; ++i) {
+      const int j = t0 + tb - (W - 1) + i;
+      win[i] = (j >= 0 && j < t0 + nt) ? st2[(row0 + j) * D2 + d2] : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < TB; ++k) {
+      const int t = tb + k;
+      if (t < nt) {
+        const float4 *wr = reinterpret_cast<const float4 *>(tw2 + t * W);
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < W / 2; ++q) {
+          const float4 w = wr[q];  // (w[2q], w[2q], w[2q+1], w[2q+1])
+          acc = __ffma2_rn(make_float2(w.x, w.y), win[k + W - 1 - 2 * q], acc);
+          acc = __ffma2_rn(make_float2(w.z, w.w), win[k + W - 2 - 2 * q], acc);
+        }
+        const float2 s = win[k + W - 1];
+        emit(t, d2, s.x + p.es * (acc.x - s.x), s.y + p.es * (acc.y - s.y), s.x, s.y);
+      }
+    }
+  }
 }
 
 // Output (t, d) depends only on states[t-W+1..t][d] and the weights of row t (no recurrence
@@ -92,15 +133,32 @@ __global__ void __launch_bounds__(256, 2) k_siso_local_ent(LocalEntParams p) {
   float *ks = qs + T * RP;           // (T + W - 1) x RP
   float *tw = ks + (T + W - 1) * RP; // T x W ternary / norm
   float *invf = tw + T * W;          // R / 2
+  // T x W duplicated weights, 16-byte aligned for the float4 reads
+  float2 *tw2 = reinterpret_cast<float2 *>((reinterpret_cast<uintptr_t>(invf + R / 2) + 15) & ~(uintptr_t)15);
   const int b = blockIdx.y, t0 = blockIdx.x * T;
   const int64_t row0 = (int64_t)b * p.L;
   const int nt = min(T, p.L - t0);
-  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt);
-  local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
-    const int64_t o = (row0 + t0 + t) * p.D + d;
-    store_f(p.out_tanh, p.out_dtype, o, th);
-    store_f(p.out_chg, p.out_dtype, o, ch);
-  });
+  const bool pairs = (p.D & 1) == 0;
+  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt, pairs ? tw2 : nullptr);
+  if (pairs) {
+    local_channels2<W>(p, tw2, row0, t0, nt, [&](int t, int d2, float ex, float ey, float sx, float sy) {
+      const int64_t o = (row0 + t0 + t) * p.D + 2 * d2;
+      const float tx = tanhf(ex), ty = tanhf(ey), cx = ex - sx, cy = ey - sy;
+      if (p.out_dtype == TESM_BF16) {
+        reinterpret_cast<__nv_bfloat162 *>(p.out_tanh)[o >> 1] = __floats2bfloat162_rn(tx, ty);
+        reinterpret_cast<__nv_bfloat162 *>(p.out_chg)[o >> 1] = __floats2bfloat162_rn(cx, cy);
+      } else {
+        reinterpret_cast<float2 *>(p.out_tanh)[o >> 1] = make_float2(tx, ty);
+        reinterpret_cast<float2 *>(p.out_chg)[o >> 1] = make_float2(cx, cy);
+      }
+    });
+  } else {
+    local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
+      const int64_t o = (row0 + t0 + t) * p.D + d;
+      store_f(p.out_tanh, p.out_dtype, o, th);
+      store_f(p.out_chg, p.out_dtype, o, ch);
+    });
+  }
 }
 
 // Same computation, but the two outputs go straight to int8: the per-token codes of tanh(ent)
@@ -130,15 +188,27 @@ __global__ void __launch_bounds__(256, 2) k_siso_local_ent_codes(LocalEntCodesPa
   float *invf = tw + T * W;
   float *oT = invf + R / 2;    // T x (D+1)
   float *oC = oT + T * DP1;    // T x (D+1)
+  // T x W duplicated weights, 16-byte aligned for the float4 reads
+  float2 *tw2 = reinterpret_cast<float2 *>((reinterpret_cast<uintptr_t>(oC + T * DP1) + 15) & ~(uintptr_t)15);
   const int b = blockIdx.y, t0 = blockIdx.x * T;
   const int64_t row0 = (int64_t)b * p.L;
   const int nt = min(T, p.L - t0);
   const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt);
-  local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
-    oT[t * DP1 + d] = round_to(pp.act_dtype, th);
-    oC[t * DP1 + d] = round_to(pp.act_dtype, ch);
-  });
+  const bool pairs = (D & 1) == 0;
+  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt, pairs ? tw2 : nullptr);
+  if (pairs) {
+    local_channels2<W>(p, tw2, row0, t0, nt, [&](int t, int d2, float ex, float ey, float sx, float sy) {
+      oT[t * DP1 + 2 * d2] = round_to(pp.act_dtype, tanhf(ex));
+      oT[t * DP1 + 2 * d2 + 1] = round_to(pp.act_dtype, tanhf(ey));
+      oC[t * DP1 + 2 * d2] = round_to(pp.act_dtype, ex - sx);
+      oC[t * DP1 + 2 * d2 + 1] = round_to(pp.act_dtype, ey - sy);
+    });
+  } else {
+    local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
+      oT[t * DP1 + d] = round_to(pp.act_dtype, th);
+      oC[t * DP1 + d] = round_to(pp.act_dtype, ch);
+    });
+  }
   __syncthreads();
   // per-token quantisation: one warp per (row, output)
   for (int item = warp; item < 2 * nt; item += nwarp) {
@@ -333,7 +403,7 @@ using namespace tesm;
 template <int W>
 static int launch_local(LocalEntParams &p, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
-                                       p.R / 2);
+                                       p.R / 2 + 2 * (size_t)p.T * W + 4);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
@@ -386,7 +456,7 @@ template <int W>
 static int launch_local_codes(LocalEntCodesParams &pp, cudaStream_t st) {
   const LocalEntParams &p = pp.e;
   const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
-                                       p.R / 2 + 2 * (size_t)p.T * (p.D + 1));
+                                       p.R / 2 + 2 * (size_t)p.T * (p.D + 1) + 4 + 2 * (size_t)p.T * W + 4);
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
