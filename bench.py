@@ -462,7 +462,7 @@ def _graph_time(fn, reps=10, inner=8):
     return statistics.median(ts)
 
 
-def run_cfg2(args, peaks):
+def run_cfg2(args, peaks, rank=0, world=1):
     """BitLinear INT2 microbench, per-tensor and per-row scales.  One call =
     activation quantisation + GEMV (M <= 64) or tensor-core GEMM; weights rotate over enough
     copies to exceed L2 so every call reads them from HBM."""
@@ -492,7 +492,7 @@ def run_cfg2(args, peaks):
     return out
 
 
-def run_cfg3(args, peaks):
+def run_cfg3(args, peaks, rank=0, world=1):
     """standalone SISO scan + local entanglement (+ codes) + global entanglement
     + fused output GEMM at batch 8 x 8192, d_state 256, d_model 2048, window 16, ent_rank 64.
     Synthetic in_proj output: decay pre-activation ~ N(0,1) with decay_bias 0 (a = sigmoid(N(0,1))),
@@ -501,6 +501,9 @@ def run_cfg3(args, peaks):
     from tesm_b200 import ops
     torch.manual_seed(0)
     B, L, D, Dm, R, W = 8, 8192, 256, 2048, 64, 16
+    if B % world:
+        raise SystemExit(f"config 3 splits its batch of {B} over the ranks; {world} does not divide it")
+    B //= world  # this rank's sequences; byte / flop counts below are per rank, scaled by world
     M = B * L
     Np = 2 * Dm + 3 * D + 2 * R
     proj = torch.randn(M, Np, device="cuda").to(torch.bfloat16)
@@ -512,37 +515,42 @@ def run_cfg3(args, peaks):
     th = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
     ch = torch.empty_like(th)
     res = []
+
+    def rec(name, t, byts=None, flops=None, **extra):
+        t = _max_over_ranks(t, world)  # whole job: every rank's share, slowest rank's time
+        r = {"kernel": name, "ms": t * 1e3, "n_gpus": world}
+        if byts is not None:
+            r.update(GB_s=byts * world / t / 1e9, hbm_frac=byts / t / 1e9 / peaks["hbm_gbs"],
+                     algorithmic_bytes=byts * world)
+        if flops is not None:
+            r.update(TFLOPS=flops * world / t / 1e12, tensor_frac=flops / t / 1e12 / peaks["bf16_tflops"])
+        r.update(extra)
+        res.append(r)
+
     t = _graph_time(lambda i: ops.siso_scan(proj, B, L, Dm, D, R, db, None, states, f32, f64), inner=4)
-    byts = M * D * (3 * 2 + 4)  # decay, write, value bf16 in; fp32 states out
-    res.append({"kernel": "k_scan (SISO)", "ms": t * 1e3, "GB_s": byts / t / 1e9, "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"],
-                "algorithmic_bytes": byts})
+    rec("k_scan (SISO)", t, M * D * (3 * 2 + 4))  # decay, write, value bf16 in; fp32 states out
     t = _graph_time(lambda i: ops.siso_local_ent(proj, B, L, Dm, D, R, W, None, bias, states, 0.1, 0.2, 1e4, th, ch),
                     inner=4)
-    byts = M * (2 * R * 2 + D * 4 + 2 * D * 2)
-    res.append({"kernel": "k_siso_local_ent<16>", "ms": t * 1e3, "GB_s": byts / t / 1e9,
-                "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": byts})
+    rec("k_siso_local_ent<16>", t, M * (2 * R * 2 + D * 4 + 2 * D * 2))
     t = _graph_time(lambda i: ops.siso_local_ent_codes(proj, B, L, Dm, D, R, W, None, bias, states, 0.1, 0.2, 1e4,
                                                        torch.bfloat16, 1e-5, 1e-5), inner=4)
-    byts = M * (2 * R * 2 + D * 4 + 2 * D + 8)
-    res.append({"kernel": "k_siso_local_ent_codes<16> (int8 out)", "ms": t * 1e3, "GB_s": byts / t / 1e9,
-                "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": byts})
+    rec("k_siso_local_ent_codes<16> (int8 out)", t, M * (2 * R * 2 + D * 4 + 2 * D + 8))
     emb = torch.randn(64, device="cuda") * 0.02
     relb = ops.global_relbias(emb, 1.0, 0.0, L)
     fl = B * (L * L / 2) * (2 * R + 2 * D)  # algorithmic: causal half, q.k and t.v once each
     t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th, ch,
                                                   force="tc"), reps=5, inner=2)
-    res.append({"kernel": "k_global_ent_tc (tcgen05 kind::f16, incl. prep kernels)", "ms": t * 1e3,
-                "TFLOPS": fl / t / 1e12, "tensor_frac": fl / t / 1e12 / peaks["bf16_tflops"],
-                "note": "causal half counted once; the kernel issues 3 q.k (hi/lo) and 2 t.v (hi/lo) MMAs, "
-                        "2.2x the algorithmic flops at R=64, D=256"})
-    t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th, ch,
-                                                  force="simt"), reps=3, inner=1)
-    res.append({"kernel": "k_siso_global_ent (SIMT fp32, fallback for ent_rank > 64 / d_state > 256)",
-                "ms": t * 1e3, "TFLOPS": fl / t / 1e12})
+    rec("k_global_ent_tc (tcgen05 kind::f16, incl. prep kernels)", t, flops=fl,
+        note="causal half counted once; the kernel issues 3 q.k (hi/lo) and 2 t.v (hi/lo) MMAs, "
+             "2.2x the algorithmic flops at R=64, D=256")
+    if world == 1:
+        t = _graph_time(lambda i: ops.siso_global_ent(proj, B, L, Dm, D, R, None, relb, states, 0.1, 0.2, 1e4, th,
+                                                      ch, force="simt"), reps=3, inner=1)
+        rec("k_siso_global_ent (SIMT fp32, fallback for ent_rank > 64 / d_state > 256)", t, flops=fl)
     return res
 
 
-def run_cfg4(args, peaks):
+def run_cfg4(args, peaks, rank=0, world=1):
     """TESMMIMO_Optimized layer forward, batch 4 x 16384, d_model 2048, 16 heads,
     d_state 64, ent_rank 48, mimo_rank 4, window 16, bf16 activations, random init seed 0."""
     import torch
@@ -550,32 +558,77 @@ def run_cfg4(args, peaks):
     from tesm_b200.modules import TESMMIMO_Optimized
     torch.manual_seed(0)
     B, L = 4, 16384
+    if B % world:
+        raise SystemExit(f"config 4 splits its batch of {B} over the ranks (2 or 4 GPUs); "
+                         f"{world} does not divide it (the batch x head split is not built)")
+    B //= world
     with torch.device("cuda"):
         m = TESMMIMO_Optimized(d_model=2048, n_heads=16, d_state=64, entanglement_window=16, max_seq_len=L,
                                kernel_backend="b200").eval()
     x = torch.randn(B, L, 2048, device="cuda").to(torch.bfloat16)
     with torch.no_grad():
-        t = _graph_time(lambda i: m(x), reps=5, inner=2)
+        t = _max_over_ranks(_graph_time(lambda i: m(x), reps=5, inner=2), world)
         H, D, R, RM, Dm = 16, 64, 48, 4, 2048
         proj = torch.randn(B * L, 2 * Dm + 3 * H * D + 2 * H * R, device="cuda").to(torch.bfloat16)
         states = torch.empty(B * L, RM, H * D, device="cuda")
         f32 = torch.empty(B, H * D, device="cuda")
         f64 = torch.empty(B, H * D, device="cuda", dtype=torch.float64)
-        ts = _graph_time(lambda i: ops.mimo_scan(proj, B, L, Dm, H, D, R, RM, m.decay_bias.float().contiguous(),
-                                                   m.mimo_x.float().contiguous(), states, f32, f64), inner=2)
+        ts = _max_over_ranks(_graph_time(lambda i: ops.mimo_scan(proj, B, L, Dm, H, D, R, RM,
+                                                                 m.decay_bias.float().contiguous(),
+                                                                 m.mimo_x.float().contiguous(), states, f32, f64),
+                                         inner=2), world)
         th = torch.empty(B * L, H * D, device="cuda", dtype=torch.bfloat16)
         ch = torch.empty_like(th)
         bias = m.local_entanglement_bias.float().contiguous()
         mo = m.mimo_o.float().contiguous()
-        te = _graph_time(lambda i: ops.mimo_local_ent(proj, B, L, Dm, H, D, R, RM, 16, bias, mo, states, 0.5, 0.2, 1e4,
-                                                        True, th, ch), inner=2)
-    E = B * L * H * D
-    return [{"workload": "cfg4 MIMO layer", "tokens_per_s": B * L / t, "ms": t * 1e3},
-            {"kernel": "k_scan (MIMO, 4 ranks)", "ms": ts * 1e3, "GB_s": E * (6 + 16) / ts / 1e9,
-             "hbm_frac": E * (6 + 16) / ts / 1e9 / peaks["hbm_gbs"], "algorithmic_bytes": E * 22},
-            {"kernel": "k_mimo_local_ent<16,4>", "ms": te * 1e3, "GB_s": (E * (16 + 4) + B * L * H * R * 4) / te / 1e9,
-             "hbm_frac": (E * (16 + 4) + B * L * H * R * 4) / te / 1e9 / peaks["hbm_gbs"],
-             "algorithmic_bytes": E * 20 + B * L * H * R * 4}]
+        te = _max_over_ranks(_graph_time(lambda i: ops.mimo_local_ent(proj, B, L, Dm, H, D, R, RM, 16, bias, mo,
+                                                                      states, 0.5, 0.2, 1e4, True, th, ch),
+                                         inner=2), world)
+    E = B * L * H * D * world  # whole job
+    ent_bytes = E * (16 + 4) + B * world * L * H * R * 4
+    return [{"workload": "cfg4 MIMO layer", "n_gpus": world, "tokens_per_s": B * world * L / t, "ms": t * 1e3},
+            {"kernel": "k_scan (MIMO, 4 ranks)", "n_gpus": world, "ms": ts * 1e3, "GB_s": E * (6 + 16) / ts / 1e9,
+             "hbm_frac": E * (6 + 16) / ts / 1e9 / world / peaks["hbm_gbs"], "algorithmic_bytes": E * 22},
+            {"kernel": "k_mimo_local_ent<16,4>", "n_gpus": world, "ms": te * 1e3, "GB_s": ent_bytes / te / 1e9,
+             "hbm_frac": ent_bytes / te / 1e9 / world / peaks["hbm_gbs"], "algorithmic_bytes": ent_bytes}]
+
+
+def run_workload(args):
+    """Supplementary configs.  Under torchrun (WORLD_SIZE > 1) configs 3 and 4 shard their batch
+    over the ranks (the split BASELINE names for them; no collective on the data path): every
+    rank runs batch / world sequences, each time is the max over ranks, and throughputs are for
+    the whole job (strong scaling: the total batch is fixed)."""
+    import torch
+    peaks, _ = load_peaks()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
+    try:
+        fn = {"cfg2": run_cfg2, "cfg3": run_cfg3, "cfg4": run_cfg4}[args.workload]
+        if world > 1 and args.workload == "cfg2":
+            raise SystemExit("config 2 is a single-GPU microbenchmark (replicas only)")
+        recs = fn(args, peaks, rank, world)
+        if rank == 0:
+            for rec in recs:
+                print(json.dumps(rec), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+def _max_over_ranks(t, world):
+    if world == 1:
+        return t
+    import torch
+    import torch.distributed as dist
+    x = torch.tensor([t], device="cuda", dtype=torch.float64)
+    dist.all_reduce(x, op=dist.ReduceOp.MAX)
+    return x.item()
 
 
 def main():
@@ -590,11 +643,7 @@ def main():
     ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine"], help="run a small ncu case")
     args = ap.parse_args()
     if args.workload:
-        peaks, _ = load_peaks()
-        fn = {"cfg2": run_cfg2, "cfg3": run_cfg3, "cfg4": run_cfg4}[args.workload]
-        for rec in fn(args, peaks):
-            print(json.dumps(rec), flush=True)
-        return 0
+        return run_workload(args)
     if args.kernel == "decode":
         return run_decode_case(args)
     if args.kernel == "combine":
