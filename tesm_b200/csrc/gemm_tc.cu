@@ -854,9 +854,9 @@ extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, c
                                         const int8_t *tern, int64_t ld_tern, const float *w_deq, int64_t M, int64_t F,
                                         int64_t K, void *out, int out_dtype, int64_t ldo, int32_t *splitk_ws,
                                         int64_t ws_bytes, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(codes && inv_scale && tern && w_deq && out, "gemm_i8_swiglu: null pointer");
   TESM_REQUIRE(M >= 0 && F > 0 && F % 128 == 0 && K > 0 && M < (1ll << 31), "gemm_i8_swiglu: need F % 128 == 0");
-  if (M == 0) return TESM_OK;
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_swiglu: out dtype");
   TESM_REQUIRE(ld_codes >= K && ld_codes % 16 == 0 && ((uintptr_t)codes & 15) == 0, "gemm_i8_swiglu: codes layout");
   TESM_REQUIRE(ld_tern >= K && ld_tern % 16 == 0 && ((uintptr_t)tern & 15) == 0, "gemm_i8_swiglu: tern layout");
@@ -887,10 +887,10 @@ extern "C" int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, 
                                          const float *deq2, const void *proj, int proj_dtype, int64_t ldp,
                                          int64_t c_local, int64_t c_gate, int64_t M, int64_t N, void *out,
                                          int out_dtype, int64_t ldo, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(codes && inv1 && inv2 && tern && deq1 && deq2 && proj && out, "gemm_i8_combine: null pointer");
   TESM_REQUIRE(M >= 0 && N > 0 && Kh > 0 && Kh % 128 == 0 && M < (1ll << 31), "gemm_i8_combine: need Kh % 128 == 0");
   TESM_REQUIRE(Kh <= 16384, "gemm_i8_combine: d_state above 16384");
-  if (M == 0) return TESM_OK;
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_combine: out dtype");
   if (proj_dtype != TESM_F32 && proj_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8_combine: proj dtype");
   TESM_REQUIRE(ld_codes >= 2 * Kh && ld_codes % 16 == 0 && ((uintptr_t)codes & 15) == 0, "gemm_i8_combine: codes");
@@ -925,9 +925,9 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
                                  int64_t ld_tern, const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K,
                                  void *out, int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc,
                                  int32_t *splitk_ws, int64_t ws_bytes, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(codes && inv_scale && tern && w_deq && (out || acc_out), "gemm_i8: null pointer");
-  TESM_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31), "gemm_i8: bad shape");
-  if (M == 0) return TESM_OK;
+  TESM_REQUIRE(M > 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31), "gemm_i8: bad shape");
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_i8: out dtype");
   TESM_REQUIRE(ld_codes >= K && ld_codes % 16 == 0 && ((uintptr_t)codes & 15) == 0,
                "gemm_i8: codes rows must be 16-byte aligned with ld_codes >= K");
@@ -976,9 +976,9 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
 extern "C" int tesm_b200_acc_scale(const int32_t *acc, int64_t M, int64_t N, const float *inv_scale,
                                    const float *w_deq, int per_row, void *out, int out_dtype, int64_t ldo,
                                    tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(acc && inv_scale && w_deq && out, "acc_scale: null pointer");
   TESM_REQUIRE(M >= 0 && N > 0 && ldo >= N && M * N < (1ll << 40), "acc_scale: bad shape");
-  if (M == 0) return TESM_OK;
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "acc_scale: out dtype");
   const int64_t n = M * N;
   tc::k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(

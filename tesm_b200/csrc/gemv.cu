@@ -225,9 +225,9 @@ extern "C" int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const 
                                    const float *w_deq, int per_row, int64_t M, int64_t N, int64_t K, void *out,
                                    int out_dtype, int64_t ldo, int32_t *acc_out, int64_t ld_acc,
                                    tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(codes && inv_scale && rowsum && packed && w_deq && out, "gemv_int2: null pointer");
-  TESM_REQUIRE(M >= 0 && M <= 64 && N > 0 && K > 0, "gemv_int2: need 0 <= M <= 64, N > 0, K > 0");
-  if (M == 0) return TESM_OK;
+  TESM_REQUIRE(M > 0 && M <= 64 && N > 0 && K > 0, "gemv_int2: need 0 <= M <= 64, N > 0, K > 0");
   TESM_REQUIRE(N < (1ll << 31), "gemv_int2: N too large");
   if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemv_int2: out dtype");
   const int64_t Kp = round_up(K, 256);

@@ -167,8 +167,8 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
                                            const float *weight, float eps, int64_t M, int64_t K, float qeps,
                                            int8_t *codes, int64_t ld_codes, int layout, float *inv_scale,
                                            int32_t *rowsum, void *y_out, int ydtype, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(x && weight && M >= 0 && K > 0, "add_rmsnorm_quant: bad argument");
-  if (M == 0) return TESM_OK;
   int64_t groups_out = ceil_div(K, 16);
   if (codes) {
     TESM_REQUIRE(inv_scale && ((uintptr_t)codes & 15) == 0 && ld_codes % 16 == 0, "add_rmsnorm_quant: codes");
@@ -199,9 +199,9 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
 
 extern "C" int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, int64_t blk, void *out,
                                   int odtype, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(blk == 0 || F % blk == 0, "silu_mul: F must be a multiple of the interleave block");
   TESM_REQUIRE(gu && out && M >= 0 && F > 0, "silu_mul: bad argument");
-  if (M == 0) return TESM_OK;
   TESM_REQUIRE(blk == 0 || blk % 8 == 0, "silu_mul: interleave block must be a multiple of 8");
   const int gsz = dtype == TESM_BF16 ? 2 : 4, osz = odtype == TESM_BF16 ? 2 : 4;
   const int vec = (F % 8 == 0) && ((uintptr_t)gu % 16 == 0) && ((uintptr_t)out % 16 == 0) && ((F * gsz) % 16 == 0) &&

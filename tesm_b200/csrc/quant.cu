@@ -199,9 +199,9 @@ extern "C" int tesm_b200_pack_ternary(const void *w, int dtype, int64_t N, int64
 static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
                           const float *amax, int8_t *codes, int64_t ld_codes, int layout, float *inv_scale,
                           int32_t *rowsum, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(x && codes && inv_scale, "quant_act: null pointer");
-  TESM_REQUIRE(M >= 0 && K > 0 && ldx >= K, "quant_act: bad shape");
-  if (M == 0) return TESM_OK;
+  TESM_REQUIRE(M > 0 && K > 0 && ldx >= K, "quant_act: bad shape");
   if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "quant_act: dtype must be f32 or bf16");
   TESM_REQUIRE(((uintptr_t)codes & 15) == 0 && ld_codes % 16 == 0, "quant_act: codes must be 16-byte aligned rows");
   int64_t groups_out;
@@ -245,8 +245,8 @@ extern "C" int tesm_b200_quant_act_amax(const void *x, int dtype, int64_t M, int
 
 extern "C" int tesm_b200_row_absmax(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float *amax,
                                     tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(x && amax && M >= 0 && K > 0 && ldx >= K, "row_absmax: bad argument");
-  if (M == 0) return TESM_OK;
   if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "row_absmax: dtype must be f32 or bf16");
   const int esz = dtype == TESM_BF16 ? 2 : 4;
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);

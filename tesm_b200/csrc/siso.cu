@@ -601,8 +601,8 @@ extern "C" int tesm_b200_mimo_global_ent(const void *proj, int dtype, int64_t ld
 extern "C" int tesm_b200_combine(const void *proj, int dtype, int64_t ldp, int64_t M, int64_t Dm, int64_t D,
                                  int64_t R, const void *sp, const void *ep, int sdtype, void *y, int ydtype,
                                  tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;  // empty batch: nothing to do (its buffers may be null)
   TESM_REQUIRE(proj && sp && ep && y && M >= 0 && Dm > 0, "combine: bad argument");
-  if (M == 0) return TESM_OK;
   ProjCols pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
   const int64_t n = M * Dm;
   const int psz = dtype == TESM_BF16 ? 2 : 4, ssz = sdtype == TESM_BF16 ? 2 : 4, ysz = ydtype == TESM_BF16 ? 2 : 4;
