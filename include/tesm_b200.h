@@ -91,6 +91,19 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
  * SMs (decode batches), K is split across up to 8 CTAs per tile; each split stores its int32
  * partial tile into its own M*N slice of the workspace and a finalize kernel sums the slices in a
  * fixed order (exact integers, deterministic).  The split count is capped so S*M*N*4 <= ws_bytes. */
+/* tesm_b200_decode_step for one SISO layer (H = 1) with the per-token int8 codes of tanh(ent) and
+ * ent - s as outputs instead of the values (tesm.py:1385-1396 then BitLinear.quantized_input
+ * tesm.py:206-209 of state_proj / ent_proj): codes (B x ldc, ldc >= 2*Dp, Dp = D rounded up to
+ * 128) hold the tanh codes in [0, D) and the change codes in [Dp, Dp + D), zero padded, ready
+ * for tesm_b200_gemm_i8_combine; inv1 / inv2 receive 1/s per token.  The values are rounded to
+ * act_dtype before quantisation, like the unfused path. */
+int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t Dm, int64_t D,
+                                     int64_t R, int64_t W, const float *decay_bias, const float *bias,
+                                     const float *cross, double *state, float *k_cache, float *v_cache, int *ctl,
+                                     float thr, float es, float rope_base, int act_dtype, float eps1, float eps2,
+                                     int8_t *codes, int64_t ldc, int64_t Dp, float *inv1, float *inv2,
+                                     float *new_state, tesm_stream_t stream);
+
 /* Tensor-parallel pieces of the row-parallel BitLinear (down_proj / out_proj split along K over
  * ranks; no counterpart in the reference, which runs on one device):
  * tesm_b200_row_absmax: amax[m] = max_k |x[m,k]| of this rank's K-shard (the caller reduces it

@@ -43,6 +43,9 @@ SIGNATURES = {
     "tesm_b200_global_relbias": [c_vp, c_i64, c_float, c_float, c_i64, c_vp, c_vp],
     "tesm_b200_siso_global_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
                                   c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp],
+    "tesm_b200_siso_decode_step_codes": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                                         c_vp, c_vp, c_vp, c_vp, c_float, c_float, c_float, c_int, c_float,
+                                         c_float, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp],
     "tesm_b200_row_absmax": [c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp],
     "tesm_b200_quant_act_amax": [c_vp, c_int, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_i64, c_int, c_vp, c_vp,
                                  c_vp],

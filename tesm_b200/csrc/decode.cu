@@ -12,6 +12,7 @@
 // the last CTA to finish advances them (every CTA reads them before it increments the
 // completion counter, so no CTA can observe the advanced values).
 #include "layer_common.cuh"
+#include "rowio.cuh"
 
 namespace tesm {
 
@@ -29,6 +30,14 @@ struct DecodeParams {
   void *out_tanh, *out_chg;   // (B, H*D)
   int out_dtype;
   float *new_state;           // (B, H*D) fp32 (cross-layer state for the next layer)
+  // codes mode (SISO, one block per row): instead of tanh(ent) / ent - s, their per-token int8
+  // codes (values first rounded to act_dtype, as the BitLinear input quantiser sees them) in
+  // the combine GEMM's A layout: tanh codes in [0, D), change codes in [Dp, Dp + D)
+  int8_t *codes;
+  int64_t ldc;
+  int Dp, act_dtype;
+  float eps1, eps2;
+  float *inv1, *inv2;
 };
 
 __global__ void k_decode_step(DecodeParams p) {
@@ -90,16 +99,39 @@ __global__ void k_decode_step(DecodeParams p) {
     if (tid < W) tw[tid] = tw[tid] / fmaxf(cnt, 1.f);
   }
   __syncthreads();
+  float th = 0.f, cg = 0.f;  // this thread's channel (codes mode: d = tid, blockDim >= D)
   for (int d = tid; d < D; d += blockDim.x) {
     const int c = h * D + d;
     const float ns = (float)newd;
     float avg = 0.f;
     for (int w = 0; w < valid; ++w) avg = fmaf(tw[w], p.vc[(((int64_t)b * W + slot[w]) * H + h) * D + d], avg);
     const float ent = ns + p.es * (avg - ns);
-    store_f(p.out_tanh, p.out_dtype, row * C + c, tanhf(ent));
-    store_f(p.out_chg, p.out_dtype, row * C + c, ent - ns);
+    th = tanhf(ent);
+    cg = ent - ns;
+    if (!p.codes) {
+      store_f(p.out_tanh, p.out_dtype, row * C + c, th);
+      store_f(p.out_chg, p.out_dtype, row * C + c, cg);
+    }
     p.state[((int64_t)b * H + h) * D + d] = newd;
     if (p.new_state) p.new_state[row * C + c] = ns;
+  }
+  if (p.codes) {  // per-token int8 codes of both outputs over the row (H == 1)
+    __shared__ float red[32];
+    const bool in = tid < D;
+    th = round_to(p.act_dtype, in ? th : 0.f);
+    cg = round_to(p.act_dtype, in ? cg : 0.f);
+    const float a1 = block_reduce(fabsf(th), red, [](float x, float y) { return fmaxf(x, y); }, 0.f);
+    const float a2 = block_reduce(fabsf(cg), red, [](float x, float y) { return fmaxf(x, y); }, 0.f);
+    const float s1 = act_scale(a1, p.eps1, p.act_dtype), s2 = act_scale(a2, p.eps2, p.act_dtype);
+    int8_t *crow = p.codes + row * p.ldc;
+    for (int d = tid; d < p.Dp; d += blockDim.x) {  // zero padding up to Dp
+      crow[d] = d < D ? (int8_t)act_code(th, s1, p.act_dtype) : 0;
+      crow[p.Dp + d] = d < D ? (int8_t)act_code(cg, s2, p.act_dtype) : 0;
+    }
+    if (tid == 0) {
+      p.inv1[row] = __frcp_rn(s1);
+      p.inv2[row] = __frcp_rn(s2);
+    }
   }
   // completion: the last CTA advances (seq_pos, cache_idx)
   __syncthreads();
@@ -151,9 +183,59 @@ extern "C" int tesm_b200_decode_step(const void *proj, int dtype, int64_t ldp, i
   p.out_chg = out_chg;
   p.out_dtype = out_dtype;
   p.new_state = new_state;
+  p.codes = nullptr;
   const int threads = (int)round_up(D < 32 ? 32 : D, 32);
   const size_t smem = sizeof(float) * (2 * R + W) + sizeof(int) * W;
   dim3 grid((unsigned)H, (unsigned)B);
   k_decode_step<<<grid, threads, smem, (cudaStream_t)stream>>>(p);
   return check_launch("decode_step");
+}
+
+extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t Dm,
+                                                int64_t D, int64_t R, int64_t W, const float *decay_bias,
+                                                const float *bias, const float *cross, double *state,
+                                                float *k_cache, float *v_cache, int *ctl, float thr, float es,
+                                                float rope_base, int act_dtype, float eps1, float eps2,
+                                                int8_t *codes, int64_t ldc, int64_t Dp, float *inv1, float *inv2,
+                                                float *new_state, tesm_stream_t stream) {
+  TESM_REQUIRE(proj && decay_bias && bias && state && k_cache && v_cache && ctl && codes && inv1 && inv2,
+               "decode_step_codes: null pointer");
+  TESM_REQUIRE(B > 0 && D > 0 && D <= 1024 && R > 0 && R % 2 == 0 && W > 0 && W <= 32,
+               "decode_step_codes: bad shape (D <= 1024, W <= 32, even R)");
+  TESM_REQUIRE(Dp >= D && Dp % 128 == 0 && ldc >= 2 * Dp, "decode_step_codes: Dp must be D rounded up to 128");
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "decode_step_codes: dtype");
+  if (act_dtype != TESM_F32 && act_dtype != TESM_BF16) return fail(TESM_EDTYPE, "decode_step_codes: act dtype");
+  DecodeParams p;
+  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
+  p.decay_bias = decay_bias;
+  p.bias = bias;
+  p.cross = cross;
+  p.state = state;
+  p.kc = k_cache;
+  p.vc = v_cache;
+  p.ctl = ctl;
+  p.B = (int)B;
+  p.H = 1;
+  p.D = (int)D;
+  p.R = (int)R;
+  p.W = (int)W;
+  p.thr = thr;
+  p.es = es;
+  p.sqrt_r = (float)sqrt((double)R);
+  p.rope_base = rope_base;
+  p.out_tanh = p.out_chg = nullptr;
+  p.out_dtype = act_dtype;
+  p.new_state = new_state;
+  p.codes = codes;
+  p.ldc = ldc;
+  p.Dp = (int)Dp;
+  p.act_dtype = act_dtype;
+  p.eps1 = eps1;
+  p.eps2 = eps2;
+  p.inv1 = inv1;
+  p.inv2 = inv2;
+  const int threads = (int)round_up(D < 32 ? 32 : D, 32);
+  const size_t smem = sizeof(float) * (2 * R + W) + sizeof(int) * W;
+  k_decode_step<<<dim3(1, (unsigned)B), threads, smem, (cudaStream_t)stream>>>(p);
+  return check_launch("decode_step_codes");
 }

@@ -267,15 +267,19 @@ def siso_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     cross_bias = None
     if cross_layer_state is not None:
         cross_bias = linear(mod.cross_layer_q_proj, cross_layer_state.reshape(B, D).float(), torch.float32)
-    tanh_e = torch.empty(B, D, device=dev, dtype=act_dtype)
-    chg = torch.empty(B, D, device=dev, dtype=act_dtype)
     new_state = torch.empty(B, D, device=dev, dtype=torch.float32)
-    ops.decode_step(proj, B, Dm, 1, D, R, W, _param_cache(mod, "decay_bias"),
-                    _param_cache(mod, "local_entanglement_bias"), cross_bias, cache["state"], cache["ent_k_cache"],
-                    cache["ent_v_cache"], cache["_ctl"], mod.entanglement_threshold, mod.entanglement_scale,
-                    mod.rope_base, tanh_e, chg, new_state)
+    # the step emits the int8 codes of tanh(ent) | ent - s; state_proj, ent_proj and the combine
+    # then run as one dual-accumulator GEMM, as in prefill
+    codes, inv1, inv2, Dp = ops.siso_decode_step_codes(
+        proj, B, Dm, D, R, W, _param_cache(mod, "decay_bias"), _param_cache(mod, "local_entanglement_bias"),
+        cross_bias, cache["state"], cache["ent_k_cache"], cache["ent_v_cache"], cache["_ctl"],
+        mod.entanglement_threshold, mod.entanglement_scale, mod.rope_base, act_dtype, mod.state_proj.bit_eps,
+        mod.ent_proj.bit_eps, new_state)
     _advance_host(cache, W)
-    out = _tail(mod, proj, B, D, R, tanh_e, chg, act_dtype)
+    tern, deq1, deq2, _ = combine_weight(mod)
+    y = torch.empty(B, Dm, device=dev, dtype=act_dtype)
+    ops.gemm_combine(codes, Dp, inv1, inv2, tern, deq1, deq2, proj, 0, Dm + 3 * D, B, Dm, y)
+    out = _out_proj(mod, y, act_dtype)
     mod._last_cross_layer_state = new_state
     return out.view(B, 1, Dm), cache["state"].clone()
 

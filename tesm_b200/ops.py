@@ -350,6 +350,21 @@ def decode_step(proj, B, Dm, H, D, R, W, decay_bias, bias, cross, state, kc, vc,
               dtype_code(out_tanh.dtype), _ptr(new_state), _stream())
 
 
+def siso_decode_step_codes(proj, B, Dm, D, R, W, decay_bias, bias, cross, state, kc, vc, ctl, thr, es, base,
+                           act_dtype, eps1, eps2, new_state):
+    """One-token SISO step emitting the int8 codes of tanh(ent) | ent - s for the combine GEMM."""
+    Dp = round_up(D, 128)
+    codes = torch.empty(B, 2 * Dp, device=proj.device, dtype=torch.int8)
+    inv1 = torch.empty(B, device=proj.device, dtype=torch.float32)
+    inv2 = torch.empty(B, device=proj.device, dtype=torch.float32)
+    _lib.call("tesm_b200_siso_decode_step_codes", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, Dm, D,
+              R, W, decay_bias.data_ptr(), bias.data_ptr(), _ptr(cross), state.data_ptr(), kc.data_ptr(),
+              vc.data_ptr(), ctl.data_ptr(), float(thr), float(es), float(base), dtype_code(act_dtype), float(eps1),
+              float(eps2), codes.data_ptr(), codes.stride(0), Dp, inv1.data_ptr(), inv2.data_ptr(), _ptr(new_state),
+              _stream())
+    return codes, inv1, inv2, Dp
+
+
 def embed(ids, emb, pos_emb, pos_dev, pos_host, out):
     B, L = ids.shape
     _lib.call("tesm_b200_embed", ids.data_ptr(), B, L, emb.data_ptr(), pos_emb.data_ptr(), dtype_code(emb.dtype),
