@@ -256,6 +256,238 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
   }
 }
 
+// SISO scan with the chunk held in registers.  A CTA covers SLICE2 = 256 channels x G*TT
+// positions: thread (g, cp) owns channels c0 + 2cp, c0 + 2cp + 1 (one bf16x2 load per column per
+// position) over positions g*TT .. g*TT+TT-1 of the chunk.  All 3*TT loads of a thread are issued
+// before any use, a and u are formed in registers, the G time groups combine their affine maps
+// through shared memory, and CTAs chain by the same decoupled look-back as k_scan.
+constexpr int SLICE2 = 256;
+
+#ifdef TESM_SCAN_TRACE  // development-only per-CTA phase timestamps (globaltimer ns)
+__device__ unsigned long long g_scan_trace[8192][8];
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define SCAN_MARK(k, v) \
+  if (threadIdx.x == 0 && tile < 8192) g_scan_trace[tile][k] = (v);
+#else
+#define SCAN_MARK(k, v)
+#endif
+
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];\n" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+// a = sigmoid(d + bias) = 1 / (1 + 2^(-(d + bias) log2 e)); nbias = -bias log2 e.
+// Relative error a few ulp (approximate 2^x and 1/x instructions).
+__device__ __forceinline__ float decay_gate(float d, float nbias) {
+  return rcp_approx(1.f + ex2_approx(fmaf(d, -kLog2e, nbias)));
+}
+// u = sigmoid(w) tanh(v) = (e^(2v) - 1) / ((1 + e^(-w)) (1 + e^(2v))), one reciprocal; v is
+// clamped to +-15 (tanh(15) rounds to 1 in fp32) so e^(2v) stays finite.  Absolute error a few
+// 1e-7 (the difference e^(2v) - 1 near v = 0 carries the exponential's rounding).
+__device__ __forceinline__ float write_value(float w, float v) {
+  v = fminf(fmaxf(v, -15.f), 15.f);
+  const float e1 = ex2_approx(w * -kLog2e), e2 = ex2_approx(v * (2.f * kLog2e));
+  return (e2 - 1.f) * rcp_approx((1.f + e1) * (1.f + e2));
+}
+
+template <int TT, int G>
+__global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
+  constexpr int NT = 128 * G;
+  __shared__ float4 s_map[G][128];  // per time group: (A0, A1, U0, U1)
+  __shared__ float2 s_carry[128];   // carry entering the chunk
+  __shared__ int s_tile, s_jinc;
+  if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1);
+  __syncthreads();
+  const int tile = s_tile;
+  const int per_chunk = p.B * p.nslices;
+  const int chunk = tile / per_chunk;
+  const int bs = tile - chunk * per_chunk;
+  const int b = bs / p.nslices, slice = bs - b * p.nslices;
+  const int g = threadIdx.x >> 7, cp = threadIdx.x & 127;
+  SCAN_MARK(0, gtimer());
+  const int c = slice * SLICE2 + 2 * cp;
+  const bool active = c < p.C;  // C even: both channels or neither
+  const int t0 = chunk * (G * TT) + g * TT;
+  const int64_t row0 = (int64_t)b * p.L;
+  const __nv_bfloat16 *proj = reinterpret_cast<const __nv_bfloat16 *>(p.pc.proj);
+
+  uint32_t rd[TT], rw[TT], rv[TT];
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+    if (active && t0 + t < p.L) {
+      const __nv_bfloat16 *row = proj + (row0 + t0 + t) * p.pc.ld + c;
+      rd[t] = ldg_nc_u32(row + p.pc.c_decay);
+      rw[t] = ldg_nc_u32(row + p.pc.c_write);
+      rv[t] = ldg_nc_u32(row + p.pc.c_value);
+    } else {
+      rd[t] = 0x7f807f80u;  // +inf, +inf: a = 1 ...
+      rw[t] = 0;
+      rv[t] = 0;            // ... and u = 0: an identity step
+    }
+  }
+  float nb0 = 0.f, nb1 = 0.f;
+  if (active) {
+    nb0 = -kLog2e * p.decay_bias[c];
+    nb1 = -kLog2e * p.decay_bias[c + 1];
+  }
+  float a0[TT], a1[TT], u0[TT], u1[TT];
+  float A0 = 1.f, A1 = 1.f, U0 = 0.f, U1 = 0.f;
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+    a0[t] = decay_gate(bf16lo(rd[t]), nb0);
+    a1[t] = decay_gate(bf16hi(rd[t]), nb1);
+    u0[t] = write_value(bf16lo(rw[t]), bf16lo(rv[t]));
+    u1[t] = write_value(bf16hi(rw[t]), bf16hi(rv[t]));
+    U0 = fmaf(a0[t], U0, u0[t]);
+    U1 = fmaf(a1[t], U1, u1[t]);
+    A0 *= a0[t];
+    A1 *= a1[t];
+  }
+  // combine the time groups: exclusive map E of groups 0..g-1, total map of the chunk
+  s_map[g][cp] = make_float4(A0, A1, U0, U1);
+  __syncthreads();
+  SCAN_MARK(1, gtimer());
+  float EA0 = 1.f, EA1 = 1.f, EU0 = 0.f, EU1 = 0.f, TA0, TA1, TU0, TU1;
+#pragma unroll
+  for (int k = 0; k < G; ++k) {
+    const float4 m = s_map[k][cp];
+    if (k == g) {
+      TA0 = EA0, TA1 = EA1, TU0 = EU0, TU1 = EU1;  // save the exclusive map
+    }
+    EU0 = fmaf(m.x, EU0, m.z);
+    EU1 = fmaf(m.y, EU1, m.w);
+    EA0 *= m.x;
+    EA1 *= m.y;
+  }
+  // now (EA, EU) is the chunk's total map and (TA, TU) this group's exclusive map
+  int *flag_row = p.flags + ((int64_t)b * p.nslices + slice) * p.nchunks;
+  const int64_t cidx = ((int64_t)b * p.nchunks + chunk);
+  if (chunk > 0 && chunk + 1 < p.nchunks) {
+    if (g == 0 && active) {
+      *reinterpret_cast<float2 *>(p.aggA + cidx * p.C + c) = make_float2(EA0, EA1);
+      *reinterpret_cast<float2 *>(p.aggU + cidx * p.C + c) = make_float2(EU0, EU1);
+    }
+    __syncthreads();  // the CTA's stores, then one gpu-scope fence + release by thread 0
+    if (threadIdx.x == 0) {
+      __threadfence();
+      st_release(flag_row + chunk, 1);
+    }
+  }
+  SCAN_MARK(2, gtimer());
+  if (g == 0) {
+    float h0 = 0.f, h1 = 0.f;
+    if (active && p.h0) {
+      h0 = (float)p.h0[(int64_t)b * p.C + c];
+      h1 = (float)p.h0[(int64_t)b * p.C + c + 1];
+    }
+    if (chunk > 0) {
+      if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int base = chunk - 1, jinc = -1;
+        const long long start = clock64();
+        while (true) {
+          const int j = base - lane;
+          const int f = j >= 0 ? ld_acquire(flag_row + j) : 2;
+          const unsigned b2 = __ballot_sync(0xffffffffu, f == 2);
+          const unsigned b0 = __ballot_sync(0xffffffffu, f == 0);
+          const int first2 = b2 ? __ffs(b2) - 1 : 32, first0 = b0 ? __ffs(b0) - 1 : 32;
+          if (first2 < 32 && first2 < first0) {
+            jinc = base - first2;
+            break;
+          }
+          if (first0 == 32) {
+            base -= 32;
+            continue;
+          }
+          if (clock64() - start > kSpinLimit * 64) {
+            if (lane == 0) flag_timeout();
+            jinc = -2;
+            break;
+          }
+        }
+        if (lane == 0) s_jinc = jinc;
+      }
+      asm volatile("bar.sync 1, 128;\n" ::: "memory");  // group 0 only
+      const int jinc = s_jinc;
+      SCAN_MARK(3, gtimer());
+      SCAN_MARK(6, (unsigned long long)(chunk - jinc));
+      if (active && jinc >= 0) {
+        const int64_t ji = (int64_t)b * p.nchunks + jinc;
+        const float2 hi = *reinterpret_cast<const float2 *>(p.incl + ji * p.C + c);
+        h0 = hi.x, h1 = hi.y;
+        constexpr int FB = 8;
+        for (int j0 = jinc + 1; j0 < chunk; j0 += FB) {
+          float2 gA[FB], gU[FB];
+#pragma unroll
+          for (int k = 0; k < FB; ++k) {
+            const int j = j0 + k;
+            const int64_t jj = (int64_t)b * p.nchunks + (j < chunk ? j : jinc);
+            gA[k] = j < chunk ? *reinterpret_cast<const float2 *>(p.aggA + jj * p.C + c) : make_float2(1.f, 1.f);
+            gU[k] = j < chunk ? *reinterpret_cast<const float2 *>(p.aggU + jj * p.C + c) : make_float2(0.f, 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < FB; ++k) {
+            h0 = fmaf(gA[k].x, h0, gU[k].x);
+            h1 = fmaf(gA[k].y, h1, gU[k].y);
+          }
+        }
+      }
+    }
+    s_carry[cp] = make_float2(h0, h1);
+    if (chunk + 1 < p.nchunks && active)
+      *reinterpret_cast<float2 *>(p.incl + cidx * p.C + c) = make_float2(fmaf(EA0, h0, EU0), fmaf(EA1, h1, EU1));
+  }
+  __syncthreads();
+  if (chunk + 1 < p.nchunks && threadIdx.x == 0) {
+    __threadfence();
+    st_release(flag_row + chunk, 2);
+  }
+  SCAN_MARK(4, gtimer());
+  if (!active) return;
+  const float2 hin = s_carry[cp];
+  float h0 = fmaf(TA0, hin.x, TU0), h1 = fmaf(TA1, hin.y, TU1);
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+    if (t0 + t < p.L) {
+      h0 = fmaf(a0[t], h0, u0[t]);
+      h1 = fmaf(a1[t], h1, u1[t]);
+      __stcs(reinterpret_cast<float2 *>(p.states + (row0 + t0 + t) * p.C + c), make_float2(h0, h1));
+      if (t0 + t == p.L - 1) {
+        p.final_f32[(int64_t)b * p.C + c] = h0;
+        p.final_f32[(int64_t)b * p.C + c + 1] = h1;
+        p.final_f64[(int64_t)b * p.C + c] = (double)h0;
+        p.final_f64[(int64_t)b * p.C + c + 1] = (double)h1;
+      }
+    }
+  }
+#ifdef TESM_SCAN_TRACE
+  if (tile < 8192 && threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %smid;" : "=r"(smid));
+    g_scan_trace[tile][5] = gtimer();
+    g_scan_trace[tile][7] = smid;
+  }
+#endif
+}
+
 struct ScanLayout {
   int T, slice, nchunks, nslices;
   int64_t off_aggU, off_incl, off_flags, bytes;
@@ -271,6 +503,7 @@ static ScanLayout scan_layout(int64_t B, int64_t L, int64_t C, int64_t RM) {
   }
   if (force > 0) s.T = force;
   s.slice = C < 256 ? (int)round_up(C, 32) : 256;
+  if (RM == 1) s.slice = 256;  // the register-resident SISO kernel always covers 256 channels per CTA
   s.nchunks = (int)ceil_div(L, s.T);
   s.nslices = (int)ceil_div(C, s.slice);
   const int64_t nA = B * s.nchunks * C;
@@ -332,7 +565,36 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
   p.ticket = p.flags + B * s.nslices * s.nchunks;
   cudaError_t e = cudaMemsetAsync(p.flags, 0, (B * s.nslices * s.nchunks + 1) * sizeof(int), st);
   if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("scan memset: ") + cudaGetErrorString(e));
-  if (!mimo_x) return launch_scan<1, false>(p, st, s.slice);
+  if (!mimo_x) {
+    // register-resident kernel for bf16 projections with 4-byte aligned channel pairs
+    static int reg_mode = -1, reg_tt = 16;
+    if (reg_mode < 0) {
+      const char *e = getenv("TESM_SCAN_REG");  // tuning override: 0 = shared-memory kernel
+      reg_mode = e ? atoi(e) : 1;
+      if (const char *t = getenv("TESM_SCAN_TT")) reg_tt = atoi(t);  // positions per thread
+    }
+    const bool pairs = dtype == TESM_BF16 && (uintptr_t)proj % 4 == 0 && ldp % 2 == 0 && C % 2 == 0 &&
+                       p.pc.c_decay % 2 == 0 && p.pc.c_write % 2 == 0 && p.pc.c_value % 2 == 0 &&
+                       (uintptr_t)states % 8 == 0;
+    if (reg_mode && pairs) {
+      const int G = s.T / reg_tt;
+      const unsigned grid = (unsigned)((int64_t)p.nchunks * p.B * p.nslices);
+#define TESM_SCAN_REG_CASE(TT_, G_)                                              \
+  if (reg_tt == TT_ && G == G_) {                                                \
+    k_scan_siso_reg<TT_, G_><<<grid, 128 * G_, 0, st>>>(p);                      \
+    return check_launch("scan");                                                 \
+  }
+      TESM_SCAN_REG_CASE(16, 2)
+      TESM_SCAN_REG_CASE(16, 1)
+      TESM_SCAN_REG_CASE(16, 4)
+      TESM_SCAN_REG_CASE(8, 2)
+      TESM_SCAN_REG_CASE(8, 4)
+      TESM_SCAN_REG_CASE(32, 1)
+      TESM_SCAN_REG_CASE(32, 2)
+#undef TESM_SCAN_REG_CASE
+    }
+    return launch_scan<1, false>(p, st, s.slice);
+  }
   switch (RM) {
     case 1: return launch_scan<1, true>(p, st, s.slice);
     case 2: return launch_scan<2, true>(p, st, s.slice);
@@ -345,6 +607,12 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
 }  // namespace tesm
 
 using namespace tesm;
+
+#ifdef TESM_SCAN_TRACE
+extern "C" int tesm_b200_scan_trace_read(unsigned long long *host) {
+  return cudaMemcpyFromSymbol(host, tesm::g_scan_trace, sizeof(tesm::g_scan_trace)) == cudaSuccess ? 0 : 3;
+}
+#endif
 
 extern "C" int tesm_b200_scan_workspace(int64_t B, int64_t L, int64_t C, int64_t RM, int64_t *bytes) {
   TESM_REQUIRE(bytes && B > 0 && L > 0 && C > 0 && RM > 0, "scan_workspace: bad argument");

@@ -42,11 +42,20 @@ def _ambiguous_rows(scores, thr, tol=2e-5):
     return amb.reshape(amb.shape[0], -1).any(-1) if amb.ndim > 1 else amb
 
 
-@pytest.mark.parametrize("B,L,D,h0", [(2, 200, 64, False), (3, 300, 300, True), (1, 7, 32, False),
-                                      (2, 4096, 256, True)])
-def test_siso_scan(ops, B, L, D, h0):
+@pytest.mark.parametrize("B,L,D,h0,dt", [(2, 200, 64, False, "f32"), (3, 300, 300, True, "f32"),
+                                         (1, 7, 32, False, "f32"), (2, 4096, 256, True, "f32"),
+                                         (2, 200, 64, False, "bf16"), (3, 300, 300, True, "bf16"),
+                                         (1, 7, 32, False, "bf16"), (2, 4096, 256, True, "bf16"),
+                                         (1, 1000, 520, False, "bf16")])
+def test_siso_scan(ops, B, L, D, h0, dt):
+    """fp32 projections take the shared-memory kernel, bf16 ones the register-resident kernel."""
     Dm, R = 32, 16
     P = _proj(B, L, Dm, D, R, 40 + D)
+    if dt == "bf16":
+        P = P.to(torch.bfloat16).float()  # the oracle sees the bf16 values
+        P_dev = P.to(torch.bfloat16).cuda()
+    else:
+        P_dev = P.cuda()
     db = torch.full((D,), 3.0) + randn((D,), 5) * 0.5
     prev = randn((B, D), 6).double() if h0 else None
     _, val, dec, wr, _, _, _ = _split(P.numpy(), Dm, D, R)
@@ -56,7 +65,7 @@ def test_siso_scan(ops, B, L, D, h0):
     st = torch.empty(B * L, D, device="cuda")
     f32 = torch.empty(B, D, device="cuda")
     f64 = torch.empty(B, D, device="cuda", dtype=torch.float64)
-    ops.siso_scan(P.cuda(), B, L, Dm, D, R, db.cuda(), prev.cuda() if h0 else None, st, f32, f64)
+    ops.siso_scan(P_dev, B, L, Dm, D, R, db.cuda(), prev.cuda() if h0 else None, st, f32, f64)
     assert ops.device_status() == 0
     assert max_rel(st.cpu().numpy().reshape(B, L, D), ref) <= 1e-5
     assert max_rel(f64.cpu().numpy(), fin) <= 1e-5
