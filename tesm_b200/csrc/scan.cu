@@ -294,6 +294,18 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 constexpr float kLog2e = 1.4426950408889634f;
+// carry words: gpu-scope relaxed accesses (L1 bypassed); 0xffffffff marks "not yet written"
+__device__ __forceinline__ void st_relaxed_f2(float *p, float x, float y) {
+  asm volatile("st.relaxed.gpu.global.v2.f32 [%0], {%1, %2};\n" ::"l"(p), "f"(x), "f"(y) : "memory");
+}
+__device__ __forceinline__ float2 ld_relaxed_f2(const float *p) {
+  float2 v;
+  asm volatile("ld.relaxed.gpu.global.v2.f32 {%0, %1}, [%2];\n" : "=f"(v.x), "=f"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool ready2(float2 v) {
+  return __float_as_uint(v.x) != 0xffffffffu && __float_as_uint(v.y) != 0xffffffffu;
+}
 // a = sigmoid(d + bias) = 1 / (1 + 2^(-(d + bias) log2 e)); nbias = -bias log2 e.
 // Relative error a few ulp (approximate 2^x and 1/x instructions).
 __device__ __forceinline__ float decay_gate(float d, float nbias) {
@@ -313,7 +325,7 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
   constexpr int NT = 128 * G;
   __shared__ float4 s_map[G][128];  // per time group: (A0, A1, U0, U1)
   __shared__ float2 s_carry[128];   // carry entering the chunk
-  __shared__ int s_tile, s_jinc;
+  __shared__ int s_tile;
   if (threadIdx.x == 0) s_tile = atomicAdd(p.ticket, 1);
   __syncthreads();
   const int tile = s_tile;
@@ -377,89 +389,67 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
     EA0 *= m.x;
     EA1 *= m.y;
   }
-  // now (EA, EU) is the chunk's total map and (TA, TU) this group's exclusive map
-  int *flag_row = p.flags + ((int64_t)b * p.nslices + slice) * p.nchunks;
+  // now (EA, EU) is the chunk's total map and (TA, TU) this group's exclusive map.
+  // Carry exchange without flags or fences: aggregate and inclusive words start as the
+  // all-ones NaN pattern (reset before the launch) and each channel's value is its own
+  // readiness signal.  Group 0 publishes, then walks back through its predecessors, K per
+  // round trip, folding aggregates until it meets an inclusive state.
   const int64_t cidx = ((int64_t)b * p.nchunks + chunk);
-  if (chunk > 0 && chunk + 1 < p.nchunks) {
-    if (g == 0 && active) {
-      *reinterpret_cast<float2 *>(p.aggA + cidx * p.C + c) = make_float2(EA0, EA1);
-      *reinterpret_cast<float2 *>(p.aggU + cidx * p.C + c) = make_float2(EU0, EU1);
-    }
-    __syncthreads();  // the CTA's stores, then one gpu-scope fence + release by thread 0
-    if (threadIdx.x == 0) {
-      __threadfence();
-      st_release(flag_row + chunk, 1);
-    }
-  }
-  SCAN_MARK(2, gtimer());
   if (g == 0) {
+    if (active && chunk > 0 && chunk + 1 < p.nchunks) {
+      st_relaxed_f2(p.aggA + cidx * p.C + c, EA0, EA1);
+      st_relaxed_f2(p.aggU + cidx * p.C + c, EU0, EU1);
+    }
+    SCAN_MARK(2, gtimer());
     float h0 = 0.f, h1 = 0.f;
     if (active && p.h0) {
       h0 = (float)p.h0[(int64_t)b * p.C + c];
       h1 = (float)p.h0[(int64_t)b * p.C + c + 1];
     }
-    if (chunk > 0) {
-      if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        int base = chunk - 1, jinc = -1;
-        const long long start = clock64();
-        while (true) {
-          const int j = base - lane;
-          const int f = j >= 0 ? ld_acquire(flag_row + j) : 2;
-          const unsigned b2 = __ballot_sync(0xffffffffu, f == 2);
-          const unsigned b0 = __ballot_sync(0xffffffffu, f == 0);
-          const int first2 = b2 ? __ffs(b2) - 1 : 32, first0 = b0 ? __ffs(b0) - 1 : 32;
-          if (first2 < 32 && first2 < first0) {
-            jinc = base - first2;
-            break;
-          }
-          if (first0 == 32) {
-            base -= 32;
-            continue;
-          }
-          if (clock64() - start > kSpinLimit * 64) {
-            if (lane == 0) flag_timeout();
-            jinc = -2;
-            break;
+    if (active && chunk > 0) {
+      constexpr int K = 4;
+      float FA0 = 1.f, FA1 = 1.f, FU0 = 0.f, FU1 = 0.f;  // fold of chunks (j, chunk)
+      int j = chunk - 1;
+      bool done = false;
+      const long long start = clock64();
+      while (!done) {
+        float2 inc[K], ga[K], gu[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const int64_t jj = (int64_t)b * p.nchunks + max(j - k, 0);
+          inc[k] = ld_relaxed_f2(p.incl + jj * p.C + c);
+          ga[k] = ld_relaxed_f2(p.aggA + jj * p.C + c);
+          gu[k] = ld_relaxed_f2(p.aggU + jj * p.C + c);
+        }
+        int next = j;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          if (done || next != j - k || j - k < 0) continue;
+          if (ready2(inc[k])) {
+            h0 = fmaf(FA0, inc[k].x, FU0);
+            h1 = fmaf(FA1, inc[k].y, FU1);
+            done = true;
+          } else if (ready2(ga[k]) && ready2(gu[k])) {
+            FU0 = fmaf(FA0, gu[k].x, FU0);
+            FU1 = fmaf(FA1, gu[k].y, FU1);
+            FA0 *= ga[k].x;
+            FA1 *= ga[k].y;
+            next = j - k - 1;
           }
         }
-        if (lane == 0) s_jinc = jinc;
-      }
-      asm volatile("bar.sync 1, 128;\n" ::: "memory");  // group 0 only
-      const int jinc = s_jinc;
-      SCAN_MARK(3, gtimer());
-      SCAN_MARK(6, (unsigned long long)(chunk - jinc));
-      if (active && jinc >= 0) {
-        const int64_t ji = (int64_t)b * p.nchunks + jinc;
-        const float2 hi = *reinterpret_cast<const float2 *>(p.incl + ji * p.C + c);
-        h0 = hi.x, h1 = hi.y;
-        constexpr int FB = 8;
-        for (int j0 = jinc + 1; j0 < chunk; j0 += FB) {
-          float2 gA[FB], gU[FB];
-#pragma unroll
-          for (int k = 0; k < FB; ++k) {
-            const int j = j0 + k;
-            const int64_t jj = (int64_t)b * p.nchunks + (j < chunk ? j : jinc);
-            gA[k] = j < chunk ? *reinterpret_cast<const float2 *>(p.aggA + jj * p.C + c) : make_float2(1.f, 1.f);
-            gU[k] = j < chunk ? *reinterpret_cast<const float2 *>(p.aggU + jj * p.C + c) : make_float2(0.f, 0.f);
-          }
-#pragma unroll
-          for (int k = 0; k < FB; ++k) {
-            h0 = fmaf(gA[k].x, h0, gU[k].x);
-            h1 = fmaf(gA[k].y, h1, gU[k].y);
-          }
+        j = next;
+        if (!done && clock64() - start > kSpinLimit * 64) {
+          flag_timeout();
+          break;
         }
       }
     }
+    SCAN_MARK(3, gtimer());
     s_carry[cp] = make_float2(h0, h1);
-    if (chunk + 1 < p.nchunks && active)
-      *reinterpret_cast<float2 *>(p.incl + cidx * p.C + c) = make_float2(fmaf(EA0, h0, EU0), fmaf(EA1, h1, EU1));
+    if (active && chunk + 1 < p.nchunks)
+      st_relaxed_f2(p.incl + cidx * p.C + c, fmaf(EA0, h0, EU0), fmaf(EA1, h1, EU1));
   }
   __syncthreads();
-  if (chunk + 1 < p.nchunks && threadIdx.x == 0) {
-    __threadfence();
-    st_release(flag_row + chunk, 2);
-  }
   SCAN_MARK(4, gtimer());
   if (!active) return;
   const float2 hin = s_carry[cp];
@@ -578,6 +568,8 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
                        (uintptr_t)states % 8 == 0;
     if (reg_mode && pairs) {
       const int G = s.T / reg_tt;
+      e = cudaMemsetAsync(workspace, 0xff, s.off_flags, st);  // carry words to "not yet written"
+      if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("scan memset: ") + cudaGetErrorString(e));
       const unsigned grid = (unsigned)((int64_t)p.nchunks * p.B * p.nslices);
 #define TESM_SCAN_REG_CASE(TT_, G_)                                              \
   if (reg_tt == TT_ && G == G_) {                                                \
