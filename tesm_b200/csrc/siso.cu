@@ -4,235 +4,13 @@
 // Layout: the in_proj output `proj` is (B*L, Nproj) row-major with the reference's
 // column split [local Dm | value D | decay D | write D | gate Dm | q R | k R]
 // (tesm.py:1195-1205); kernels read their columns in place through offsets.
-#include "layer_common.cuh"
+#include "window.cuh"
 #include "rowio.cuh"
+
+#include <algorithm>
 
 namespace tesm {
 
-
-// ---------------------------------------------------------------- local entanglement
-// For lag o in [0, W): j = t - o valid iff j >= 0, score = q_t.k_j / sqrt(R) + bias[W-1-o];
-// avg_t = sum tern * states_j / max(sum|tern|, 1); ent = s + es (avg - s)  (tesm.py:922-952,1231).
-// Outputs tanh(ent) and ent - s, the inputs of state_proj / ent_proj.
-struct LocalEntParams {
-  ProjCols pc;
-  const float *cross;  // (B*L, R) additive q bias, or null
-  const float *bias;   // (W) local_entanglement_bias (full parameter)
-  const float *states; // (B, L, D)
-  int B, L, D, R, W, T;
-  float thr, es, inv_sqrt_r_div, rope_base;
-  float sqrt_r;
-  void *out_tanh;      // (B*L, D)
-  void *out_chg;
-  int out_dtype;
-};
-
-// Shared front half of the local-entanglement kernels: RoPE'd q (+ cross bias) and k rows of
-// the tile (k with a W-1 halo) in shared memory, then the normalised ternary window weights.
-template <int W>
-__device__ __forceinline__ void local_front(const LocalEntParams &p, float *qs, float *ks, float *tw, float *invf,
-                                            int64_t row0, int t0, int nt, float2 *tw2 = nullptr) {
-  const int R = p.R, RP = R + 1;
-  for (int i = threadIdx.x; i < R / 2; i += blockDim.x) invf[i] = rope_inv_freq(i, R, p.rope_base);
-  __syncthreads();
-  const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < nt; r += nwarp) {
-    const int64_t row = row0 + t0 + r;
-    load_rope_row_tab(qs + r * RP, p.pc, p.pc.c_q, row, R, t0 + r, invf, p.cross ? p.cross + row * R : nullptr,
-                      lane, 32);
-  }
-  for (int r = warp; r < nt + W - 1; r += nwarp) {
-    const int pos = t0 - (W - 1) + r;
-    if (pos < 0) continue;
-    load_rope_row_tab(ks + r * RP, p.pc, p.pc.c_k, row0 + pos, R, pos, invf, nullptr, lane, 32);
-  }
-  __syncthreads();
-  window_scores<W>(qs, ks, RP, R, nt, t0, p.bias, p.sqrt_r, p.thr, tw, [](int gt, int o) { return gt - o >= 0; });
-  __syncthreads();
-  if (tw2) {  // each weight duplicated into both halves of a float2, for the packed FMAs
-    for (int i = threadIdx.x; i < nt * W; i += blockDim.x) tw2[i] = make_float2(tw[i], tw[i]);
-    __syncthreads();
-  }
-}
-
-// Two channels per thread (D even): the same sums as local_channels, in the same order, with
-// packed fp32 FMAs (FFMA2) on float2 state pairs and duplicated weights, so each weight load
-// and each instruction serves two channels.  emit(t, d2, ent.x, ent.y, s.x, s.y).
-template <int W, class Emit>
-__device__ __forceinline__ void local_channels2(const LocalEntParams &p, const float2 *tw2, int64_t row0, int t0,
-                                                int nt, Emit emit) {
-  constexpr int TB = 8;
-  const int D2 = p.D >> 1;
-  const int nblk = (nt + TB - 1) / TB;
-  const float2 *st2 = reinterpret_cast<const float2 *>(p.states);
-  for (int item = threadIdx.x; item < nblk * D2; item += blockDim.x) {
-    const int tbi = item / D2, d2 = item - tbi * D2, tb = tbi * TB;
-    float2 win[TB + W - 1];  // win[i] = states[t0 + tb - (W-1) + i][2*d2 .. 2*d2+1]
-#pragma unroll
-    for (int i = 0; i < TB + W - 1; ++i) {
-      const int j = t0 + tb - (W - 1) + i;
-      win[i] = (j >= 0 && j < t0 + nt) ? st2[(row0 + j) * D2 + d2] : make_float2(0.f, 0.f);
-    }
-#pragma unroll
-    for (int k = 0; k < TB; ++k) {
-      const int t = tb + k;
-      if (t < nt) {
-        const float4 *wr = reinterpret_cast<const float4 *>(tw2 + t * W);
-        float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int q = 0; q < W / 2; ++q) {
-          const float4 w = wr[q];  // (w[2q], w[2q], w[2q+1], w[2q+1])
-          acc = __ffma2_rn(make_float2(w.x, w.y), win[k + W - 1 - 2 * q], acc);
-          acc = __ffma2_rn(make_float2(w.z, w.w), win[k + W - 2 - 2 * q], acc);
-        }
-        const float2 s = win[k + W - 1];
-        emit(t, d2, s.x + p.es * (acc.x - s.x), s.y + p.es * (acc.y - s.y), s.x, s.y);
-      }
-    }
-  }
-}
-
-// Output (t, d) depends only on states[t-W+1..t][d] and the weights of row t (no recurrence
-// over t), so the work is split into independent items of TB consecutive timesteps x one
-// channel: each item loads its TB + W - 1 states at once (all in flight together) and emits
-// TB outputs.  emit(t, d, tanh_ent, chg) consumes them.
-template <int W, class Emit>
-__device__ __forceinline__ void local_channels(const LocalEntParams &p, const float *tw, int64_t row0, int t0, int nt,
-                                               Emit emit) {
-  constexpr int TB = 8;
-  const int D = p.D;
-  const int nblk = (nt + TB - 1) / TB;
-  for (int item = threadIdx.x; item < nblk * D; item += blockDim.x) {
-    const int tb = (item / D) * TB, d = item - (item / D) * D;
-    float win[TB + W - 1];  // win[i] = states[t0 + tb - (W-1) + i]
-#pragma unroll
-    for (int i = 0; i < TB + W - 1; ++i) {
-      const int j = t0 + tb - (W - 1) + i;
-      win[i] = (j >= 0 && j < t0 + nt) ? p.states[(row0 + j) * D + d] : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < TB; ++k) {
-      const int t = tb + k;
-      if (t < nt) {
-        const float s = win[k + W - 1];
-        float avg = 0.f;
-#pragma unroll
-        for (int o = 0; o < W; ++o) avg = fmaf(tw[t * W + o], win[k + W - 1 - o], avg);
-        const float ent = s + p.es * (avg - s);
-        emit(t, d, tanhf(ent), ent - s);
-      }
-    }
-  }
-}
-
-template <int W>
-__global__ void __launch_bounds__(256, 2) k_siso_local_ent(LocalEntParams p) {
-  extern __shared__ float sm[];
-  const int R = p.R, T = p.T, RP = R + 1;
-  float *qs = sm;                    // T x RP
-  float *ks = qs + T * RP;           // (T + W - 1) x RP
-  float *tw = ks + (T + W - 1) * RP; // T x W ternary / norm
-  float *invf = tw + T * W;          // R / 2
-  // T x W duplicated weights, 16-byte aligned for the float4 reads
-  float2 *tw2 = reinterpret_cast<float2 *>((reinterpret_cast<uintptr_t>(invf + R / 2) + 15) & ~(uintptr_t)15);
-  const int b = blockIdx.y, t0 = blockIdx.x * T;
-  const int64_t row0 = (int64_t)b * p.L;
-  const int nt = min(T, p.L - t0);
-  const bool pairs = (p.D & 1) == 0;
-  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt, pairs ? tw2 : nullptr);
-  if (pairs) {
-    local_channels2<W>(p, tw2, row0, t0, nt, [&](int t, int d2, float ex, float ey, float sx, float sy) {
-      const int64_t o = (row0 + t0 + t) * p.D + 2 * d2;
-      const float tx = tanhf(ex), ty = tanhf(ey), cx = ex - sx, cy = ey - sy;
-      if (p.out_dtype == TESM_BF16) {
-        reinterpret_cast<__nv_bfloat162 *>(p.out_tanh)[o >> 1] = __floats2bfloat162_rn(tx, ty);
-        reinterpret_cast<__nv_bfloat162 *>(p.out_chg)[o >> 1] = __floats2bfloat162_rn(cx, cy);
-      } else {
-        reinterpret_cast<float2 *>(p.out_tanh)[o >> 1] = make_float2(tx, ty);
-        reinterpret_cast<float2 *>(p.out_chg)[o >> 1] = make_float2(cx, cy);
-      }
-    });
-  } else {
-    local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
-      const int64_t o = (row0 + t0 + t) * p.D + d;
-      store_f(p.out_tanh, p.out_dtype, o, th);
-      store_f(p.out_chg, p.out_dtype, o, ch);
-    });
-  }
-}
-
-// Same computation, but the two outputs go straight to int8: the per-token codes of tanh(ent)
-// (state_proj input) and of ent - s (ent_proj input), quantised exactly like
-// tesm_b200_quant_act over the full d_state row (values first rounded to `act_dtype`).  The
-// codes land in one (M, ldc) matrix: tanh codes in columns [0, D), chg codes in [Dp, Dp + D),
-// zero padding up to Dp and 2*Dp -- the A operand of tesm_b200_gemm_i8_combine.
-struct LocalEntCodesParams {
-  LocalEntParams e;
-  int act_dtype;
-  float eps1, eps2;
-  int8_t *codes;
-  int64_t ldc;
-  int Dp;
-  float *inv1, *inv2;
-};
-
-template <int W>
-__global__ void __launch_bounds__(256, 2) k_siso_local_ent_codes(LocalEntCodesParams pp) {
-  extern __shared__ float sm[];
-  const LocalEntParams &p = pp.e;
-  const int R = p.R, T = p.T, D = p.D, DP1 = D + 1;
-  const int RP = R + 1;
-  float *qs = sm;
-  float *ks = qs + T * RP;
-  float *tw = ks + (T + W - 1) * RP;
-  float *invf = tw + T * W;
-  float *oT = invf + R / 2;    // T x (D+1)
-  float *oC = oT + T * DP1;    // T x (D+1)
-  // T x W duplicated weights, 16-byte aligned for the float4 reads
-  float2 *tw2 = reinterpret_cast<float2 *>((reinterpret_cast<uintptr_t>(oC + T * DP1) + 15) & ~(uintptr_t)15);
-  const int b = blockIdx.y, t0 = blockIdx.x * T;
-  const int64_t row0 = (int64_t)b * p.L;
-  const int nt = min(T, p.L - t0);
-  const int nwarp = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool pairs = (D & 1) == 0;
-  local_front<W>(p, qs, ks, tw, invf, row0, t0, nt, pairs ? tw2 : nullptr);
-  if (pairs) {
-    local_channels2<W>(p, tw2, row0, t0, nt, [&](int t, int d2, float ex, float ey, float sx, float sy) {
-      oT[t * DP1 + 2 * d2] = round_to(pp.act_dtype, tanhf(ex));
-      oT[t * DP1 + 2 * d2 + 1] = round_to(pp.act_dtype, tanhf(ey));
-      oC[t * DP1 + 2 * d2] = round_to(pp.act_dtype, ex - sx);
-      oC[t * DP1 + 2 * d2 + 1] = round_to(pp.act_dtype, ey - sy);
-    });
-  } else {
-    local_channels<W>(p, tw, row0, t0, nt, [&](int t, int d, float th, float ch) {
-      oT[t * DP1 + d] = round_to(pp.act_dtype, th);
-      oC[t * DP1 + d] = round_to(pp.act_dtype, ch);
-    });
-  }
-  __syncthreads();
-  // per-token quantisation: one warp per (row, output)
-  for (int item = warp; item < 2 * nt; item += nwarp) {
-    const int t = item >> 1, which = item & 1;
-    const float *src = (which ? oC : oT) + t * DP1;
-    float amax = 0.f;
-    for (int d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(src[d]));
-    amax = warp_max(amax);
-    const float sc = act_scale(amax, which ? pp.eps2 : pp.eps1, pp.act_dtype);
-    const int64_t row = row0 + t0 + t;
-    int8_t *crow = pp.codes + row * pp.ldc + (which ? pp.Dp : 0);
-    for (int d4 = lane * 4; d4 < pp.Dp; d4 += 128) {
-      uint32_t wv = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int d = d4 + i;
-        const int c = d < D ? act_code(src[d], sc, pp.act_dtype) : 0;
-        wv |= (uint32_t)(uint8_t)c << (8 * i);
-      }
-      *reinterpret_cast<uint32_t *>(crow + d4) = wv;
-    }
-    if (lane == 0) (which ? pp.inv2 : pp.inv1)[row] = __frcp_rn(sc);
-  }
-}
 
 // ---------------------------------------------------------------- global entanglement
 // Causal O(L^2) variant (tesm.py:963-1043): relative bias depends on i - j only and is
@@ -400,21 +178,43 @@ __global__ void k_combine(ProjCols pc, const void *sp, const void *ep, int sdtyp
 
 using namespace tesm;
 
-template <int W>
-static int launch_local(LocalEntParams &p, cudaStream_t st) {
-  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
-                                       p.R / 2 + 2 * (size_t)p.T * W + 4);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    cudaFuncSetAttribute(k_siso_local_ent<W>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr = true;
-  }
-  if (smem > 160 * 1024) return fail(TESM_EUNSUPPORTED, "local_ent: ent_rank too large");
-  dim3 grid((unsigned)ceil_div(p.L, p.T), (unsigned)p.B);
-  const int threads = p.D >= 256 ? 256 : (int)round_up(p.D, 32);
-  k_siso_local_ent<W><<<grid, threads < 64 ? 64 : threads, smem, st>>>(p);
-  return check_launch("local_ent");
+// Local entanglement (tesm.py:922-952 with the lerp :1231-1232): the persistent window kernel
+// of window.cuh, SISO mode (one head of d_state channels, cross-layer q bias).
+static int siso_win_params(WinEntParams &p, const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L,
+                           int64_t Dm, int64_t D, int64_t R, const float *cross, const float *bias,
+                           const float *states, float thr, float es, float rope_base) {
+  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "local_ent: dtype");
+  const ProjCols pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
+  p = WinEntParams{};
+  p.proj = proj;
+  p.ld = ldp;
+  p.c_q = pc.c_q;
+  p.c_k = pc.c_k;
+  p.states = states;
+  p.pos_ld = D;
+  p.rank_ld = 0;
+  p.cross = cross;
+  p.bias = bias;
+  p.B = (int)B;
+  p.L = (int)L;
+  p.H = 1;
+  p.D = (int)D;
+  p.R = (int)R;
+  p.thr = thr;
+  p.es = es;
+  p.sqrt_r = (float)sqrt((double)R);
+  p.rope_base = rope_base;
+  return TESM_OK;
+}
+
+template <int MODE>
+static int siso_win_dispatch(WinEntParams &p, int dtype, int64_t W, cudaStream_t st, const char *what) {
+#define TESM_SISO_WIN(WW)                                                                       \
+  if (W == WW)                                                                                  \
+    return dtype == TESM_BF16 ? win_launch<WW, 1, 2, MODE>(p, st, what) : win_launch<WW, 1, 4, MODE>(p, st, what);
+  TESM_SISO_WIN(4) TESM_SISO_WIN(8) TESM_SISO_WIN(16) TESM_SISO_WIN(32)
+#undef TESM_SISO_WIN
+  return fail(TESM_EUNSUPPORTED, std::string(what) + ": entanglement_window must be 4, 8, 16 or 32");
 }
 
 extern "C" int tesm_b200_siso_local_ent(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
@@ -423,51 +223,15 @@ extern "C" int tesm_b200_siso_local_ent(const void *proj, int dtype, int64_t ldp
                                         void *out_chg, int out_dtype, tesm_stream_t stream) {
   TESM_REQUIRE(proj && bias && states && out_tanh && out_chg, "local_ent: null pointer");
   TESM_REQUIRE(B > 0 && L > 0 && D > 0 && R > 0 && R % 2 == 0, "local_ent: bad shape");
-  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "local_ent: dtype");
-  LocalEntParams p;
-  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
-  p.cross = cross;
-  p.bias = bias;
-  p.states = states;
-  p.B = (int)B;
-  p.L = (int)L;
-  p.D = (int)D;
-  p.R = (int)R;
-  p.W = (int)W;
-  p.T = 64;
-  p.thr = thr;
-  p.es = es;
-  p.sqrt_r = (float)sqrt((double)R);
-  p.rope_base = rope_base;
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "local_ent: out dtype");
+  WinEntParams p;
+  int rc = siso_win_params(p, proj, dtype, ldp, B, L, Dm, D, R, cross, bias, states, thr, es, rope_base);
+  if (rc) return rc;
   p.out_tanh = out_tanh;
   p.out_chg = out_chg;
   p.out_dtype = out_dtype;
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (W) {
-    case 4: return launch_local<4>(p, st);
-    case 8: return launch_local<8>(p, st);
-    case 16: return launch_local<16>(p, st);
-    case 32: return launch_local<32>(p, st);
-    default: return fail(TESM_EUNSUPPORTED, "local_ent: entanglement_window must be 4, 8, 16 or 32");
-  }
-}
-
-template <int W>
-static int launch_local_codes(LocalEntCodesParams &pp, cudaStream_t st) {
-  const LocalEntParams &p = pp.e;
-  const size_t smem = sizeof(float) * ((size_t)p.T * (p.R + 1) + (size_t)(p.T + W - 1) * (p.R + 1) + p.T * W +
-                                       p.R / 2 + 2 * (size_t)p.T * (p.D + 1) + 4 + 2 * (size_t)p.T * W + 4);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(k_siso_local_ent_codes<W>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr = true;
-  }
-  if (smem > 200 * 1024) return fail(TESM_EUNSUPPORTED, "local_ent_codes: d_state / ent_rank too large");
-  dim3 grid((unsigned)ceil_div(p.L, p.T), (unsigned)p.B);
-  const int threads = p.D >= 256 ? 256 : (p.D <= 64 ? 64 : 128);
-  k_siso_local_ent_codes<W><<<grid, threads, smem, st>>>(pp);
-  return check_launch("local_ent_codes");
+  p.out_ld = D;
+  return siso_win_dispatch<kWinSiso>(p, dtype, W, (cudaStream_t)stream, "local_ent");
 }
 
 extern "C" int tesm_b200_siso_local_ent_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L,
@@ -480,41 +244,18 @@ extern "C" int tesm_b200_siso_local_ent_codes(const void *proj, int dtype, int64
   TESM_REQUIRE(B > 0 && L > 0 && D > 0 && R > 0 && R % 2 == 0, "local_ent_codes: bad shape");
   TESM_REQUIRE(Dp >= D && Dp % 128 == 0 && ldc >= 2 * Dp && ldc % 16 == 0 && ((uintptr_t)codes & 15) == 0,
                "local_ent_codes: codes layout (Dp multiple of 128 >= D, ldc >= 2*Dp, 16-byte rows)");
-  if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "local_ent_codes: dtype");
-  LocalEntCodesParams pp;
-  LocalEntParams &p = pp.e;
-  p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
-  p.cross = cross;
-  p.bias = bias;
-  p.states = states;
-  p.B = (int)B;
-  p.L = (int)L;
-  p.D = (int)D;
-  p.R = (int)R;
-  p.W = (int)W;
-  p.T = 32;
-  p.thr = thr;
-  p.es = es;
-  p.sqrt_r = (float)sqrt((double)R);
-  p.rope_base = rope_base;
-  p.out_tanh = p.out_chg = nullptr;
-  p.out_dtype = act_dtype;
-  pp.act_dtype = act_dtype;
-  pp.eps1 = eps1;
-  pp.eps2 = eps2;
-  pp.codes = codes;
-  pp.ldc = ldc;
-  pp.Dp = (int)Dp;
-  pp.inv1 = inv1;
-  pp.inv2 = inv2;
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (W) {
-    case 4: return launch_local_codes<4>(pp, st);
-    case 8: return launch_local_codes<8>(pp, st);
-    case 16: return launch_local_codes<16>(pp, st);
-    case 32: return launch_local_codes<32>(pp, st);
-    default: return fail(TESM_EUNSUPPORTED, "local_ent_codes: entanglement_window must be 4, 8, 16 or 32");
-  }
+  WinEntParams p;
+  int rc = siso_win_params(p, proj, dtype, ldp, B, L, Dm, D, R, cross, bias, states, thr, es, rope_base);
+  if (rc) return rc;
+  p.act_dtype = act_dtype;
+  p.eps1 = eps1;
+  p.eps2 = eps2;
+  p.codes = codes;
+  p.ldc = ldc;
+  p.Dp = (int)Dp;
+  p.inv1 = inv1;
+  p.inv2 = inv2;
+  return siso_win_dispatch<kWinSisoCodes>(p, dtype, W, (cudaStream_t)stream, "local_ent_codes");
 }
 
 extern "C" int tesm_b200_global_relbias(const float *embed, int64_t dim, float scale, float bias0, int64_t L,

@@ -1,0 +1,539 @@
+// Local-window ternary entanglement: one persistent kernel for the SISO layer (bf16/fp32
+// outputs, or int8 codes for the combine GEMM) and the MIMO layer (rank merge).
+// Reference: tesm.py:922-952 (torch rung) with ternary_entanglement :672-714 and the lerp
+// :1231-1232; MIMO tesm_mimo.py:525-588 (per-rank window sums) and :996-1017 (merge).
+//
+// Work unit = (sequence b, tile of T = 32 positions, head h); a CTA owns a strided list of
+// tiles and walks each tile's heads in turn (SISO: one head).  Per unit:
+//   fill     every byte the unit reads -- its q rows, the k rows and state rows of the window
+//            (positions t0-(W-1) ..), all mimo ranks -- is requested with 16-byte cp.async
+//            copies into one of two shared stages; the copies of unit n+1 are issued before
+//            unit n is computed, so HBM traffic overlaps the arithmetic.  Positions outside
+//            the sequence / tile are zero-filled by the copy itself.
+//   table    (cos, sin) of every (position, frequency) of the tile, once per tile (shared by
+//            q, k and all heads), theta = fl(pos * inv_freq) as in tesm.py:783-793.
+//   rope     q rows (+ cross-layer bias, tesm.py:1213-1218) and k rows, fp32 in shared memory.
+//   scores   q_t . k_{t-o} / sqrt(R) + bias[W-1-o] for the W lags o, thresholded to {-1,0,1};
+//            a lane owns one lag of one row and the row's |tern| count is a shuffle sum.
+//   window   avg[t][n] = sum_o tern[t][o] s[t-o][n] is a banded matrix product: for a block of
+//            16 positions, A[16 x K] holds the ternary weights on a diagonal band (exact in
+//            TF32) and B[K x 8] the states of K = 16 + W - 1 (rounded to 8) consecutive
+//            positions of 8 channels.  It runs on the tensor cores (mma.sync m16n8k8 TF32) with
+//            the fp32 states split as hi + lo (two MMAs, error ~2^-21 relative), then is scaled
+//            by 1 / max(sum |tern|, 1).
+//   epilogue ent = s + es (avg - s); SISO writes tanh(ent) and ent - s (or stages them for the
+//            per-token int8 codes), MIMO merges the ranks with mimo_o first.
+#pragma once
+
+#include "layer_common.cuh"
+#include "rowio.cuh"
+
+#include <algorithm>
+
+namespace tesm {
+
+enum WinMode { kWinSiso = 0, kWinSisoCodes = 1, kWinMimo = 2 };
+
+constexpr int kWinT = 32;         // positions per tile
+constexpr int kWinThreads = 512;  // 16 warps
+
+struct WinEntParams {
+  const void *proj;
+  int64_t ld;          // proj row stride (elements)
+  int64_t c_q, c_k;    // first q / k column; head h at + h * R
+  const float *states; // states[(row0 + pos) * pos_ld + k * rank_ld + h * D + ch]
+  int64_t pos_ld, rank_ld;
+  const float *cross;  // SISO cross-layer q bias (B*L, R) or null
+  const float *bias;   // window bias of head h at bias + h * W, read at [W-1-o]
+  const float *mimo_o; // MIMO (H, RM, D)
+  int B, L, H, D, R, quirk, async16, ntiles_b;
+  float thr, es, sqrt_r, rope_base;
+  void *out_tanh, *out_chg;  // out[(row0 + t) * out_ld + h * D + ch]
+  int out_dtype;
+  int64_t out_ld;
+  // kWinSisoCodes
+  int act_dtype, Dp;
+  float eps1, eps2;
+  int8_t *codes;
+  int64_t ldc;
+  float *inv1, *inv2;
+};
+
+// Tile geometry shared by host (shared-memory size) and device (carving).
+struct WinGeom {
+  int W, R, D, RM, ES, mode;
+  int half, RP, nk, KS, NROWS, SR, SRR, QRS;
+};
+
+__host__ __device__ inline int64_t win_r16(int64_t b) { return (b + 15) & ~(int64_t)15; }
+
+__host__ __device__ inline WinGeom win_geom(int W, int R, int D, int RM, int ES, int mode) {
+  WinGeom g;
+  g.W = W;
+  g.R = R;
+  g.D = D;
+  g.RM = RM;
+  g.ES = ES;
+  g.mode = mode;
+  g.half = R / 2;
+  g.RP = ((R + 3) / 4) * 4 + 4;
+  g.nk = kWinT + W - 1;
+  g.KS = (15 + W + 7) / 8;          // k-steps of 8 covering the 16 + W - 1 window rows of a block
+  g.NROWS = kWinT - 16 + g.KS * 8;  // state rows staged (>= nk)
+  g.SR = ((D + 3) / 4) * 4;         // rank stride in a state row
+  int srr = RM * g.SR;
+  while (srr % 32 != 8) srr += 4;   // row stride: the 4 rows x 8 channels of a B fragment hit 32 banks
+  g.SRR = srr;
+  g.QRS = (int)win_r16((int64_t)R * ES);
+  return g;
+}
+
+struct WinStage {
+  float *st;      // NROWS x SRR
+  uint8_t *qraw;  // T x QRS
+  uint8_t *kraw;  // nk x QRS
+};
+
+struct WinSmem {
+  WinStage stage[2];
+  float2 *cs;      // nk x half
+  float *invf;     // half
+  float *qs;       // T x RP
+  float *ks;       // nk x RP
+  float *twr;      // T x W ternary
+  float *inv;      // T     1 / max(sum |tern|, 1)
+  float *oT, *oC;  // kWinSisoCodes: T x (D + 1) staged outputs
+};
+
+__host__ __device__ inline size_t win_smem_bytes(const WinGeom &g) {
+  const size_t stage = win_r16((int64_t)g.NROWS * g.SRR * 4) + win_r16((int64_t)kWinT * g.QRS) +
+                       win_r16((int64_t)g.nk * g.QRS);
+  size_t b = 2 * stage + win_r16((int64_t)g.nk * g.half * 8) + win_r16((int64_t)g.half * 4) +
+             win_r16((int64_t)kWinT * g.RP * 4) + win_r16((int64_t)g.nk * g.RP * 4) +
+             win_r16((int64_t)kWinT * g.W * 4) + win_r16((int64_t)kWinT * 4);
+  if (g.mode == kWinSisoCodes) b += 2 * win_r16((int64_t)kWinT * (g.D + 1) * 4);
+  return b;
+}
+
+__device__ __forceinline__ WinSmem win_carve(uint8_t *p, const WinGeom &g) {
+  WinSmem s;
+  auto take = [&p](int64_t bytes) {
+    uint8_t *r = p;
+    p += win_r16(bytes);
+    return r;
+  };
+  for (int i = 0; i < 2; ++i) {
+    s.stage[i].st = reinterpret_cast<float *>(take((int64_t)g.NROWS * g.SRR * 4));
+    s.stage[i].qraw = take((int64_t)kWinT * g.QRS);
+    s.stage[i].kraw = take((int64_t)g.nk * g.QRS);
+  }
+  s.cs = reinterpret_cast<float2 *>(take((int64_t)g.nk * g.half * 8));
+  s.invf = reinterpret_cast<float *>(take((int64_t)g.half * 4));
+  s.qs = reinterpret_cast<float *>(take((int64_t)kWinT * g.RP * 4));
+  s.ks = reinterpret_cast<float *>(take((int64_t)g.nk * g.RP * 4));
+  s.twr = reinterpret_cast<float *>(take((int64_t)kWinT * g.W * 4));
+  s.inv = reinterpret_cast<float *>(take((int64_t)kWinT * 4));
+  s.oT = s.oC = nullptr;
+  if (g.mode == kWinSisoCodes) {
+    s.oT = reinterpret_cast<float *>(take((int64_t)kWinT * (g.D + 1) * 4));
+    s.oC = reinterpret_cast<float *>(take((int64_t)kWinT * (g.D + 1) * 4));
+  }
+  return s;
+}
+
+// Whether every q/k row and state chunk starts on a 16-byte boundary (then units are staged
+// with asynchronous 16-byte copies; otherwise with plain element copies).
+inline bool win_async_ok(const WinEntParams &p, int ES) {
+  return ((uintptr_t)p.proj & 15) == 0 && (p.ld * ES) % 16 == 0 && (p.c_q * ES) % 16 == 0 &&
+         (p.c_k * ES) % 16 == 0 && (p.R * ES) % 16 == 0 && ((uintptr_t)p.states & 15) == 0 && p.D % 4 == 0 &&
+         p.pos_ld % 4 == 0 && p.rank_ld % 4 == 0 && p.R * ES / 16 <= kWinThreads &&
+         (int64_t)p.D / 4 * (p.rank_ld ? (p.pos_ld / p.rank_ld) : 1) <= kWinThreads;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t f32_to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Per-thread strided walk over a (rows x per_row) index space without per-element division:
+// the thread handles (r0 + k * rstep, c0); threads beyond rstep * per_row stay idle.
+struct WinMap {
+  int r0, c0, rstep;
+  bool active;
+};
+__device__ __forceinline__ WinMap win_map(int per_row) {
+  WinMap m;
+  m.rstep = per_row > 0 ? kWinThreads / per_row : 0;
+  m.r0 = per_row > 0 ? (int)threadIdx.x / per_row : 0;
+  m.c0 = (int)threadIdx.x - m.r0 * per_row;
+  m.active = per_row > 0 && per_row <= kWinThreads && m.r0 < m.rstep;
+  return m;
+}
+
+// Stage the unit (tile at row0 + t0, nt positions, head h) into `sg`.  Asynchronous path: a
+// thread owns one 16-byte column chunk of the q/k rows (mq) and one of the state rows (ms:
+// rank k, chunk c) and walks rows with pointer increments.
+template <int W, int RM, int ES>
+__device__ __forceinline__ void win_fill(const WinEntParams &p, const WinGeom &g, const WinStage &sg,
+                                         const WinMap &mq, const WinMap &ms, int64_t row0, int t0, int nt, int h) {
+  const int nkv = nt + W - 1;
+  const uint8_t *proj = reinterpret_cast<const uint8_t *>(p.proj);
+  const int64_t qcol = p.c_q + (int64_t)h * p.R, kcol = p.c_k + (int64_t)h * p.R;
+  const int64_t scol = (int64_t)h * p.D;
+  if (p.async16) {
+    if (mq.active) {
+      const int64_t rstride = (int64_t)mq.rstep * p.ld * ES;
+      const uint8_t *src = proj + ((row0 + t0 + mq.r0) * p.ld + qcol) * ES + mq.c0 * 16;
+      uint8_t *dst = sg.qraw + (size_t)mq.r0 * g.QRS + mq.c0 * 16;
+      for (int r = mq.r0; r < nt; r += mq.rstep, src += rstride, dst += mq.rstep * g.QRS) cp_async16(dst, src, 16);
+      int pos = t0 - (W - 1) + mq.r0;
+      src = proj + ((row0 + pos) * p.ld + kcol) * ES + mq.c0 * 16;
+      dst = sg.kraw + (size_t)mq.r0 * g.QRS + mq.c0 * 16;
+      for (int r = mq.r0; r < nkv; r += mq.rstep, pos += mq.rstep, src += rstride, dst += mq.rstep * g.QRS)
+        cp_async16(dst, pos < 0 ? proj : src, pos < 0 ? 0 : 16);
+    }
+    if (ms.active) {
+      const int cpr = p.D / 4;  // chunks per rank block
+      const int k = ms.c0 / cpr, c = ms.c0 - k * cpr;
+      int pos = t0 - (W - 1) + ms.r0;
+      const int lim = t0 + nt;
+      const float *src = p.states + (row0 + pos) * p.pos_ld + k * p.rank_ld + scol + c * 4;
+      float *dst = sg.st + (size_t)ms.r0 * g.SRR + k * g.SR + c * 4;
+      const int64_t sstride = (int64_t)ms.rstep * p.pos_ld;
+      for (int r = ms.r0; r < g.NROWS; r += ms.rstep, pos += ms.rstep, src += sstride, dst += ms.rstep * g.SRR) {
+        const bool ok = pos >= 0 && pos < lim;
+        cp_async16(dst, ok ? src : p.states, ok ? 16 : 0);
+      }
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < (nt + nkv) * p.R; idx += kWinThreads) {
+      const int r = idx / p.R, e = idx - r * p.R;
+      const bool isq = r < nt;
+      const int rr = isq ? r : r - nt;
+      const int pos = isq ? t0 + rr : t0 - (W - 1) + rr;
+      uint8_t *dst = (isq ? sg.qraw : sg.kraw) + (size_t)rr * g.QRS + e * ES;
+      const int64_t off = (row0 + pos) * p.ld + (isq ? qcol : kcol) + e;
+      if (ES == 2)
+        *reinterpret_cast<uint16_t *>(dst) = pos < 0 ? 0 : reinterpret_cast<const uint16_t *>(proj)[off];
+      else
+        *reinterpret_cast<float *>(dst) = pos < 0 ? 0.f : reinterpret_cast<const float *>(proj)[off];
+    }
+    for (int idx = threadIdx.x; idx < g.NROWS * RM * p.D; idx += kWinThreads) {
+      const int rk = idx / p.D, j = idx - rk * p.D;
+      const int r = rk / RM, k = rk - r * RM;
+      const int pos = t0 - (W - 1) + r;
+      const bool ok = pos >= 0 && pos < t0 + nt;
+      sg.st[(size_t)r * g.SRR + k * g.SR + j] = ok ? p.states[(row0 + pos) * p.pos_ld + k * p.rank_ld + scol + j] : 0.f;
+    }
+  }
+}
+
+// tanh from the hardware exponential: 1 - 2 / (1 + e^{2x}) (absolute error ~2e-7; saturates
+// to +-1 through the infinities of e^{2x}).
+__device__ __forceinline__ float win_tanh(float x) { return 1.f - __fdividef(2.f, 1.f + __expf(2.f * x)); }
+
+template <int ES>
+__device__ __forceinline__ float raw_at(const uint8_t *row, int i) {
+  if (ES == 2) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(row)[i]);
+  return reinterpret_cast<const float *>(row)[i];
+}
+
+__device__ __forceinline__ void win_store2(void *out, int dtype, int64_t o, float x, float y, bool pair, bool has_y) {
+  if (pair) {
+    if (dtype == TESM_BF16)
+      *reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(out) + o) = __floats2bfloat162_rn(x, y);
+    else
+      *reinterpret_cast<float2 *>(reinterpret_cast<float *>(out) + o) = make_float2(x, y);
+  } else {
+    store_f(out, dtype, o, x);
+    if (has_y) store_f(out, dtype, o + 1, y);
+  }
+}
+
+template <int W, int RM, int ES, int MODE>
+__global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const WinGeom g = win_geom(W, p.R, p.D, RM, ES, MODE);
+  const WinSmem s = win_carve(smem_raw, g);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tig = lane & 3;
+  const int half = g.half, R = p.R, RP = g.RP, D = p.D, H = p.H;
+  const int R4 = (R + 3) & ~3;
+  const WinMap mq = win_map(R * ES / 16), ms = win_map(RM * (D / 4)), mh = win_map(half);
+
+  for (int i = tid; i < half; i += kWinThreads) s.invf[i] = rope_inv_freq(i, R, p.rope_base);
+  if (R4 > R)  // pad columns read by the 4-wide dot products stay zero
+    for (int i = tid; i < (kWinT + g.nk) * (R4 - R); i += kWinThreads) {
+      const int row = i / (R4 - R), j = i - row * (R4 - R);
+      (row < kWinT ? s.qs + row * RP : s.ks + (row - kWinT) * RP)[R + j] = 0.f;
+    }
+
+  const int ntiles = p.B * p.ntiles_b;
+  int tile = blockIdx.x, h = 0;
+  auto unit_of = [&](int tl, int64_t &row0, int &t0, int &nt) {
+    const int b = tl / p.ntiles_b;
+    t0 = (tl - b * p.ntiles_b) * kWinT;
+    row0 = (int64_t)b * p.L;
+    nt = min(kWinT, p.L - t0);
+  };
+  if (tile < ntiles) {
+    int64_t row0;
+    int t0, nt;
+    unit_of(tile, row0, t0, nt);
+    win_fill<W, RM, ES>(p, g, s.stage[0], mq, ms, row0, t0, nt, 0);
+  }
+  cp_async_commit();
+  __syncthreads();
+
+  const float es = p.es;
+  const int tb = (warp & 1) * 16;  // this warp's 16-position block for the window product
+  int stage = 0;
+  bool new_tile = true;
+  while (tile < ntiles) {
+    int64_t row0;
+    int t0, nt;
+    unit_of(tile, row0, t0, nt);
+    const int nkv = nt + W - 1;
+    // issue the next unit's copies into the other stage (released at the end of the previous
+    // unit), then wait for this unit's
+    {
+      int nh = h + 1, ntl = tile;
+      if (nh == H) {
+        nh = 0;
+        ntl += gridDim.x;
+      }
+      if (ntl < ntiles) {
+        int64_t r1;
+        int a1, n1;
+        unit_of(ntl, r1, a1, n1);
+        win_fill<W, RM, ES>(p, g, stage ? s.stage[0] : s.stage[1], mq, ms, r1, a1, n1, nh);
+      }
+      cp_async_commit();
+    }
+    if (new_tile && mh.active) {
+      for (int r = mh.r0; r < nkv; r += mh.rstep) {
+        const int pos = t0 - (W - 1) + r;
+        float sn = 0.f, cn = 1.f;
+        if (pos >= 0) sincosf((float)pos * s.invf[mh.c0], &sn, &cn);
+        s.cs[r * half + mh.c0] = make_float2(cn, sn);
+      }
+    }
+    cp_async_wait_1();
+    __syncthreads();
+    const WinStage sg = stage ? s.stage[1] : s.stage[0];  // static indices keep s in registers
+    // RoPE: q rows then k rows (rows before the sequence start hold zeros)
+    if (mh.active) {
+      for (int r = mh.r0; r < nt + nkv; r += mh.rstep) {
+        const bool isq = r < nt;
+        const int rr = isq ? r : r - nt;
+        const uint8_t *raw = (isq ? sg.qraw : sg.kraw) + (size_t)rr * g.QRS;
+        const float2 c = s.cs[(isq ? rr + W - 1 : rr) * half + mh.c0];
+        const float x1 = raw_at<ES>(raw, mh.c0), x2 = raw_at<ES>(raw, half + mh.c0);
+        float o1 = x1 * c.x - x2 * c.y, o2 = x1 * c.y + x2 * c.x;
+        if (isq && MODE != kWinMimo && p.cross) {
+          const float *add = p.cross + (row0 + t0 + rr) * R;
+          o1 += add[mh.c0];
+          o2 += add[half + mh.c0];
+        }
+        float *dst = isq ? s.qs + rr * RP : s.ks + rr * RP;
+        dst[mh.c0] = o1;
+        dst[half + mh.c0] = o2;
+      }
+    }
+    __syncthreads();
+    // scores: lane = (row t, lag o); the row's W lanes are adjacent
+    {
+      const float *brow = p.bias + (MODE == kWinMimo ? h * W : 0);
+      for (int item = tid; item < kWinT * W; item += kWinThreads) {
+        const int t = item / W, o = item - t * W;  // W compile-time
+        float tv = 0.f;
+        if (t < nt) {
+          const float *qr = s.qs + t * RP, *kr = s.ks + (t + W - 1 - o) * RP;
+          float d0 = 0.f;
+          for (int c = 0; c < R4; c += 4) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(qr + c);
+            const float4 k4 = *reinterpret_cast<const float4 *>(kr + c);
+            d0 = fmaf(q4.x, k4.x, d0);
+            d0 = fmaf(q4.y, k4.y, d0);
+            d0 = fmaf(q4.z, k4.z, d0);
+            d0 = fmaf(q4.w, k4.w, d0);
+          }
+          const int gt = t0 + t;
+          if (gt - o >= 0 && (MODE != kWinMimo || !p.quirk || o >= W - 1 - gt))
+            tv = ternary_of(__fdiv_rn(d0, p.sqrt_r) + brow[W - 1 - o], p.thr);
+        }
+        s.twr[item] = tv;
+        float cnt = fabsf(tv);
+#pragma unroll
+        for (int m = W / 2; m >= 1; m >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, m);
+        if (o == 0) s.inv[t] = 1.f / fmaxf(cnt, 1.f);
+      }
+    }
+    __syncthreads();
+    // banded window product on the tensor cores + epilogue
+    {
+      constexpr int KS = (15 + W + 7) / 8;
+      const int SRR = g.SRR, SR = g.SR;
+      uint32_t a[KS][4];
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int row = gq + ((j & 1) ? 8 : 0), k = ks * 8 + tig + ((j & 2) ? 4 : 0);
+          const int o = row + W - 1 - k;
+          const float v = (o >= 0 && o < W) ? s.twr[(tb + row) * W + o] : 0.f;
+          a[ks][j] = __float_as_uint(v);
+        }
+      }
+      const int ngroups = (D + 7) / 8;
+      const float *st = sg.st;
+      for (int cg = warp >> 1; cg < ngroups; cg += kWinThreads / 64) {
+        float acc[RM][4];
+#pragma unroll
+        for (int k = 0; k < RM; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
+        const float *bcol = st + (size_t)(tb + tig) * SRR + cg * 8 + gq;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+          for (int k = 0; k < RM; ++k) {
+            const float x0 = bcol[(size_t)(ks * 8) * SRR + k * SR], x1 = bcol[(size_t)(ks * 8 + 4) * SRR + k * SR];
+            const uint32_t h0 = f32_to_tf32(x0), h1 = f32_to_tf32(x1);
+            mma_tf32(acc[k], a[ks], h0, h1);
+            mma_tf32(acc[k], a[ks], __float_as_uint(x0 - __uint_as_float(h0)),
+                     __float_as_uint(x1 - __uint_as_float(h1)));
+          }
+        }
+        // epilogue: the lane holds rows tb+gq, tb+gq+8 x channels ch, ch+1 of every rank
+        const int ch = cg * 8 + 2 * tig;
+        const bool has_x = ch < D, has_y = ch + 1 < D;
+        float2 mo[RM];
+        if (MODE == kWinMimo) {
+#pragma unroll
+          for (int k = 0; k < RM; ++k) {
+            const float *m = p.mimo_o + ((int64_t)h * RM + k) * D + ch;
+            mo[k] = make_float2(has_x ? m[0] : 0.f, has_y ? m[1] : 0.f);
+          }
+        }
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int t = tb + gq + 8 * hr;
+          if (t >= nt || !has_x) continue;
+          const float iv = s.inv[t];
+          const float *srow = st + (size_t)(t + W - 1) * SRR + ch;
+          float ex = 0.f, ey = 0.f, cx = 0.f, cy = 0.f;
+#pragma unroll
+          for (int k = 0; k < RM; ++k) {
+            float sx, sy;
+            if (has_y) {
+              const float2 v = *reinterpret_cast<const float2 *>(srow + k * SR);  // ch even, SR % 4 == 0
+              sx = v.x;
+              sy = v.y;
+            } else {
+              sx = srow[k * SR];
+              sy = 0.f;
+            }
+            const float e0 = sx + es * (acc[k][2 * hr] * iv - sx);
+            const float e1 = sy + es * (acc[k][2 * hr + 1] * iv - sy);
+            if (MODE == kWinMimo) {
+              ex = fmaf(mo[k].x, e0, ex);
+              ey = fmaf(mo[k].y, e1, ey);
+              cx = fmaf(mo[k].x, e0 - sx, cx);
+              cy = fmaf(mo[k].y, e1 - sy, cy);
+            } else {
+              ex = e0;
+              ey = e1;
+              cx = e0 - sx;
+              cy = e1 - sy;
+            }
+          }
+          if (MODE == kWinSisoCodes) {
+            float *rt = s.oT + t * (D + 1) + ch, *rc = s.oC + t * (D + 1) + ch;
+            rt[0] = round_to(p.act_dtype, win_tanh(ex));
+            rc[0] = round_to(p.act_dtype, cx);
+            if (has_y) {
+              rt[1] = round_to(p.act_dtype, win_tanh(ey));
+              rc[1] = round_to(p.act_dtype, cy);
+            }
+          } else {
+            const int64_t o = (row0 + t0 + t) * p.out_ld + (int64_t)h * D + ch;
+            const bool pair = has_y && (o & 1) == 0;
+            win_store2(p.out_tanh, p.out_dtype, o, win_tanh(ex), has_y ? win_tanh(ey) : 0.f, pair, has_y);
+            win_store2(p.out_chg, p.out_dtype, o, cx, cy, pair, has_y);
+          }
+        }
+      }
+    }
+    if (MODE == kWinSisoCodes) {
+      // per-token int8 codes of both staged outputs (exactly as tesm_b200_quant_act)
+      __syncthreads();
+      for (int item = warp; item < 2 * nt; item += kWinThreads / 32) {
+        const int t = item >> 1, which = item & 1;
+        const float *src = (which ? s.oC : s.oT) + t * (D + 1);
+        float amax = 0.f;
+        for (int d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(src[d]));
+        amax = warp_max(amax);
+        const float sc = act_scale(amax, which ? p.eps2 : p.eps1, p.act_dtype);
+        const int64_t row = row0 + t0 + t;
+        int8_t *crow = p.codes + row * p.ldc + (which ? p.Dp : 0);
+        for (int d4 = lane * 4; d4 < p.Dp; d4 += 128) {
+          uint32_t wv = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int d = d4 + i;
+            const int c = d < D ? act_code(src[d], sc, p.act_dtype) : 0;
+            wv |= (uint32_t)(uint8_t)c << (8 * i);
+          }
+          *reinterpret_cast<uint32_t *>(crow + d4) = wv;
+        }
+        if (lane == 0) (which ? p.inv2 : p.inv1)[row] = __frcp_rn(sc);
+      }
+    }
+    __syncthreads();  // this stage, qs/ks, twr and the staged outputs are free again
+    stage ^= 1;
+    if (++h == H) {
+      h = 0;
+      tile += gridDim.x;
+      new_tile = true;
+    } else {
+      new_tile = false;
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+// Host launcher: persistent grid of one CTA per SM (fewer when there are fewer tiles).
+template <int W, int RM, int ES, int MODE>
+static int win_launch(WinEntParams &p, cudaStream_t st, const char *what) {
+  p.ntiles_b = (int)ceil_div(p.L, kWinT);
+  p.async16 = win_async_ok(p, ES);
+  const WinGeom g = win_geom(W, p.R, p.D, RM, ES, MODE);
+  const size_t smem = win_smem_bytes(g);
+  if (smem > 227 * 1024)
+    return fail(TESM_EUNSUPPORTED, std::string(what) + ": d_state / ent_rank too large for one tile in shared memory");
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_win_ent<W, RM, ES, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = true;
+  }
+  const int64_t ntiles = (int64_t)p.B * p.ntiles_b;
+  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  k_win_ent<W, RM, ES, MODE><<<grid, kWinThreads, smem, st>>>(p);
+  return check_launch(what);
+}
+
+}  // namespace tesm
