@@ -35,7 +35,6 @@ namespace tesm {
 enum WinMode { kWinSiso = 0, kWinSisoCodes = 1, kWinMimo = 2 };
 
 constexpr int kWinT = 32;         // positions per tile
-constexpr int kWinThreads = 512;  // 16 warps
 
 struct WinEntParams {
   const void *proj;
@@ -61,14 +60,15 @@ struct WinEntParams {
 
 // Tile geometry shared by host (shared-memory size) and device (carving).
 struct WinGeom {
-  int W, R, D, RM, ES, mode;
+  int W, R, D, RM, ES, mode, nst;  // nst: staging buffers (2: the next unit streams in meanwhile)
   int half, RP, nk, KS, NROWS, SR, SRR, QRS;
 };
 
 __host__ __device__ inline int64_t win_r16(int64_t b) { return (b + 15) & ~(int64_t)15; }
 
-__host__ __device__ inline WinGeom win_geom(int W, int R, int D, int RM, int ES, int mode) {
+__host__ __device__ inline WinGeom win_geom(int W, int R, int D, int RM, int ES, int mode, int nst) {
   WinGeom g;
+  g.nst = nst;
   g.W = W;
   g.R = R;
   g.D = D;
@@ -108,7 +108,7 @@ struct WinSmem {
 __host__ __device__ inline size_t win_smem_bytes(const WinGeom &g) {
   const size_t stage = win_r16((int64_t)g.NROWS * g.SRR * 4) + win_r16((int64_t)kWinT * g.QRS) +
                        win_r16((int64_t)g.nk * g.QRS);
-  size_t b = 2 * stage + win_r16((int64_t)g.nk * g.half * 8) + win_r16((int64_t)g.half * 4) +
+  size_t b = g.nst * stage + win_r16((int64_t)g.nk * g.half * 8) + win_r16((int64_t)g.half * 4) +
              win_r16((int64_t)kWinT * g.RP * 4) + win_r16((int64_t)g.nk * g.RP * 4) +
              win_r16((int64_t)kWinT * g.W * 4) + win_r16((int64_t)kWinT * 4);
   if (g.mode == kWinSisoCodes) b += 2 * win_r16((int64_t)kWinT * (g.D + 1) * 4);
@@ -122,11 +122,12 @@ __device__ __forceinline__ WinSmem win_carve(uint8_t *p, const WinGeom &g) {
     p += win_r16(bytes);
     return r;
   };
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < g.nst; ++i) {
     s.stage[i].st = reinterpret_cast<float *>(take((int64_t)g.NROWS * g.SRR * 4));
     s.stage[i].qraw = take((int64_t)kWinT * g.QRS);
     s.stage[i].kraw = take((int64_t)g.nk * g.QRS);
   }
+  if (g.nst == 1) s.stage[1] = s.stage[0];
   s.cs = reinterpret_cast<float2 *>(take((int64_t)g.nk * g.half * 8));
   s.invf = reinterpret_cast<float *>(take((int64_t)g.half * 4));
   s.qs = reinterpret_cast<float *>(take((int64_t)kWinT * g.RP * 4));
@@ -143,11 +144,11 @@ __device__ __forceinline__ WinSmem win_carve(uint8_t *p, const WinGeom &g) {
 
 // Whether every q/k row and state chunk starts on a 16-byte boundary (then units are staged
 // with asynchronous 16-byte copies; otherwise with plain element copies).
-inline bool win_async_ok(const WinEntParams &p, int ES) {
+inline bool win_async_ok(const WinEntParams &p, int ES, int nthr) {
   return ((uintptr_t)p.proj & 15) == 0 && (p.ld * ES) % 16 == 0 && (p.c_q * ES) % 16 == 0 &&
          (p.c_k * ES) % 16 == 0 && (p.R * ES) % 16 == 0 && ((uintptr_t)p.states & 15) == 0 && p.D % 4 == 0 &&
-         p.pos_ld % 4 == 0 && p.rank_ld % 4 == 0 && p.R * ES / 16 <= kWinThreads &&
-         (int64_t)p.D / 4 * (p.rank_ld ? (p.pos_ld / p.rank_ld) : 1) <= kWinThreads;
+         p.pos_ld % 4 == 0 && p.rank_ld % 4 == 0 && p.R * ES / 16 <= nthr &&
+         (int64_t)p.D / 4 * (p.rank_ld ? (p.pos_ld / p.rank_ld) : 1) <= nthr;
 }
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
@@ -176,19 +177,20 @@ struct WinMap {
   int r0, c0, rstep;
   bool active;
 };
+template <int NT>
 __device__ __forceinline__ WinMap win_map(int per_row) {
   WinMap m;
-  m.rstep = per_row > 0 ? kWinThreads / per_row : 0;
+  m.rstep = per_row > 0 ? NT / per_row : 0;
   m.r0 = per_row > 0 ? (int)threadIdx.x / per_row : 0;
   m.c0 = (int)threadIdx.x - m.r0 * per_row;
-  m.active = per_row > 0 && per_row <= kWinThreads && m.r0 < m.rstep;
+  m.active = per_row > 0 && per_row <= NT && m.r0 < m.rstep;
   return m;
 }
 
 // Stage the unit (tile at row0 + t0, nt positions, head h) into `sg`.  Asynchronous path: a
 // thread owns one 16-byte column chunk of the q/k rows (mq) and one of the state rows (ms:
 // rank k, chunk c) and walks rows with pointer increments.
-template <int W, int RM, int ES>
+template <int W, int RM, int ES, int NT>
 __device__ __forceinline__ void win_fill(const WinEntParams &p, const WinGeom &g, const WinStage &sg,
                                          const WinMap &mq, const WinMap &ms, int64_t row0, int t0, int nt, int h) {
   const int nkv = nt + W - 1;
@@ -221,7 +223,7 @@ __device__ __forceinline__ void win_fill(const WinEntParams &p, const WinGeom &g
       }
     }
   } else {
-    for (int idx = threadIdx.x; idx < (nt + nkv) * p.R; idx += kWinThreads) {
+    for (int idx = threadIdx.x; idx < (nt + nkv) * p.R; idx += NT) {
       const int r = idx / p.R, e = idx - r * p.R;
       const bool isq = r < nt;
       const int rr = isq ? r : r - nt;
@@ -233,7 +235,7 @@ __device__ __forceinline__ void win_fill(const WinEntParams &p, const WinGeom &g
       else
         *reinterpret_cast<float *>(dst) = pos < 0 ? 0.f : reinterpret_cast<const float *>(proj)[off];
     }
-    for (int idx = threadIdx.x; idx < g.NROWS * RM * p.D; idx += kWinThreads) {
+    for (int idx = threadIdx.x; idx < g.NROWS * RM * p.D; idx += NT) {
       const int rk = idx / p.D, j = idx - rk * p.D;
       const int r = rk / RM, k = rk - r * RM;
       const int pos = t0 - (W - 1) + r;
@@ -265,20 +267,22 @@ __device__ __forceinline__ void win_store2(void *out, int dtype, int64_t o, floa
   }
 }
 
-template <int W, int RM, int ES, int MODE>
-__global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
+// NT threads; NST = 2: one CTA per SM streams the next unit in while computing this one;
+// NST = 1: two CTAs per SM, each loading its next unit after finishing the current one.
+template <int W, int RM, int ES, int MODE, int NT, int NST>
+__global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(WinEntParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  const WinGeom g = win_geom(W, p.R, p.D, RM, ES, MODE);
+  const WinGeom g = win_geom(W, p.R, p.D, RM, ES, MODE, NST);
   const WinSmem s = win_carve(smem_raw, g);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tig = lane & 3;
   const int half = g.half, R = p.R, RP = g.RP, D = p.D, H = p.H;
   const int R4 = (R + 3) & ~3;
-  const WinMap mq = win_map(R * ES / 16), ms = win_map(RM * (D / 4)), mh = win_map(half);
+  const WinMap mq = win_map<NT>(R * ES / 16), ms = win_map<NT>(RM * (D / 4)), mh = win_map<NT>(half);
 
-  for (int i = tid; i < half; i += kWinThreads) s.invf[i] = rope_inv_freq(i, R, p.rope_base);
+  for (int i = tid; i < half; i += NT) s.invf[i] = rope_inv_freq(i, R, p.rope_base);
   if (R4 > R)  // pad columns read by the 4-wide dot products stay zero
-    for (int i = tid; i < (kWinT + g.nk) * (R4 - R); i += kWinThreads) {
+    for (int i = tid; i < (kWinT + g.nk) * (R4 - R); i += NT) {
       const int row = i / (R4 - R), j = i - row * (R4 - R);
       (row < kWinT ? s.qs + row * RP : s.ks + (row - kWinT) * RP)[R + j] = 0.f;
     }
@@ -295,7 +299,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
     int64_t row0;
     int t0, nt;
     unit_of(tile, row0, t0, nt);
-    win_fill<W, RM, ES>(p, g, s.stage[0], mq, ms, row0, t0, nt, 0);
+    win_fill<W, RM, ES, NT>(p, g, s.stage[0], mq, ms, row0, t0, nt, 0);
   }
   cp_async_commit();
   __syncthreads();
@@ -309,9 +313,9 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
     int t0, nt;
     unit_of(tile, row0, t0, nt);
     const int nkv = nt + W - 1;
-    // issue the next unit's copies into the other stage (released at the end of the previous
-    // unit), then wait for this unit's
-    {
+    // NST = 2: issue the next unit's copies into the other stage (released at the end of the
+    // previous unit), then wait for this unit's
+    if (NST == 2) {
       int nh = h + 1, ntl = tile;
       if (nh == H) {
         nh = 0;
@@ -321,7 +325,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
         int64_t r1;
         int a1, n1;
         unit_of(ntl, r1, a1, n1);
-        win_fill<W, RM, ES>(p, g, stage ? s.stage[0] : s.stage[1], mq, ms, r1, a1, n1, nh);
+        win_fill<W, RM, ES, NT>(p, g, stage ? s.stage[0] : s.stage[1], mq, ms, r1, a1, n1, nh);
       }
       cp_async_commit();
     }
@@ -333,7 +337,10 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
         s.cs[r * half + mh.c0] = make_float2(cn, sn);
       }
     }
-    cp_async_wait_1();
+    if (NST == 2)
+      cp_async_wait_1();
+    else
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     __syncthreads();
     const WinStage sg = stage ? s.stage[1] : s.stage[0];  // static indices keep s in registers
     // RoPE: q rows then k rows (rows before the sequence start hold zeros)
@@ -359,7 +366,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
     // scores: lane = (row t, lag o); the row's W lanes are adjacent
     {
       const float *brow = p.bias + (MODE == kWinMimo ? h * W : 0);
-      for (int item = tid; item < kWinT * W; item += kWinThreads) {
+      for (int item = tid; item < kWinT * W; item += NT) {
         const int t = item / W, o = item - t * W;  // W compile-time
         float tv = 0.f;
         if (t < nt) {
@@ -402,7 +409,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
       }
       const int ngroups = (D + 7) / 8;
       const float *st = sg.st;
-      for (int cg = warp >> 1; cg < ngroups; cg += kWinThreads / 64) {
+      for (int cg = warp >> 1; cg < ngroups; cg += NT / 64) {
         float acc[RM][4];
 #pragma unroll
         for (int k = 0; k < RM; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
@@ -481,7 +488,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
     if (MODE == kWinSisoCodes) {
       // per-token int8 codes of both staged outputs (exactly as tesm_b200_quant_act)
       __syncthreads();
-      for (int item = warp; item < 2 * nt; item += kWinThreads / 32) {
+      for (int item = warp; item < 2 * nt; item += NT / 32) {
         const int t = item >> 1, which = item & 1;
         const float *src = (which ? s.oC : s.oT) + t * (D + 1);
         float amax = 0.f;
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
       }
     }
     __syncthreads();  // this stage, qs/ks, twr and the staged outputs are free again
-    stage ^= 1;
+    stage ^= (NST == 2);
     if (++h == H) {
       h = 0;
       tile += gridDim.x;
@@ -512,28 +519,51 @@ __global__ void __launch_bounds__(kWinThreads, 1) k_win_ent(WinEntParams p) {
     } else {
       new_tile = false;
     }
+    if (NST == 1 && tile < ntiles) {
+      int64_t r1;
+      int a1, n1;
+      unit_of(tile, r1, a1, n1);
+      win_fill<W, RM, ES, NT>(p, g, s.stage[0], mq, ms, r1, a1, n1, h);
+      cp_async_commit();
+    }
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
 
-// Host launcher: persistent grid of one CTA per SM (fewer when there are fewer tiles).
-template <int W, int RM, int ES, int MODE>
-static int win_launch(WinEntParams &p, cudaStream_t st, const char *what) {
-  p.ntiles_b = (int)ceil_div(p.L, kWinT);
-  p.async16 = win_async_ok(p, ES);
-  const WinGeom g = win_geom(W, p.R, p.D, RM, ES, MODE);
+template <int W, int RM, int ES, int MODE, int NT, int NST>
+static int win_launch_v(WinEntParams &p, const WinGeom &g, int ctas_per_sm, cudaStream_t st, const char *what) {
+  p.async16 = win_async_ok(p, ES, NT);
   const size_t smem = win_smem_bytes(g);
-  if (smem > 227 * 1024)
-    return fail(TESM_EUNSUPPORTED, std::string(what) + ": d_state / ent_rank too large for one tile in shared memory");
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_win_ent<W, RM, ES, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_win_ent<W, RM, ES, MODE, NT, NST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         227 * 1024);
     attr = true;
   }
   const int64_t ntiles = (int64_t)p.B * p.ntiles_b;
-  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
-  k_win_ent<W, RM, ES, MODE><<<grid, kWinThreads, smem, st>>>(p);
+  const int grid = (int)std::min<int64_t>(ntiles, (int64_t)sm_count() * ctas_per_sm);
+  k_win_ent<W, RM, ES, MODE, NT, NST><<<grid, NT, smem, st>>>(p);
   return check_launch(what);
+}
+
+// Host launcher: a persistent grid.  Two CTAs of 256 threads per SM when one staging buffer
+// per CTA fits twice in shared memory, else one CTA of 512 threads with two buffers
+// (TESM_WIN_VARIANT = 1 / 2 forces one of them).
+template <int W, int RM, int ES, int MODE>
+static int win_launch(WinEntParams &p, cudaStream_t st, const char *what) {
+  p.ntiles_b = (int)ceil_div(p.L, kWinT);
+  const WinGeom g1 = win_geom(W, p.R, p.D, RM, ES, MODE, 1), g2 = win_geom(W, p.R, p.D, RM, ES, MODE, 2);
+  static int force = -1;
+  if (force < 0) {
+    const char *e = getenv("TESM_WIN_VARIANT");
+    force = e ? atoi(e) : 0;
+  }
+  const bool two = win_smem_bytes(g1) <= 113 * 1024;
+  if ((two && force != 2) || (force == 1 && win_smem_bytes(g1) <= 227 * 1024))
+    return win_launch_v<W, RM, ES, MODE, 256, 1>(p, g1, two ? 2 : 1, st, what);
+  if (win_smem_bytes(g2) <= 227 * 1024) return win_launch_v<W, RM, ES, MODE, 512, 2>(p, g2, 1, st, what);
+  if (win_smem_bytes(g1) <= 227 * 1024) return win_launch_v<W, RM, ES, MODE, 256, 1>(p, g1, 1, st, what);
+  return fail(TESM_EUNSUPPORTED, std::string(what) + ": d_state / ent_rank too large for one tile in shared memory");
 }
 
 }  // namespace tesm
