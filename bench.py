@@ -485,7 +485,7 @@ def run_cfg2(args, peaks, rank=0, world=1):
                 gbs, tops = byts / t / 1e9, ops_ / t / 1e12
                 bound = "hbm" if M <= 16 else ("mixed" if M <= 128 else "tensor")
                 out.append({"workload": "cfg2 BitLinear", "N": N, "K": K, "M": M, "scale": "row" if per_row else "tensor",
-                            "path": "gemv (mma.sync, packed int2)" if M <= 64 else "tcgen05 int8",
+                            "path": "quant + row-block gemv (mma.sync, packed int2)" if M <= 64 else "tcgen05 int8",
                             "us": t * 1e6, "tokens_per_s": M / t, "GB_s": gbs, "TOPS": tops, "bound": bound,
                             "hbm_frac": gbs / peaks["hbm_gbs"]})
             del pws
