@@ -56,9 +56,9 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
 // memory.  No cluster barriers on the critical path: every weight byte of the CTA is requested
 // before the activation wait, and the activation fragments are read straight from L2 (every
 // CTA reads the same few KB of codes).
-template <int NT, int WPC>
+template <int NT, int WPC, int PF>
 __global__ void __launch_bounds__(WPC * 32, (NT >= 4 ? 1 : NT == 2 ? (WPC == 8 ? 3 : 1) : (WPC == 8 ? 5 : 2))) k_gemv_rows(GemvParams p) {
-  constexpr int TOK = NT * 8, PF = 4;
+  constexpr int TOK = NT * 8;
   __shared__ int32_t red[WPC][16][TOK + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(WPC * 32, (NT >= 4 ? 1 : NT == 2 ? (WPC == 8 ?
   }
 }
 
-template <int NT, int WPC>
+template <int NT, int WPC, int PF>
 static int launch_gemv_rows(const GemvParams &p, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ceil_div(p.N, 16), 1, 1);
@@ -159,19 +159,20 @@ static int launch_gemv_rows(const GemvParams &p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_rows<NT, WPC>, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_rows<NT, WPC, PF>, p);
   if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemv_int2 launch: ") + cudaGetErrorString(e));
   return TESM_OK;
 }
 
-// 16 warps per CTA for M <= 16 (fewer K steps per warp: one prefetch round)
+// Warps per CTA for M <= 16: short K (<= 16 steps of 256) -> 8 warps of <= 2 steps with a
+// small register budget, so the whole grid is resident in one wave; longer K -> 16 warps.
 static bool gemv_wide(const GemvParams &p) {
   static int wpc_force = -1;
   if (wpc_force < 0) {
     const char *e = getenv("TESM_GEMV_WPC");  // tuning override: 8 or 16
     wpc_force = e ? atoi(e) : 0;
   }
-  return wpc_force ? wpc_force == 16 : true;
+  return wpc_force ? wpc_force == 16 : p.steps_total > 16;
 }
 
 }  // namespace tesm
@@ -213,8 +214,8 @@ extern "C" int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const 
   p.steps_total = (int)(Kp / 256);
   cudaStream_t st = (cudaStream_t)stream;
   const bool wide = gemv_wide(p);
-  if (M <= 8) return wide ? launch_gemv_rows<1, 16>(p, st) : launch_gemv_rows<1, 8>(p, st);
-  if (M <= 16) return wide ? launch_gemv_rows<2, 16>(p, st) : launch_gemv_rows<2, 8>(p, st);
-  if (M <= 32) return launch_gemv_rows<4, 8>(p, st);
-  return launch_gemv_rows<8, 8>(p, st);
+  if (M <= 8) return wide ? launch_gemv_rows<1, 16, 4>(p, st) : launch_gemv_rows<1, 8, 2>(p, st);
+  if (M <= 16) return wide ? launch_gemv_rows<2, 16, 4>(p, st) : launch_gemv_rows<2, 8, 4>(p, st);
+  if (M <= 32) return launch_gemv_rows<4, 8, 4>(p, st);
+  return launch_gemv_rows<8, 8, 4>(p, st);
 }
