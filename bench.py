@@ -531,10 +531,10 @@ def run_cfg3(args, peaks, rank=0, world=1):
     rec("k_scan (SISO)", t, M * D * (3 * 2 + 4))  # decay, write, value bf16 in; fp32 states out
     t = _graph_time(lambda i: ops.siso_local_ent(proj, B, L, Dm, D, R, W, None, bias, states, 0.1, 0.2, 1e4, th, ch),
                     inner=4)
-    rec("k_siso_local_ent<16>", t, M * (2 * R * 2 + D * 4 + 2 * D * 2))
+    rec("k_win_ent<16> SISO local entanglement (bf16 out)", t, M * (2 * R * 2 + D * 4 + 2 * D * 2))
     t = _graph_time(lambda i: ops.siso_local_ent_codes(proj, B, L, Dm, D, R, W, None, bias, states, 0.1, 0.2, 1e4,
                                                        torch.bfloat16, 1e-5, 1e-5), inner=4)
-    rec("k_siso_local_ent_codes<16> (int8 out)", t, M * (2 * R * 2 + D * 4 + 2 * D + 8))
+    rec("k_win_ent<16> SISO local entanglement (int8 codes out)", t, M * (2 * R * 2 + D * 4 + 2 * D + 8))
     emb = torch.randn(64, device="cuda") * 0.02
     relb = ops.global_relbias(emb, 1.0, 0.0, L)
     fl = B * (L * L / 2) * (2 * R + 2 * D)  # algorithmic: causal half, q.k and t.v once each
@@ -589,7 +589,7 @@ def run_cfg4(args, peaks, rank=0, world=1):
     return [{"workload": "cfg4 MIMO layer", "n_gpus": world, "tokens_per_s": B * world * L / t, "ms": t * 1e3},
             {"kernel": "k_scan (MIMO, 4 ranks)", "n_gpus": world, "ms": ts * 1e3, "GB_s": E * (6 + 16) / ts / 1e9,
              "hbm_frac": E * (6 + 16) / ts / 1e9 / world / peaks["hbm_gbs"], "algorithmic_bytes": E * 22},
-            {"kernel": "k_mimo_local_ent<16,4>", "n_gpus": world, "ms": te * 1e3, "GB_s": ent_bytes / te / 1e9,
+            {"kernel": "k_win_ent<16,4> MIMO local entanglement", "n_gpus": world, "ms": te * 1e3, "GB_s": ent_bytes / te / 1e9,
              "hbm_frac": ent_bytes / te / 1e9 / world / peaks["hbm_gbs"], "algorithmic_bytes": ent_bytes}]
 
 
