@@ -415,6 +415,30 @@ def run_kernel_case(args):
     return 0
 
 
+def run_skinny_case(args):
+    """Decode-batch BitLinear GEMMs of config 5 (M = 256 rows, int8 codes x ternary weights on
+    tcgen05): in_proj, out_proj and down_proj shapes, graph-timed with rotating weight copies
+    (> L2) so every call streams its weights from HBM.  One JSON line per shape."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    peaks, _ = load_peaks()
+    M = 256
+    for name, N, K in [("in_proj", 9088, 4096), ("out_proj", 4096, 4096), ("down_proj", 4096, 11008)]:
+        ncopy = max(2, int(3 * 126e6 // (N * K)) + 1)
+        w = torch.randn(N, K, device="cuda") * 0.02
+        pws = [ops.pack_weight(w.roll(i, 0), 1e-5, with_tern=True) for i in range(ncopy)]
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        codes, inv, _ = ops.quant_act(x, 1e-5, ops.LAYOUT_ROWMAJOR)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        t = _graph_time(lambda i: ops.gemm(codes, inv, pws[i % ncopy], M, torch.bfloat16, out), inner=ncopy)
+        wbytes = N * ((K + 255) // 256 * 256)  # int8 ternary operand the tensor cores read
+        print(json.dumps({"kernel": "skinny gemm_i8", "shape": name, "M": M, "N": N, "K": K, "us": t * 1e6,
+                          "TOPS": 2.0 * M * N * K / t / 1e12, "weight_GB_s": wbytes / t / 1e9,
+                          "hbm_frac": wbytes / t / 1e9 / peaks["hbm_gbs"]}), flush=True)
+    return 0
+
+
 def run_decode_case(args):
     """Config-5 model, batch 256: 16-token prefill then `steps` eager one-token decode steps
     (the kernels a decode graph replays), for launch-list captures."""
@@ -640,7 +664,8 @@ def main():
     ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg4"],
                     help="supplementary measurements of BASELINE configs 2-4 (one JSON line per measurement)")
     ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
-    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine"], help="run a small ncu case")
+    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine", "skinny"],
+                    help="run a small ncu case")
     args = ap.parse_args()
     if args.workload:
         return run_workload(args)
@@ -648,6 +673,8 @@ def main():
         return run_decode_case(args)
     if args.kernel == "combine":
         return run_combine_case(args)
+    if args.kernel == "skinny":
+        return run_skinny_case(args)
     if args.kernel:
         return run_kernel_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -953,11 +953,22 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
   cudaStream_t st = (cudaStream_t)stream;
-  if (M <= 256) {  // decode-sized batches: skinny tiles, enough CTAs, weights streamed once
+  if (M <= 256) {  // decode-sized batches: narrow tiles, enough CTAs, weights streamed once
     static const int forced = [] {
       const char *e = getenv("TESM_SKINNY_BN");  // tuning override: 32, 64 or 128
       return e ? atoi(e) : 0;
     }();
+    // CTA pairs (M = 256 MMAs, cta_group::2): each CTA stages only its 128 activation rows and
+    // half of the weight tile, so per-CTA bytes per k-block halve and twice as many SMs work
+    // (TESM_SKINNY_PAIR=0 selects the single-CTA skinny tiles below)
+    static const int pair = [] {
+      const char *e = getenv("TESM_SKINNY_PAIR");
+      return e ? atoi(e) : 1;
+    }();
+    if (pair && forced == 0) {
+      if (N >= 8192) return tc::launch<128, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
+      return tc::launch<64, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
+    }
     if (forced == 128) return tc::launch<128, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     if (forced == 64) return tc::launch<64, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
     if (forced == 32) return tc::launch<32, false, 2>(codes, ld_codes, tern, ld_tern, p, st);
