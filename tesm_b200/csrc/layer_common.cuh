@@ -62,54 +62,6 @@ __device__ __forceinline__ void load_rope_row(float *dst, const ProjCols &pc, in
   }
 }
 
-// Same rotation with a precomputed inverse-frequency table (R/2 entries, identical values).
-__device__ __forceinline__ void load_rope_row_tab(float *dst, const ProjCols &pc, int col, int64_t row, int R,
-                                                  int pos, const float *invf, const float *add, int tid, int nthr) {
-  const int half = R / 2;
-  for (int i = tid; i < half; i += nthr) {
-    const float x1 = load_f(pc.proj, pc.dtype, row * pc.ld + col + i);
-    const float x2 = load_f(pc.proj, pc.dtype, row * pc.ld + col + half + i);
-    float sn, cs;
-    sincosf((float)pos * invf[i], &sn, &cs);
-    float o1 = x1 * cs - x2 * sn, o2 = x1 * sn + x2 * cs;
-    if (add) {
-      o1 += add[i];
-      o2 += add[half + i];
-    }
-    dst[i] = o1;
-    dst[half + i] = o2;
-  }
-}
-
-// Window scores for T query rows: one thread per (t, lag); raw ternary in tw, then each row is
-// divided by max(sum |tern|, 1).  valid(gt, o) decides which lags take part.
-template <int W, class Valid>
-__device__ __forceinline__ void window_scores(const float *qs, const float *ks, int RP, int R, int nt, int t0,
-                                              const float *bias_row, float sqrt_r, float thr, float *tw,
-                                              Valid valid) {
-  for (int i = threadIdx.x; i < nt * W; i += blockDim.x) {
-    const int t = i / W, o = i - t * W;
-    float tv = 0.f;
-    if (valid(t0 + t, o)) {
-      const float *qr = qs + t * RP;
-      const float *kr = ks + (t + W - 1 - o) * RP;
-      float dot = 0.f;
-      for (int c = 0; c < R; ++c) dot = fmaf(qr[c], kr[c], dot);
-      tv = ternary_of(__fdiv_rn(dot, sqrt_r) + bias_row[W - 1 - o], thr);
-    }
-    tw[i] = tv;
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < nt; t += blockDim.x) {
-    float cnt = 0.f;
-#pragma unroll
-    for (int o = 0; o < W; ++o) cnt += fabsf(tw[t * W + o]);
-    const float inv = 1.f / fmaxf(cnt, 1.f);
-#pragma unroll
-    for (int o = 0; o < W; ++o) tw[t * W + o] = tw[t * W + o] * inv;
-  }
-}
-
 __device__ __forceinline__ int ld_acquire(const int *p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");

@@ -263,18 +263,6 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
 // through shared memory, and CTAs chain by the same decoupled look-back as k_scan.
 constexpr int SLICE2 = 256;
 
-#ifdef TESM_SCAN_TRACE  // development-only per-CTA phase timestamps (globaltimer ns)
-__device__ unsigned long long g_scan_trace[8192][8];
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-#define SCAN_MARK(k, v) \
-  if (threadIdx.x == 0 && tile < 8192) g_scan_trace[tile][k] = (v);
-#else
-#define SCAN_MARK(k, v)
-#endif
 
 __device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
   uint32_t v;
@@ -322,7 +310,6 @@ __device__ __forceinline__ float write_value(float w, float v) {
 
 template <int TT, int G>
 __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
-  constexpr int NT = 128 * G;
   __shared__ float4 s_map[G][128];  // per time group: (A0, A1, U0, U1)
   __shared__ float2 s_carry[128];   // carry entering the chunk
   __shared__ int s_tile;
@@ -334,7 +321,6 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
   const int bs = tile - chunk * per_chunk;
   const int b = bs / p.nslices, slice = bs - b * p.nslices;
   const int g = threadIdx.x >> 7, cp = threadIdx.x & 127;
-  SCAN_MARK(0, gtimer());
   const int c = slice * SLICE2 + 2 * cp;
   const bool active = c < p.C;  // C even: both channels or neither
   const int t0 = chunk * (G * TT) + g * TT;
@@ -376,7 +362,6 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
   // combine the time groups: exclusive map E of groups 0..g-1, total map of the chunk
   s_map[g][cp] = make_float4(A0, A1, U0, U1);
   __syncthreads();
-  SCAN_MARK(1, gtimer());
   float EA0 = 1.f, EA1 = 1.f, EU0 = 0.f, EU1 = 0.f, TA0, TA1, TU0, TU1;
 #pragma unroll
   for (int k = 0; k < G; ++k) {
@@ -400,7 +385,6 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
       st_relaxed_f2(p.aggA + cidx * p.C + c, EA0, EA1);
       st_relaxed_f2(p.aggU + cidx * p.C + c, EU0, EU1);
     }
-    SCAN_MARK(2, gtimer());
     float h0 = 0.f, h1 = 0.f;
     if (active && p.h0) {
       h0 = (float)p.h0[(int64_t)b * p.C + c];
@@ -444,13 +428,11 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
         }
       }
     }
-    SCAN_MARK(3, gtimer());
     s_carry[cp] = make_float2(h0, h1);
     if (active && chunk + 1 < p.nchunks)
       st_relaxed_f2(p.incl + cidx * p.C + c, fmaf(EA0, h0, EU0), fmaf(EA1, h1, EU1));
   }
   __syncthreads();
-  SCAN_MARK(4, gtimer());
   if (!active) return;
   const float2 hin = s_carry[cp];
   float h0 = fmaf(TA0, hin.x, TU0), h1 = fmaf(TA1, hin.y, TU1);
@@ -468,14 +450,6 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
       }
     }
   }
-#ifdef TESM_SCAN_TRACE
-  if (tile < 8192 && threadIdx.x == 0) {
-    unsigned smid;
-    asm volatile("mov.u32 %0, %smid;" : "=r"(smid));
-    g_scan_trace[tile][5] = gtimer();
-    g_scan_trace[tile][7] = smid;
-  }
-#endif
 }
 
 struct ScanLayout {
@@ -600,11 +574,6 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
 
 using namespace tesm;
 
-#ifdef TESM_SCAN_TRACE
-extern "C" int tesm_b200_scan_trace_read(unsigned long long *host) {
-  return cudaMemcpyFromSymbol(host, tesm::g_scan_trace, sizeof(tesm::g_scan_trace)) == cudaSuccess ? 0 : 3;
-}
-#endif
 
 extern "C" int tesm_b200_scan_workspace(int64_t B, int64_t L, int64_t C, int64_t RM, int64_t *bytes) {
   TESM_REQUIRE(bytes && B > 0 && L > 0 && C > 0 && RM > 0, "scan_workspace: bad argument");
