@@ -960,12 +960,12 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
     }();
     // CTA pairs (M = 256 MMAs, cta_group::2): each CTA stages only its 128 activation rows and
     // half of the weight tile, so per-CTA bytes per k-block halve and twice as many SMs work
-    // (TESM_SKINNY_PAIR=0 selects the single-CTA skinny tiles below)
+    // (TESM_SKINNY_PAIR=0 selects the single-CTA skinny tiles below for every M)
     static const int pair = [] {
       const char *e = getenv("TESM_SKINNY_PAIR");
       return e ? atoi(e) : 1;
     }();
-    if (pair && forced == 0) {
+    if (pair && forced == 0 && M > 128) {  // <= 128 rows would leave half of each pair tile empty
       if (N >= 8192) return tc::launch<128, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
       return tc::launch<64, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
     }
