@@ -363,32 +363,50 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(WinEntParams p
       }
     }
     __syncthreads();
-    // scores: lane = (row t, lag o); the row's W lanes are adjacent
+    // scores: lane = (row t, lag group og) with lags og + j * OG, j < LPT, so one q load feeds
+    // LPT independent dot products; the row's OG lanes are adjacent (shuffle-summed count)
     {
+      constexpr int LPT = (kWinT * W) / NT >= 2 ? (kWinT * W) / NT : 1;  // lags per lane
+      constexpr int OG = W / LPT;                                        // lanes per row
       const float *brow = p.bias + (MODE == kWinMimo ? h * W : 0);
-      for (int item = tid; item < kWinT * W; item += NT) {
-        const int t = item / W, o = item - t * W;  // W compile-time
-        float tv = 0.f;
+      for (int item = tid; item < kWinT * OG; item += NT) {
+        const int t = item / OG, og = item - t * OG;  // OG compile-time
+        float tv[LPT];
+#pragma unroll
+        for (int j = 0; j < LPT; ++j) tv[j] = 0.f;
         if (t < nt) {
-          const float *qr = s.qs + t * RP, *kr = s.ks + (t + W - 1 - o) * RP;
-          float d0 = 0.f;
+          const float *qr = s.qs + t * RP, *k0 = s.ks + (t + W - 1 - og) * RP;
+          float d[LPT];
+#pragma unroll
+          for (int j = 0; j < LPT; ++j) d[j] = 0.f;
           for (int c = 0; c < R4; c += 4) {
             const float4 q4 = *reinterpret_cast<const float4 *>(qr + c);
-            const float4 k4 = *reinterpret_cast<const float4 *>(kr + c);
-            d0 = fmaf(q4.x, k4.x, d0);
-            d0 = fmaf(q4.y, k4.y, d0);
-            d0 = fmaf(q4.z, k4.z, d0);
-            d0 = fmaf(q4.w, k4.w, d0);
+#pragma unroll
+            for (int j = 0; j < LPT; ++j) {
+              const float4 k4 = *reinterpret_cast<const float4 *>(k0 - j * OG * RP + c);  // lag og + j*OG
+              d[j] = fmaf(q4.x, k4.x, d[j]);
+              d[j] = fmaf(q4.y, k4.y, d[j]);
+              d[j] = fmaf(q4.z, k4.z, d[j]);
+              d[j] = fmaf(q4.w, k4.w, d[j]);
+            }
           }
           const int gt = t0 + t;
-          if (gt - o >= 0 && (MODE != kWinMimo || !p.quirk || o >= W - 1 - gt))
-            tv = ternary_of(__fdiv_rn(d0, p.sqrt_r) + brow[W - 1 - o], p.thr);
-        }
-        s.twr[item] = tv;
-        float cnt = fabsf(tv);
 #pragma unroll
-        for (int m = W / 2; m >= 1; m >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, m);
-        if (o == 0) s.inv[t] = 1.f / fmaxf(cnt, 1.f);
+          for (int j = 0; j < LPT; ++j) {
+            const int o = og + j * OG;
+            if (gt - o >= 0 && (MODE != kWinMimo || !p.quirk || o >= W - 1 - gt))
+              tv[j] = ternary_of(__fdiv_rn(d[j], p.sqrt_r) + brow[W - 1 - o], p.thr);
+          }
+        }
+        float cnt = 0.f;
+#pragma unroll
+        for (int j = 0; j < LPT; ++j) {
+          s.twr[t * W + og + j * OG] = tv[j];
+          cnt += fabsf(tv[j]);
+        }
+#pragma unroll
+        for (int m = OG / 2; m >= 1; m >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, m);
+        if (og == 0) s.inv[t] = 1.f / fmaxf(cnt, 1.f);
       }
     }
     __syncthreads();
@@ -442,32 +460,30 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(WinEntParams p
           if (t >= nt || !has_x) continue;
           const float iv = s.inv[t];
           const float *srow = st + (size_t)(t + W - 1) * SRR + ch;
-          float ex = 0.f, ey = 0.f, cx = 0.f, cy = 0.f;
+          // the two channels ch, ch+1 in packed fp32 (FFMA2): e = s + es (acc / norm - s)
+          const float2 iv2 = make_float2(iv, iv), es2 = make_float2(es, es);
+          float2 E = make_float2(0.f, 0.f), Cg = make_float2(0.f, 0.f);
 #pragma unroll
           for (int k = 0; k < RM; ++k) {
-            float sx, sy;
+            float2 sv;
             if (has_y) {
-              const float2 v = *reinterpret_cast<const float2 *>(srow + k * SR);  // ch even, SR % 4 == 0
-              sx = v.x;
-              sy = v.y;
+              sv = *reinterpret_cast<const float2 *>(srow + k * SR);  // ch even, SR % 4 == 0
             } else {
-              sx = srow[k * SR];
-              sy = 0.f;
+              sv = make_float2(srow[k * SR], 0.f);
             }
-            const float e0 = sx + es * (acc[k][2 * hr] * iv - sx);
-            const float e1 = sy + es * (acc[k][2 * hr + 1] * iv - sy);
+            const float2 nsv = make_float2(-sv.x, -sv.y);
+            const float2 dlt = __ffma2_rn(make_float2(acc[k][2 * hr], acc[k][2 * hr + 1]), iv2, nsv);
+            const float2 e = __ffma2_rn(es2, dlt, sv);
+            const float2 chg = __fadd2_rn(e, nsv);
             if (MODE == kWinMimo) {
-              ex = fmaf(mo[k].x, e0, ex);
-              ey = fmaf(mo[k].y, e1, ey);
-              cx = fmaf(mo[k].x, e0 - sx, cx);
-              cy = fmaf(mo[k].y, e1 - sy, cy);
+              E = __ffma2_rn(mo[k], e, E);
+              Cg = __ffma2_rn(mo[k], chg, Cg);
             } else {
-              ex = e0;
-              ey = e1;
-              cx = e0 - sx;
-              cy = e1 - sy;
+              E = e;
+              Cg = chg;
             }
           }
+          const float ex = E.x, ey = E.y, cx = Cg.x, cy = Cg.y;
           if (MODE == kWinSisoCodes) {
             float *rt = s.oT + t * (D + 1) + ch, *rc = s.oC + t * (D + 1) + ch;
             rt[0] = round_to(p.act_dtype, win_tanh(ex));
