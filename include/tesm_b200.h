@@ -65,6 +65,13 @@ int tesm_b200_pack_ternary(const void *w, int dtype, int64_t N, int64_t K, int64
                            const float *scale, uint8_t *packed, int64_t ld_packed, int8_t *tern, int64_t ld_tern,
                            tesm_stream_t stream);
 
+/* Packed INT2 bytes (the format of pack_int2_to_uint8, int2_quantization.py:21-60) -> the
+ * int8 ternary operand of tesm_b200_gemm_i8 (unpack_uint8_to_int2, int2_quantization.py:64-94,
+ * without the dequantisation): tern[n, k] = code(n, k) - 1 for k < Kp (Kp a multiple of 16).
+ * Loads exported INT2 weights without going back to the latent weights. */
+int tesm_b200_unpack_ternary(const uint8_t *packed, int64_t ld_packed, int64_t N, int64_t Kp, int8_t *tern,
+                             int64_t ld_tern, tesm_stream_t stream);
+
 /* Per-token int8 activation quantisation of BitLinear.quantized_input (tesm.py:206-209):
  * s = 127 * fl(1/max(max|x|, eps)), c = clamp(round(x*s), -128, 127), bit-exact codes for
  * fp32 and bf16 input.  inv_scale[m] = 1/s.  layout TESM_LAYOUT_GEMV writes the permuted

@@ -28,6 +28,7 @@ SIGNATURES = {
     "tesm_b200_device_status": [c_vp],
     "tesm_b200_weight_scale": [c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_float, c_vp, c_vp, c_vp, c_vp],
     "tesm_b200_pack_ternary": [c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp],
+    "tesm_b200_unpack_ternary": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp],
     "tesm_b200_quant_act": [c_vp, c_int, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_int, c_vp, c_vp, c_vp],
     "tesm_b200_gemv_int2": [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int,
                             c_i64, c_vp, c_i64, c_vp],

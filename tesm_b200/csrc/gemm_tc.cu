@@ -965,7 +965,10 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
       const char *e = getenv("TESM_SKINNY_PAIR");
       return e ? atoi(e) : 1;
     }();
-    if (pair && forced == 0 && M > 128) {  // <= 128 rows would leave half of each pair tile empty
+    // up to 128 rows leave half of each pair tile empty: pairs still win when N is small (fewer,
+    // longer-K tiles: 4096 x 11008 at M = 128, 34.5 vs 43.7 us) but not for wide N
+    // (11008 x 4096: 29.3 vs 24.8 us)
+    if (pair && forced == 0 && (M > 128 || N < 8192)) {
       if (N >= 8192) return tc::launch<128, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
       return tc::launch<64, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
     }

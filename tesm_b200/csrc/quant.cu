@@ -85,6 +85,27 @@ __global__ void k_pack(const void *__restrict__ w, int dtype, int64_t N, int64_t
   }
 }
 
+// Packed INT2 bytes -> int8 ternary operand (unpack_uint8_to_int2, int2_quantization.py:64-94:
+// code c in bits 2i..2i+1 of byte j is column 4j + i, t = c - 1).  One thread per packed word of
+// 4 bytes = 16 columns; padding codes (1) give t = 0.
+__global__ void k_unpack(const uint8_t *__restrict__ packed, int64_t ld_packed, int64_t N, int64_t words_per_row,
+                         int8_t *__restrict__ tern, int64_t ld_tern) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= N * words_per_row) return;
+  const int64_t row = gid / words_per_row, wd = gid - row * words_per_row;
+  const uint32_t w = reinterpret_cast<const uint32_t *>(packed + row * ld_packed)[wd];
+  uint32_t out[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {  // byte q of the word -> columns 4q .. 4q+3
+    const uint32_t b = (w >> (8 * q)) & 0xffu;
+    uint32_t v = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v |= (uint32_t)(uint8_t)(int8_t)((int)((b >> (2 * i)) & 3u) - 1) << (8 * i);
+    out[q] = v;
+  }
+  reinterpret_cast<uint4 *>(tern + row * ld_tern)[wd] = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 // ---------------------------------------------------------------- activation quant
 // One block per row; each thread owns up to GPT 16-element groups kept in registers
 // (16-byte vector loads when the row is aligned).
@@ -252,4 +273,16 @@ extern "C" int tesm_b200_row_absmax(const void *x, int dtype, int64_t M, int64_t
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
   k_row_absmax<<<(unsigned)M, 128, 0, (cudaStream_t)stream>>>(x, dtype, K, ldx, vec, amax);
   return check_launch("row_absmax");
+}
+
+extern "C" int tesm_b200_unpack_ternary(const uint8_t *packed, int64_t ld_packed, int64_t N, int64_t Kp,
+                                        int8_t *tern, int64_t ld_tern, tesm_stream_t stream) {
+  TESM_REQUIRE(packed && tern && N > 0 && Kp > 0 && Kp % 16 == 0, "unpack_ternary: need Kp a multiple of 16");
+  TESM_REQUIRE(ld_packed >= Kp / 4 && ld_packed % 4 == 0 && ((uintptr_t)packed & 3) == 0,
+               "unpack_ternary: packed rows must hold Kp / 4 bytes, 4-byte aligned");
+  TESM_REQUIRE(ld_tern >= Kp && ld_tern % 16 == 0 && ((uintptr_t)tern & 15) == 0,
+               "unpack_ternary: tern rows must hold Kp bytes, 16-byte aligned");
+  const int64_t wpr = Kp / 16, total = N * wpr;
+  k_unpack<<<(unsigned)ceil_div(total, 256), 256, 0, (cudaStream_t)stream>>>(packed, ld_packed, N, wpr, tern, ld_tern);
+  return check_launch("unpack_ternary");
 }

@@ -58,7 +58,11 @@ def _param_cache(mod, name: str) -> torch.Tensor:
 # ------------------------------------------------------------------ BitLinear
 def packed_weight(lin, need_tern: bool = False) -> ops.PackedWeight:
     """Device ternary weight of a BitLinear, rebuilt whenever the weight changes
-    (mirrors the eval-mode cache keyed on weight._version, tesm.py:226-236)."""
+    (mirrors the eval-mode cache keyed on weight._version, tesm.py:226-236).  A weight imported
+    from an INT2 export (``tesm_b200.int2``) takes precedence over the latent weight."""
+    imported = lin.__dict__.get("_b200_int2")
+    if imported is not None:
+        return imported
     w = lin.weight
     key = (w.data_ptr(), w._version, w.dtype, tuple(w.shape))
     cache = lin.__dict__.get("_b200")
@@ -187,7 +191,8 @@ def combine_weight(mod):
     """[state_proj | ent_proj] ternary rows side by side (each half D rounded up to 128, zero
     padded) for the dual-accumulator combine GEMM, plus the two dequantisation scalars."""
     sw, ew = mod.state_proj.weight, mod.ent_proj.weight
-    key = (sw.data_ptr(), sw._version, ew.data_ptr(), ew._version)
+    key = (sw.data_ptr(), sw._version, ew.data_ptr(), ew._version, id(mod.state_proj.__dict__.get("_b200_int2")),
+           id(mod.ent_proj.__dict__.get("_b200_int2")))
     hit = mod.__dict__.get("_b200_comb")
     if hit is None or hit[0] != key:
         ps = packed_weight(mod.state_proj, need_tern=True)
@@ -404,8 +409,26 @@ def ffn_packed(ffn):
     d_intermediate % 128 == 0 the rows are interleaved in blocks of 128 ([gate | up] per block)
     so the tensor-core GEMM applies the SiLU gate in its epilogue."""
     g, u = ffn.gate_proj.weight, ffn.up_proj.weight
-    key = (g.data_ptr(), g._version, u.data_ptr(), u._version)
+    gi, ui = ffn.gate_proj.__dict__.get("_b200_int2"), ffn.up_proj.__dict__.get("_b200_int2")
+    key = (g.data_ptr(), g._version, u.data_ptr(), u._version, id(gi), id(ui))
     hit = ffn.__dict__.get("_b200_gu")
+    if (hit is None or hit[0] != key) and (gi is not None or ui is not None):
+        # imported INT2 weights: interleave the two imported (or packed latent) weights' rows
+        pg, pu = packed_weight(ffn.gate_proj, True), packed_weight(ffn.up_proj, True)
+        Fd, K = pg.N, pg.K
+        dev = pg.packed.device
+        blk = SWIGLU_BLK if Fd % SWIGLU_BLK == 0 else 0
+        f = torch.arange(Fd, device=dev)
+        packed = torch.empty(2 * Fd, pg.packed.shape[1], device=dev, dtype=torch.uint8)
+        tern = torch.empty(2 * Fd, pg.tern.shape[1], device=dev, dtype=torch.int8)
+        deq = torch.empty(2 * Fd, device=dev, dtype=torch.float32)
+        for i, pw_i in enumerate((pg, pu)):
+            dst = (f // blk) * 2 * blk + i * blk + f % blk if blk else f + i * Fd
+            packed[dst] = pw_i.packed
+            tern[dst] = pw_i.tern
+            deq[dst] = pw_i.deq.expand(Fd)
+        hit = (key, ops.PackedWeight(packed, tern, deq.clone(), deq, 2 * Fd, K, True), blk)
+        ffn.__dict__["_b200_gu"] = hit
     if hit is None or hit[0] != key:
         Fd, K = g.shape
         Kp = ops.round_up(K, 256)

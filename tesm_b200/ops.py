@@ -88,6 +88,27 @@ def pack_weight(w: torch.Tensor, eps: float = 1e-5, per_row: bool = False, with_
     return PackedWeight(packed, tern, scale, deq, N, K, per_row)
 
 
+def packed_from_int2(packed: torch.Tensor, weight_scale, K: int, device) -> PackedWeight:
+    """PackedWeight from an exported INT2 weight (pack_int2_to_uint8 bytes, (N, ceil(K/4)) uint8,
+    and its weight_scale = 1 / mean|W|; int2_quantization.py:21-60): the bytes are kept as they
+    are (rows padded with code 1 up to K rounded to 256) and the int8 ternary operand of the
+    tensor-core GEMM is unpacked from them on the device."""
+    N, kb = packed.shape
+    if packed.dtype != torch.uint8 or kb != (K + 3) // 4:
+        raise ValueError(f"packed INT2 weight must be uint8 (N, ceil(K/4)) = (N, {(K + 3) // 4}), got "
+                         f"{tuple(packed.shape)} {packed.dtype}")
+    Kp = round_up(K, 256)
+    dev = torch.device(device)
+    buf = torch.full((N, Kp // 4), 0x55, device=dev, dtype=torch.uint8)
+    buf[:, :kb] = packed.to(dev)
+    scale = torch.as_tensor(weight_scale, dtype=torch.float32).reshape(1).to(dev)
+    deq = torch.reciprocal(scale)
+    tern = torch.empty(N, Kp, device=dev, dtype=torch.int8)
+    _lib.call("tesm_b200_unpack_ternary", buf.data_ptr(), buf.stride(0), N, Kp, tern.data_ptr(), tern.stride(0),
+              _stream())
+    return PackedWeight(buf, tern, scale, deq, N, K, False)
+
+
 def ensure_tern(pw: PackedWeight, w: torch.Tensor):
     if pw.tern is None:
         Kp = round_up(pw.K, 256)

@@ -26,6 +26,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import ops
+from ._lib import TesmError
 
 
 @dataclass
@@ -70,8 +71,16 @@ def _all_reduce(t: torch.Tensor, op: str, tp: TPGroup):
 
 
 # ------------------------------------------------------------------ shards
+def _no_imported(*lins):
+    for lin in lins:
+        if "_b200_int2" in lin.__dict__:
+            raise TesmError("tesm_b200: tensor-parallel shards are cut from the latent weights; weights "
+                            "imported from an INT2 export are supported on one GPU / data-parallel only")
+
+
 def ffn_shards(ffn, tp: TPGroup, blk: int = 128):
     """(interleaved gate/up shard, down_proj column shard, (f0, f1)) of this rank, cached."""
+    _no_imported(ffn.gate_proj, ffn.up_proj, ffn.down_proj)
     g, u, d = ffn.gate_proj.weight, ffn.up_proj.weight, ffn.down_proj.weight
     key = (g.data_ptr(), g._version, u.data_ptr(), u._version, d.data_ptr(), d._version, tp.rank, tp.world)
     hit = ffn.__dict__.get("_b200_tp_shards")
@@ -103,6 +112,7 @@ def ffn_shards(ffn, tp: TPGroup, blk: int = 128):
 
 
 def out_proj_shard(mixer, tp: TPGroup):
+    _no_imported(mixer.out_proj)
     w = mixer.out_proj.weight
     key = (w.data_ptr(), w._version, tp.rank, tp.world)
     hit = mixer.__dict__.get("_b200_tp_out")

@@ -32,7 +32,7 @@ from tesm_ssm.modules.tesm import BitLinear, TESM_SISO  # noqa: E402
 from tesm_ssm.modules.tesm_mimo import TESMMIMO_Optimized  # noqa: E402
 from tesm_ssm.models.config_tesm import TESMConfig  # noqa: E402
 from tesm_ssm.models.mixer_seq_simple import TESMLMHeadModel  # noqa: E402
-from tesm_ssm.utils.int2_quantization import pack_int2_to_uint8  # noqa: E402
+from tesm_ssm.utils.int2_quantization import export_model_to_int2, pack_int2_to_uint8  # noqa: E402
 
 import cases  # noqa: E402  (shared case table; no reference import inside)
 
@@ -152,6 +152,22 @@ def run_model(c):
     save("model_" + c["name"], **out)
 
 
+def gen_int2_export():
+    """The reference's on-disk INT2 export (export_model_to_int2, int2_quantization.py:196-217) of
+    the tiny SISO model of cases.MODEL: per BitLinear its packed bytes and weight_scale."""
+    c = cases.MODEL[0]
+    torch.manual_seed(0)
+    cfg = TESMConfig(kernel_backend="torch", **c["cfg"])
+    m = TESMLMHeadModel(cfg).eval()
+    ex = export_model_to_int2(m)
+    out = {"sd_sha256": sd_hash(m), "names": np.array(sorted(ex))}
+    for name, d in ex.items():
+        out[name + "/packed"] = t2n(d["packed_weight"])
+        out[name + "/scale"] = np.asarray(float(d["weight_scale"]), np.float32)
+        out[name + "/shape"] = np.array([d["out_features"], d["in_features"]])
+    save("int2_export_tiny", **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(8)
     gen_bitlinear()
@@ -161,3 +177,4 @@ if __name__ == "__main__":
         run_mimo(c)
     for c in cases.MODEL:
         run_model(c)
+    gen_int2_export()
