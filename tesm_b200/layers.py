@@ -16,6 +16,7 @@ import torch.nn.functional as F
 from . import ops
 from . import parallel
 from ._lib import TesmError
+from .paged_cache import PagedStateCache, snapshot_if_due
 
 B200 = "b200"
 
@@ -114,21 +115,34 @@ def _new_cache(batch, W, state_shape, kshape, vshape, dev, dtype):
     }
 
 
+def _with_pages(cache, kwargs, max_seqlen, batch, d_state, ent_rank, W, dev):
+    """``use_paged_cache=True`` with max_seqlen > 1024 adds the paged snapshot store
+    (tesm.py:636-657; page_size and max_gpu_pages keyword arguments as the reference)."""
+    if kwargs.get("use_paged_cache", False) and max_seqlen > 1024:
+        cache["use_paged"] = True
+        cache["paged_cache"] = PagedStateCache(batch_size=batch, d_state=d_state, ent_rank=ent_rank, window=W,
+                                               page_size=kwargs.get("page_size", 512),
+                                               max_gpu_pages=kwargs.get("max_gpu_pages", 100), device=dev)
+    return cache
+
+
 def siso_alloc_cache(mod, batch_size, max_seqlen, dtype=None, **kwargs):
-    """Non-paged cache with the reference's keys (tesm.py:659-670); the recurrent state is
-    fp64 like the reference, the window caches fp32 on the device, plus a device
-    (seq_pos, cache_idx) pair used by the decode kernel."""
+    """Cache with the reference's keys (tesm.py:620-670); the recurrent state is fp64 like the
+    reference, the window caches fp32 on the device, plus a device (seq_pos, cache_idx) pair
+    used by the decode kernel."""
     W = max(mod.entanglement_window, 1)
-    return _new_cache(batch_size, W, (mod.d_state,), (mod.ent_rank,), (mod.d_state,), mod.out_proj.weight.device,
-                      dtype)
+    dev = mod.out_proj.weight.device
+    c = _new_cache(batch_size, W, (mod.d_state,), (mod.ent_rank,), (mod.d_state,), dev, dtype)
+    return _with_pages(c, kwargs, max_seqlen, batch_size, mod.d_state, mod.ent_rank, W, dev)
 
 
 def mimo_alloc_cache(mod, batch_size, max_seqlen, dtype=None, **kwargs):
     """MIMO cache (tesm_mimo.py:719-731): state (B, H, D), windows (B, W, H, R|D)."""
     W = max(mod.entanglement_window, 1)
     H = mod.n_heads
-    return _new_cache(batch_size, W, (H, mod.d_state), (H, mod.ent_rank), (H, mod.d_state),
-                      mod.out_proj.weight.device, dtype)
+    dev = mod.out_proj.weight.device
+    c = _new_cache(batch_size, W, (H, mod.d_state), (H, mod.ent_rank), (H, mod.d_state), dev, dtype)
+    return _with_pages(c, kwargs, max_seqlen, batch_size, H * mod.d_state, H * mod.ent_rank, W, dev)
 
 
 def _prepare_cache(cache, dev):
@@ -267,6 +281,7 @@ def siso_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(B, Dm))
     dev = q.codes.device
     _prepare_cache(cache, dev)
+    snapshot_if_due(cache)
     W = cache["ent_k_cache"].shape[1]
     proj = linear_q(mod.in_proj, q, act_dtype)
     cross_bias = None
@@ -337,6 +352,7 @@ def mimo_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(B, Dm))
     dev = q.codes.device
     _prepare_cache(cache, dev)
+    snapshot_if_due(cache)
     W = cache["ent_k_cache"].shape[1]
     proj = linear_q(mod.in_proj, q, act_dtype)
     cross_bias = None
@@ -598,6 +614,8 @@ class DecodeGraph:
             c["seq_pos"], c["cache_idx"], c["_ctl_host"] = h
 
     def step(self):
+        for c in self.caches.values():  # paged snapshots are host-driven, outside the graph
+            snapshot_if_due(c)
         self.graph.replay()
         for c in self.caches.values():
             _advance_host(c, c["ent_k_cache"].shape[1])
