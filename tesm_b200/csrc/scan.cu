@@ -45,60 +45,107 @@ __device__ __forceinline__ float step(float a, float h, float u) {
 // decay_bias); SISO plane 1 = u = sigmoid(write) * tanh(value); MIMO planes 1, 2 = sigmoid(write),
 // tanh(value) (the ranks are formed on the fly).  Rows are read once with 16-byte loads when
 // rows and column offsets are aligned.  (sigmoid with __expf: relative error ~1e-7.)
+template <bool MIMO, int VPT>
+__device__ __forceinline__ void stage_store(const ScanParams &p, int o, int c, const float *dv, const float *wv,
+                                            const float *vv, float *s0, float *s1, float *s2) {
+  float a[VPT], x[VPT], y[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    a[j] = fast_sigmoid(dv[j] + p.decay_bias[c + j]);
+    const float w = fast_sigmoid(wv[j]), v = tanhf(vv[j]);
+    x[j] = MIMO ? w : w * v;
+    y[j] = v;
+  }
+  if (VPT == 8 || VPT == 4) {  // 16-byte stores (o is a multiple of VPT)
+#pragma unroll
+    for (int q = 0; q < VPT; q += 4) {
+      *reinterpret_cast<float4 *>(s0 + o + q) = make_float4(a[q], a[q + 1], a[q + 2], a[q + 3]);
+      *reinterpret_cast<float4 *>(s1 + o + q) = make_float4(x[q], x[q + 1], x[q + 2], x[q + 3]);
+      if (MIMO) *reinterpret_cast<float4 *>(s2 + o + q) = make_float4(y[q], y[q + 1], y[q + 2], y[q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      s0[o + j] = a[j];
+      s1[o + j] = x[j];
+      if (MIMO) s2[o + j] = y[j];
+    }
+  }
+}
+
+// Stage the chunk's inputs in shared memory, transformed once: plane 0 = a = sigmoid(decay +
+// decay_bias); SISO plane 1 = u = sigmoid(write) * tanh(value); MIMO planes 1, 2 = sigmoid(write),
+// tanh(value) (the ranks are formed on the fly).  With aligned rows every thread issues all of
+// its 16-byte loads (PFI groups at a time) before converting any, and stores 16-byte vectors.
+// (sigmoid with __expf: relative error ~1e-7.)
 template <bool MIMO>
 __device__ __forceinline__ void stage_inputs(const ScanParams &p, int64_t row0, int t0, int nt, int c0, int S,
                                              float *s0, float *s1, float *s2, int vec) {
   const int esz = p.pc.dtype == TESM_BF16 ? 2 : 4;
   const uint8_t *base = reinterpret_cast<const uint8_t *>(p.pc.proj);
-  const int VPT = vec ? 16 / esz : 1;
-  const int groups = S / VPT;
-  for (int i = threadIdx.x; i < nt * groups; i += blockDim.x) {
-    const int t = i / groups, cg = (i - t * groups) * VPT;
-    const int c = c0 + cg;
-    if (c >= p.C) continue;
-    const uint8_t *rowp = base + ((row0 + t0 + t) * p.pc.ld) * esz;
-    float dv[8], wv[8], vv[8];
-    if (vec) {
-      const uint4 d4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_decay + c) * esz);
-      const uint4 w4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_write + c) * esz);
-      const uint4 v4 = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_value + c) * esz);
-      if (esz == 2) {
-        const __nv_bfloat16 *dh = reinterpret_cast<const __nv_bfloat16 *>(&d4);
-        const __nv_bfloat16 *wh = reinterpret_cast<const __nv_bfloat16 *>(&w4);
-        const __nv_bfloat16 *vh = reinterpret_cast<const __nv_bfloat16 *>(&v4);
+  if (vec) {
+    const int VPT = 16 / esz;
+    const int groups = S / VPT, items = nt * groups;
+    constexpr int PFI = 2;
+    for (int i0 = threadIdx.x; i0 < items; i0 += PFI * blockDim.x) {
+      uint4 d4[PFI], w4[PFI], v4[PFI];
+      int tt[PFI], cg[PFI];
+      bool ok[PFI];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          dv[j] = __bfloat162float(dh[j]);
-          wv[j] = __bfloat162float(wh[j]);
-          vv[j] = __bfloat162float(vh[j]);
-        }
-      } else {
-        const float *df = reinterpret_cast<const float *>(&d4);
-        const float *wf = reinterpret_cast<const float *>(&w4);
-        const float *vf = reinterpret_cast<const float *>(&v4);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          dv[j] = df[j];
-          wv[j] = wf[j];
-          vv[j] = vf[j];
+      for (int k = 0; k < PFI; ++k) {
+        const int i = i0 + k * blockDim.x;
+        tt[k] = i / groups;
+        cg[k] = (i - tt[k] * groups) * VPT;
+        ok[k] = i < items && c0 + cg[k] < p.C;
+        if (ok[k]) {
+          const uint8_t *rowp = base + ((row0 + t0 + tt[k]) * p.pc.ld) * esz;
+          const int c = c0 + cg[k];
+          d4[k] = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_decay + c) * esz);
+          w4[k] = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_write + c) * esz);
+          v4[k] = *reinterpret_cast<const uint4 *>(rowp + (int64_t)(p.pc.c_value + c) * esz);
         }
       }
-    } else {
+#pragma unroll
+      for (int k = 0; k < PFI; ++k) {
+        if (!ok[k]) continue;
+        float dv[8], wv[8], vv[8];
+        if (esz == 2) {
+          const __nv_bfloat16 *dh = reinterpret_cast<const __nv_bfloat16 *>(&d4[k]);
+          const __nv_bfloat16 *wh = reinterpret_cast<const __nv_bfloat16 *>(&w4[k]);
+          const __nv_bfloat16 *vh = reinterpret_cast<const __nv_bfloat16 *>(&v4[k]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            dv[j] = __bfloat162float(dh[j]);
+            wv[j] = __bfloat162float(wh[j]);
+            vv[j] = __bfloat162float(vh[j]);
+          }
+        } else {
+          const float *df = reinterpret_cast<const float *>(&d4[k]);
+          const float *wf = reinterpret_cast<const float *>(&w4[k]);
+          const float *vf = reinterpret_cast<const float *>(&v4[k]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dv[j] = df[j];
+            wv[j] = wf[j];
+            vv[j] = vf[j];
+          }
+        }
+        if (esz == 2)
+          stage_store<MIMO, 8>(p, tt[k] * S + cg[k], c0 + cg[k], dv, wv, vv, s0, s1, s2);
+        else
+          stage_store<MIMO, 4>(p, tt[k] * S + cg[k], c0 + cg[k], dv, wv, vv, s0, s1, s2);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < nt * S; i += blockDim.x) {
+      const int t = i / S, cg = i - t * S, c = c0 + cg;
+      if (c >= p.C) continue;
       const int64_t rb = (row0 + t0 + t) * p.pc.ld;
+      float dv[1], wv[1], vv[1];
       dv[0] = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_decay + c);
       wv[0] = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_write + c);
       vv[0] = load_f(p.pc.proj, p.pc.dtype, rb + p.pc.c_value + c);
-    }
-    for (int j = 0; j < VPT; ++j) {
-      const int o = t * S + cg + j;
-      s0[o] = fast_sigmoid(dv[j] + p.decay_bias[c + j]);
-      const float w = fast_sigmoid(wv[j]), v = tanhf(vv[j]);
-      if (MIMO) {
-        s1[o] = w;
-        s2[o] = v;
-      } else {
-        s1[o] = w * v;
-      }
+      stage_store<MIMO, 1>(p, t * S + cg, c, dv, wv, vv, s0, s1, s2);
     }
   }
 }
