@@ -5,7 +5,8 @@
 // average, the lerp toward it, and the ranks are merged with mimo_o:
 //   ent = sum_r mo[h,r,:] * (s_r + es (avg_r - s_r)),  chg = sum_r mo[h,r,:] * es (avg_r - s_r).
 // The reference's window truncation for t < W-1 (only lags o in [W-1-t, t] take part) is
-// reproduced when `quirk` is set (the default, for parity).
+// reproduced when `quirk` is set (the default, for parity).  The kernel is the persistent window
+// kernel of window.cuh in its MIMO mode (ranks in the tensor-core columns, merge in the epilogue).
 #include "window.cuh"
 
 #include <algorithm>

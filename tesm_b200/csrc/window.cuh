@@ -7,9 +7,11 @@
 // tiles and walks each tile's heads in turn (SISO: one head).  Per unit:
 //   fill     every byte the unit reads -- its q rows, the k rows and state rows of the window
 //            (positions t0-(W-1) ..), all mimo ranks -- is requested with 16-byte cp.async
-//            copies into one of two shared stages; the copies of unit n+1 are issued before
-//            unit n is computed, so HBM traffic overlaps the arithmetic.  Positions outside
-//            the sequence / tile are zero-filled by the copy itself.
+//            copies into shared memory.  Two 256-thread CTAs per SM with one stage each when
+//            that fits (one CTA's copies and barriers hide behind the other's arithmetic),
+//            else one 512-thread CTA with two stages whose next unit's copies are issued
+//            before the current unit is computed.  Positions outside the sequence / tile are
+//            zero-filled by the copy itself.
 //   table    (cos, sin) of every (position, frequency) of the tile, once per tile (shared by
 //            q, k and all heads), theta = fl(pos * inv_freq) as in tesm.py:783-793.
 //   rope     q rows (+ cross-layer bias, tesm.py:1213-1218) and k rows, fp32 in shared memory.
