@@ -157,9 +157,15 @@ int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const float *inv_sc
  * h0 (nullable, SISO only): prev_state (B, D) fp64.  workspace: caller-owned device
  * memory of at least tesm_b200_scan_workspace() bytes (look-back aggregates and flags). */
 int tesm_b200_scan_workspace(int64_t B, int64_t L, int64_t C, int64_t RM, int64_t *bytes);
+/* scan_chunk: the module's state_scan_chunk_size (reference default 16).  The reference scans
+ * in chunks with h_t = A_t (h_c + sum_s u_s / max(A_s, 1e-12)), A the in-chunk cumulative
+ * product of max(a, 1e-12) (tesm.py:1065-1089, :1133-1153); once A falls below 1e-12 inside a
+ * chunk this departs from the plain recurrence, and the kernel reproduces it.  0 runs the plain
+ * recurrence.  Supported chunk sizes divide 16 (or are >= L). */
 int tesm_b200_siso_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t D,
-                        int64_t R, const float *decay_bias, const double *h0, float *states, float *final_f32,
-                        double *final_f64, void *workspace, int64_t ws_bytes, tesm_stream_t stream);
+                        int64_t R, int64_t scan_chunk, const float *decay_bias, const double *h0, float *states,
+                        float *final_f32, double *final_f64, void *workspace, int64_t ws_bytes,
+                        tesm_stream_t stream);
 int tesm_b200_mimo_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t H,
                         int64_t D, int64_t R, int64_t RM, const float *decay_bias, const float *mimo_x,
                         float *states, float *final_f32, double *final_f64, void *workspace, int64_t ws_bytes,
@@ -284,13 +290,15 @@ int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, const float 
  * tesm_b200_siso_scan minus the workspace: the look-back scratch is a fixed 8 MiB array
  * inside the library, present on every GPU that loads it until the process exits.  Shapes
  * whose scratch (tesm_b200_scan_workspace) exceeds 8 MiB are rejected with TESM_EUNSUPPORTED.
- * The first call on a device looks up the array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture.  Every call shares the one array, so calls
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * keeps it for the life of the process (it is not looked up again, so a cudaDeviceReset
+ * between calls is not supported); make that first call before any stream capture.  Every call shares the one array, so calls
  * that overlap on the GPU (different streams, or several host threads) race; serialise them.
  * Nothing is allocated or freed. */
 int tesm_b200_siso_scan_noalloc(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
-                                int64_t D, int64_t R, const float *decay_bias, const double *h0, float *states,
-                                float *final_f32, double *final_f64, tesm_stream_t stream);
+                                int64_t D, int64_t R, int64_t scan_chunk, const float *decay_bias,
+                                const double *h0, float *states, float *final_f32, double *final_f64,
+                                tesm_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -171,10 +171,39 @@ def bitlinear(x, w, eps=1e-5, dtype="float32", per_row=False, return_acc=False):
     return (y, acc) if return_acc else y
 
 
+def bitlinear_codes(codes, inv, w, eps=1e-5, dtype="float32"):
+    """:func:`bitlinear` from given int8 activation codes and per-row 1/s (the dequantisation
+    of ``BitLinear.quantized_input``, tesm.py:206-209) instead of quantising an input: lets a
+    test hand the oracle the exact codes a device kernel quantised, so that rounding ties in
+    the quantiser's input cannot make the two sides diverge."""
+    t, _, deq = _ternary_cached(w, eps, dtype, False)
+    K = t.shape[1]
+    acc = int_gemm(np.asarray(codes)[..., :K], t)
+    y = acc.astype(F64) * np.asarray(inv, F64)[..., None] * F64(deq.reshape(-1)[0])
+    return cast(y.astype(F32), dtype)
+
+
+def bitlinear_f32out(x, w, eps=1e-5, dtype="float32"):
+    """:func:`bitlinear` with the input quantised and the weight ternarised in ``dtype`` but
+    the output kept in fp32 (a consumer that fuses the next operation, such as the output
+    combine, rounds once after it)."""
+    x = np.asarray(x, dtype=F32)
+    t, _, deq = _ternary_cached(w, eps, dtype, False)
+    c, s = quant_act(x, eps, dtype)
+    acc = int_gemm(c, t)
+    return (acc.astype(F64) * (1.0 / s.astype(F64))[..., None] * F64(deq.reshape(-1)[0])).astype(F32)
+
+
 # ---------------------------------------------------------------- layer pieces
 def _inv_freq(dim, base):
-    idx = np.arange(dim // 2, dtype=F32)
-    return (F32(1.0) / np.power(F32(base), (F32(2.0) * idx / F32(dim))).astype(F32)).astype(F32)
+    """``1.0 / (rope_base ** (2.0 * dim_idx / D))`` in fp32 (tesm.py:787-789): the power rounded
+    to fp32 once (evaluated in fp64, i.e. correctly rounded), then an fp32 reciprocal.  This is
+    what torch's CPU pow yields for every even D <= 64 (tests/test_oracle_golden.py checks it);
+    numpy's own fp32 power differs from it by 1-2 ulp at several indices, which RoPE multiplies
+    by the position."""
+    ex = (F32(2.0) * np.arange(dim // 2, dtype=F32) / F32(dim)).astype(F32)
+    pw = np.power(np.float64(F32(base)), ex.astype(np.float64)).astype(F32)
+    return (F32(1.0) / pw).astype(F32)
 
 
 def rope(x, pos_offset=0, base=10000.0):
@@ -344,12 +373,18 @@ def alloc_cache(cfg, batch, mimo=False):
             "ent_v_cache": np.zeros((batch, W, cfg["d_state"]), F32), "cache_idx": 0}
 
 
-def siso_forward(P, cfg, u, cross=None, prev_state=None, cache=None, details=False):
+def siso_forward(P, cfg, u, cross=None, prev_state=None, cache=None, details=False, in_codes=None, dtype="float32"):
     """``TESM_SISO.forward`` prefill in eval mode (tesm.py:1175-1272), float32 module.
 
     P: parameter dict with the reference's names; cfg: d_model, d_state, ent_rank,
     entanglement_window, entanglement_threshold, entanglement_scale, bit_eps, rope_base,
     state_scan_chunk_size.  Returns (y, final_state_f64, states) [+ details dict].
+
+    ``dtype="bfloat16"`` gives the layer bf16 activations the way a bf16 module would run
+    its BitLinears (tesm.py:206-215 in bf16: weight scale, products and codes rounded to
+    bf16; outputs rounded to bf16) while the scan and the entanglement stay in fp32 on the
+    bf16 projections; the output combine rounds once.  (The reference's own SISO layer
+    cannot run in bf16, tesm.py:944, so this mode exists to check bf16 device paths.)
     """
     Dm, D, R = cfg["d_model"], cfg["d_state"], cfg["ent_rank"]
     eps = cfg.get("bit_eps", 1e-5)
@@ -357,7 +392,10 @@ def siso_forward(P, cfg, u, cross=None, prev_state=None, cache=None, details=Fal
     W = cfg["entanglement_window"]
     u = np.asarray(u, F32)
     B, L, _ = u.shape
-    proj = bitlinear(u, P["in_proj.weight"], eps)
+    if in_codes is None:
+        proj = bitlinear(u, P["in_proj.weight"], eps, dtype)
+    else:  # test hook: in_proj from given (codes, 1/s), see bitlinear_codes
+        proj = bitlinear_codes(in_codes[0], in_codes[1], P["in_proj.weight"], eps, dtype).reshape(B, L, -1)
     local, value, decay, write, gate, q, k = _split(proj, [Dm, D, D, D, Dm, R, R])
     value = np.tanh(value).astype(F32)
     decay = sigmoid(decay + P["decay_bias"])
@@ -389,13 +427,18 @@ def siso_forward(P, cfg, u, cross=None, prev_state=None, cache=None, details=Fal
             cache["ent_k_cache"][:, -L:] = k
             cache["ent_v_cache"][:, -L:] = states
         cache["cache_idx"] = 0
-    sp = bitlinear(np.tanh(ent).astype(F32), P["state_proj.weight"], eps)
-    ep = bitlinear(chg, P["ent_proj.weight"], eps)
-    y = (local + gate * sp + ep).astype(F32)
-    out = bitlinear(y, P["out_proj.weight"], eps)
+    if dtype == "float32":
+        sp = bitlinear(np.tanh(ent).astype(F32), P["state_proj.weight"], eps)
+        ep = bitlinear(chg, P["ent_proj.weight"], eps)
+        y = (local + gate * sp + ep).astype(F32)
+    else:
+        sp = bitlinear_f32out(np.tanh(ent).astype(F32), P["state_proj.weight"], eps, dtype)
+        ep = bitlinear_f32out(chg, P["ent_proj.weight"], eps, dtype)
+        y = cast((local + gate * sp + ep).astype(F32), dtype)
+    out = bitlinear(y, P["out_proj.weight"], eps, dtype)
     if details:
-        tie = np.minimum(np.minimum(quant_tie_margin(np.tanh(ent), eps), quant_tie_margin(chg, eps)),
-                         quant_tie_margin(y, eps))
+        tie = np.minimum(np.minimum(quant_tie_margin(np.tanh(ent), eps, dtype), quant_tie_margin(chg, eps, dtype)),
+                         quant_tie_margin(y, eps, dtype))
         return out, final, states, dict(proj=proj, q=q, k=k, states=states, avg=avg, ent=ent, chg=chg,
                                         y=y, scores=scores, decay=decay, update=update, tie_margin=tie)
     return out, final, states
@@ -439,13 +482,16 @@ def _decode_window(cache, k_vec, v_new, q_vec, bias, thr, R, mimo):
     return avg, np.stack(scs, -1)
 
 
-def siso_decode(P, cfg, u, cache, cross=None, details=False):
+def siso_decode(P, cfg, u, cache, cross=None, details=False, in_codes=None, dtype="float32"):
     """``TESM_SISO._forward_incremental`` (tesm.py:1274-1400), one token, float32 module."""
     Dm, D, R = cfg["d_model"], cfg["d_state"], cfg["ent_rank"]
     eps = cfg.get("bit_eps", 1e-5)
     thr, es = cfg["entanglement_threshold"], cfg["entanglement_scale"]
     u = np.asarray(u, F32)
-    proj = bitlinear(u, P["in_proj.weight"], eps)
+    if in_codes is None:
+        proj = bitlinear(u, P["in_proj.weight"], eps, dtype)
+    else:
+        proj = bitlinear_codes(in_codes[0], in_codes[1], P["in_proj.weight"], eps, dtype).reshape(u.shape[0], 1, -1)
     local, value, decay, write, gate, q, k = _split(proj, [Dm, D, D, D, Dm, R, R])
     value = np.tanh(value).astype(F32)
     decay = sigmoid(decay + P["decay_bias"])
@@ -464,12 +510,17 @@ def siso_decode(P, cfg, u, cache, cross=None, details=False):
     chg = (ent - new).astype(F32)
     cache["state"] = new64
     cache["seq_pos"] += 1
-    sp = bitlinear(np.tanh(ent), P["state_proj.weight"], eps)
-    ep = bitlinear(chg, P["ent_proj.weight"], eps)
-    y = (local[:, 0] + gate[:, 0] * sp + ep).astype(F32)
-    out = bitlinear(y[:, None], P["out_proj.weight"], eps)
+    if dtype == "float32":
+        sp = bitlinear(np.tanh(ent), P["state_proj.weight"], eps)
+        ep = bitlinear(chg, P["ent_proj.weight"], eps)
+        y = (local[:, 0] + gate[:, 0] * sp + ep).astype(F32)
+    else:
+        sp = bitlinear_f32out(np.tanh(ent), P["state_proj.weight"], eps, dtype)
+        ep = bitlinear_f32out(chg, P["ent_proj.weight"], eps, dtype)
+        y = cast((local[:, 0] + gate[:, 0] * sp + ep).astype(F32), dtype)
+    out = bitlinear(y[:, None], P["out_proj.weight"], eps, dtype)
     if details:
-        return out, new64, new, dict(scores=scs, avg=avg)
+        return out, new64, new, dict(scores=scs, avg=avg, ent=ent, chg=chg)
     return out, new64, new
 
 
@@ -534,7 +585,9 @@ def mimo_forward(P, cfg, u, cache=None, details=False):
     y = (local + gate * sp + ep).astype(F32)
     out = bitlinear(y, P["out_proj.weight"], eps)
     if details:
-        return out, final, states0[:, -1], dict(ent=ent, chg=chg, states0=states0, q=q, k=k)
+        tie = np.minimum(np.minimum(quant_tie_margin(np.tanh(ent.reshape(B, L, H * D)), eps),
+                                    quant_tie_margin(chg.reshape(B, L, H * D), eps)), quant_tie_margin(y, eps))
+        return out, final, states0[:, -1], dict(ent=ent, chg=chg, states0=states0, q=q, k=k, y=y, tie_margin=tie)
     return out, final, states0[:, -1]
 
 
@@ -584,16 +637,24 @@ def rmsnorm(x, w, eps=1e-5):
     return (x * (1.0 / np.sqrt(var + eps)).astype(F32) * w).astype(F32)
 
 
-def ffn(P, x, eps=1e-5):
-    """``FeedForward.forward`` grouped gate/up path (mixer_seq_simple.py:45-67)."""
-    tg, _, dg = _ternary_cached(P["gate_proj.weight"], eps, "float32", False)
-    tu, _, du = _ternary_cached(P["up_proj.weight"], eps, "float32", False)
-    c, s = quant_act(x, eps)
-    inv_s = (1.0 / s.astype(F64))[..., None]
+def ffn(P, x, eps=1e-5, dtype="float32", in_codes=None, return_h=False):
+    """``FeedForward.forward`` grouped gate/up path (mixer_seq_simple.py:45-67).  With
+    ``dtype="bfloat16"`` the BitLinears take bf16 semantics and silu(g) * u is rounded to bf16
+    once (a fused SwiGLU epilogue).  ``in_codes`` = (codes, 1/s) replaces the quantisation of
+    x (a test hook, see :func:`bitlinear_codes`)."""
+    tg, _, dg = _ternary_cached(P["gate_proj.weight"], eps, dtype, False)
+    tu, _, du = _ternary_cached(P["up_proj.weight"], eps, dtype, False)
+    if in_codes is None:
+        c, s = quant_act(x, eps, dtype)
+        inv_s = (1.0 / s.astype(F64))[..., None]
+    else:
+        c = np.asarray(in_codes[0])[..., :tg.shape[1]]
+        inv_s = np.asarray(in_codes[1], F64)[..., None]
     gx = (int_gemm(c, tg).astype(F64) * inv_s * dg).astype(F32)
     ux = (int_gemm(c, tu).astype(F64) * inv_s * du).astype(F32)
-    h = (gx / (F32(1) + np.exp(-gx)) * ux).astype(F32)
-    return bitlinear(h, P["down_proj.weight"], eps)
+    h = cast((gx / (F32(1) + np.exp(-gx)) * ux).astype(F32), dtype)
+    out = bitlinear(h, P["down_proj.weight"], eps, dtype)
+    return (out, h) if return_h else out
 
 
 def model_alloc_cache(cfg, batch):

@@ -35,8 +35,8 @@ SIGNATURES = {
     "tesm_b200_gemm_i8": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
                           c_vp, c_i64, c_vp, c_i64, c_vp],
     "tesm_b200_scan_workspace": [c_i64, c_i64, c_i64, c_i64, c_vp],
-    "tesm_b200_siso_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,
-                            c_vp, c_i64, c_vp],
+    "tesm_b200_siso_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,
+                            c_vp, c_vp, c_i64, c_vp],
     "tesm_b200_mimo_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
                             c_vp, c_vp, c_vp, c_i64, c_vp],
     "tesm_b200_siso_local_ent": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
@@ -74,8 +74,8 @@ SIGNATURES = {
                                   c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_vp],
     "tesm_b200_gemm_i8_swiglu": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
                                  c_vp, c_i64, c_vp],
-    "tesm_b200_siso_scan_noalloc": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,
-                                    c_vp, c_vp],
+    "tesm_b200_siso_scan_noalloc": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                    c_vp, c_vp, c_vp, c_vp],
 }
 _RESTYPES = {"tesm_b200_last_error": ctypes.c_char_p}
 

@@ -35,10 +35,15 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-
 
 __device__ __forceinline__ float ternary_of(float s, float thr) { return s > thr ? 1.f : (s < -thr ? -1.f : 0.f); }
 
-// theta = pos * (1 / base^(2i/R)) in fp32 (tesm.py:783-793; tesm_mimo.py:210-220).
+// theta = pos * (1 / base^(2i/R)) in fp32 (tesm.py:783-793; tesm_mimo.py:210-220).  The power
+// is evaluated in fp64 and rounded to fp32 once (the correctly rounded fp32 power), then the
+// fp32 reciprocal is taken: for every even R <= 64 this reproduces the reference's torch
+// values bit for bit, which matters because theta = pos * inv_freq magnifies a one-ulp
+// difference in inv_freq by the position (a few 1e-4 rad at pos ~ 8000).
 __device__ __forceinline__ float rope_inv_freq(int i, int R, float base) {
   const float ex = (2.f * (float)i) / (float)R;
-  return 1.f / powf(base, ex);
+  const float pw = (float)pow((double)base, (double)ex);
+  return 1.f / pw;
 }
 
 // One q/k row of R values starting at column `col` -> dst with RoPE at `pos`, plus an

@@ -3,6 +3,12 @@
 //   SISO (tesm.py:1198-1223, scan :1091-1164): a = sigmoid(decay + decay_bias),
 //        u = sigmoid(write) * tanh(value); the reference scans in fp64 chunks, here fp32 FMA in
 //        time order (relative error ~1e-6, within the 1e-3 fp32 bar).
+//        The reference's chunk formula h_t = A_t (h_c + sum_s u_s / max(A_s, 1e-12)), with A the
+//        in-chunk cumulative product of max(a, 1e-12) (tesm.py:1085-1088, 1133-1153), differs
+//        from the plain recurrence once A drops below 1e-12 inside a chunk (small decays, e.g.
+//        a = sigmoid(N(0,1))).  It equals the recurrence h_t = a_t h_{t-1} + u_t min(1, A_t/1e-12),
+//        which the SISO kernels run with A restarted at every multiple of the reference's
+//        state_scan_chunk_size (`cs`; 0 = the plain recurrence).
 //   MIMO (tesm_mimo.py:959-989, scan :375-392): ranks r share a; u_r = (write*x_r)*(value*x_r)
 //        with x_r = mimo_x[h, r, :]; the reference scans in fp32 with separate mul/add roundings,
 //        reproduced with __fmul_rn/__fadd_rn.
@@ -24,6 +30,7 @@ struct ScanParams {
   const float *mimo_x;      // (H, RM, D) or null (SISO)
   const double *h0;         // (B, C) or null
   int B, L, C, D, RM;
+  int cs;                   // reference scan chunk for the 1e-12 clamp (SISO), 0 = none
   int T, nchunks, nslices;
   float *states;            // (B, L, RM, C)
   float *final_f32;         // (B, C) rank 0
@@ -178,6 +185,9 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
     for (int r = 0; r < RM; ++r) mx[r] = p.mimo_x[((int64_t)h * RM + r) * p.D + d];
   }
   __syncthreads();
+  // SISO: running product of max(a, 1e-12) since the last reference chunk start (T % cs == 0,
+  // so every kernel chunk starts one); the caller resets `cp` to 1 before each pass
+  float cp = 1.f;
   auto inputs = [&](int t, float &a, float (&u)[RM]) {
     const int i = t * S + threadIdx.x;
     a = s0[i];
@@ -187,6 +197,11 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
       for (int r = 0; r < RM; ++r) u[r] = __fmul_rn(__fmul_rn(w, mx[r]), __fmul_rn(v, mx[r]));
     } else {
       u[0] = s1[i];
+      if (p.cs > 0) {
+        if (t % p.cs == 0) cp = 1.f;
+        cp *= fmaxf(a, 1e-12f);
+        u[0] *= fminf(1.f, cp * 1e12f);
+      }
     }
   };
 
@@ -195,6 +210,7 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
 #pragma unroll
   for (int r = 0; r < RM; ++r) U[r] = 0.f;
   if (active) {
+    cp = 1.f;
     for (int t = 0; t < nt; ++t) {
       float a, u[RM];
       inputs(t, a, u);
@@ -286,6 +302,7 @@ __global__ void __launch_bounds__(256, 4) k_scan(ScanParams p, int vec) {
   }
   // pass 2: states of this chunk from the carry
   if (active) {
+    cp = 1.f;
     for (int t = 0; t < nt; ++t) {
       float a, u[RM];
       inputs(t, a, u);
@@ -395,12 +412,21 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
   }
   float a0[TT], a1[TT], u0[TT], u1[TT];
   float A0 = 1.f, A1 = 1.f, U0 = 0.f, U1 = 0.f;
+  float P0 = 1.f, P1 = 1.f;  // running products since the last reference chunk start (TT % cs == 0)
+  const int cs = p.cs;
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     a0[t] = decay_gate(bf16lo(rd[t]), nb0);
     a1[t] = decay_gate(bf16hi(rd[t]), nb1);
     u0[t] = write_value(bf16lo(rw[t]), bf16lo(rv[t]));
     u1[t] = write_value(bf16hi(rw[t]), bf16hi(rv[t]));
+    if (cs > 0) {
+      if (t % cs == 0) P0 = P1 = 1.f;
+      P0 *= fmaxf(a0[t], 1e-12f);
+      P1 *= fmaxf(a1[t], 1e-12f);
+      u0[t] *= fminf(1.f, P0 * 1e12f);
+      u1[t] *= fminf(1.f, P1 * 1e12f);
+    }
     U0 = fmaf(a0[t], U0, u0[t]);
     U1 = fmaf(a1[t], U1, u1[t]);
     A0 *= a0[t];
@@ -545,7 +571,7 @@ static int launch_scan(ScanParams &p, cudaStream_t st, int slice) {
 static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm, int64_t H,
                     int64_t D, int64_t R, int64_t RM, const float *decay_bias, const float *mimo_x,
                     const double *h0, float *states, float *final_f32, double *final_f64, void *workspace,
-                    int64_t ws_bytes, cudaStream_t st) {
+                    int64_t ws_bytes, cudaStream_t st, int64_t scan_chunk = 0) {
   TESM_REQUIRE(proj && decay_bias && states && final_f32 && final_f64 && workspace, "scan: null pointer");
   TESM_REQUIRE(B > 0 && L > 0 && D > 0 && H > 0 && ldp >= 2 * Dm + 3 * H * D + 2 * H * R, "scan: bad shape");
   if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "scan: dtype");
@@ -562,6 +588,9 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
   p.C = (int)C;
   p.D = (int)D;
   p.RM = (int)RM;
+  TESM_REQUIRE(scan_chunk >= 0, "scan: bad state_scan_chunk_size");
+  // the reference's chunk is min(state_scan_chunk_size, L) (tesm.py:1094)
+  p.cs = mimo_x ? 0 : (int)(scan_chunk < L ? scan_chunk : L);
   p.T = s.T;
   p.nchunks = s.nchunks;
   p.nslices = s.nslices;
@@ -587,7 +616,7 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
     const bool pairs = dtype == TESM_BF16 && (uintptr_t)proj % 4 == 0 && ldp % 2 == 0 && C % 2 == 0 &&
                        p.pc.c_decay % 2 == 0 && p.pc.c_write % 2 == 0 && p.pc.c_value % 2 == 0 &&
                        (uintptr_t)states % 8 == 0;
-    if (reg_mode && pairs) {
+    if (reg_mode && pairs && (p.cs == 0 || reg_tt % p.cs == 0 || L <= reg_tt)) {
       const int G = s.T / reg_tt;
       e = cudaMemsetAsync(workspace, 0xff, s.off_flags, st);  // carry words to "not yet written"
       if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("scan memset: ") + cudaGetErrorString(e));
@@ -606,6 +635,10 @@ static int run_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t
       TESM_SCAN_REG_CASE(32, 2)
 #undef TESM_SCAN_REG_CASE
     }
+    // every restart of the clamp product must fall inside one thread's chunk of T positions
+    if (p.cs > 0 && p.T % p.cs != 0 && L > p.T)
+      return fail(TESM_EUNSUPPORTED, "scan: state_scan_chunk_size " + std::to_string(scan_chunk) +
+                                         " must divide " + std::to_string(p.T) + " (the kernel's chunk)");
     return launch_scan<1, false>(p, st, s.slice);
   }
   switch (RM) {
@@ -629,11 +662,11 @@ extern "C" int tesm_b200_scan_workspace(int64_t B, int64_t L, int64_t C, int64_t
 }
 
 extern "C" int tesm_b200_siso_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,
-                                   int64_t D, int64_t R, const float *decay_bias, const double *h0, float *states,
-                                   float *final_f32, double *final_f64, void *workspace, int64_t ws_bytes,
-                                   tesm_stream_t stream) {
+                                   int64_t D, int64_t R, int64_t scan_chunk, const float *decay_bias,
+                                   const double *h0, float *states, float *final_f32, double *final_f64,
+                                   void *workspace, int64_t ws_bytes, tesm_stream_t stream) {
   return run_scan(proj, dtype, ldp, B, L, Dm, 1, D, R, 1, decay_bias, nullptr, h0, states, final_f32, final_f64,
-                  workspace, ws_bytes, (cudaStream_t)stream);
+                  workspace, ws_bytes, (cudaStream_t)stream, scan_chunk);
 }
 
 extern "C" int tesm_b200_mimo_scan(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t L, int64_t Dm,

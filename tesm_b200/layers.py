@@ -236,7 +236,8 @@ def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, ac
     fin32 = torch.empty(B, D, device=dev, dtype=torch.float32)
     fin64 = torch.empty(B, D, device=dev, dtype=torch.float64)
     h0 = prev_state.to(device=dev, dtype=torch.float64).contiguous() if prev_state is not None else None
-    ops.siso_scan(proj, B, L, Dm, D, R, _param_cache(mod, "decay_bias"), h0, states, fin32, fin64)
+    ops.siso_scan(proj, B, L, Dm, D, R, _param_cache(mod, "decay_bias"), h0, states, fin32, fin64,
+                  mod.state_scan_chunk_size)
     thr, es, base = mod.entanglement_threshold, mod.entanglement_scale, mod.rope_base
     fused = W > 0 and M > ops.GEMV_MAX_M and W in (4, 8, 16, 32)
     if fused:

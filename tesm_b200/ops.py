@@ -296,10 +296,12 @@ def scan_workspace(B: int, L: int, C: int, RM: int, device) -> torch.Tensor:
     return torch.empty(n.value, device=device, dtype=torch.uint8)
 
 
-def siso_scan(proj, B, L, Dm, D, R, decay_bias, h0, states, f32, f64):
+def siso_scan(proj, B, L, Dm, D, R, decay_bias, h0, states, f32, f64, scan_chunk=16):
+    """SISO scan; ``scan_chunk`` is the module's state_scan_chunk_size (the reference's chunked
+    fp64 formula clamps the in-chunk decay product at 1e-12, which the kernel reproduces)."""
     ws = scan_workspace(B, L, D, 1, proj.device)
     _lib.call("tesm_b200_siso_scan", proj.data_ptr(), dtype_code(proj.dtype), proj.stride(0), B, L, Dm, D, R,
-              decay_bias.data_ptr(), _ptr(h0), states.data_ptr(), f32.data_ptr(), f64.data_ptr(), ws.data_ptr(),
+              int(scan_chunk), decay_bias.data_ptr(), _ptr(h0), states.data_ptr(), f32.data_ptr(), f64.data_ptr(), ws.data_ptr(),
               ws.numel(), _stream())
 
 

@@ -168,8 +168,43 @@ def gen_int2_export():
     save("int2_export_tiny", **out)
 
 
+def gen_scan_rope():
+    """Two pieces of the SISO prefill in isolation, at inputs where their fp details show:
+
+    * ``_parallel_state_scan`` (tesm.py:1091-1164) with small decays a = sigmoid(N(0, 1.5) - 1)
+      (the in-chunk cumulative product often drops below the 1e-12 clamp) and with the
+      module's usual decays (a = sigmoid(N(0,1) + 3));
+    * ``_apply_rope`` (tesm.py:783-793) at positions 8000.. for widths 64 and 48, where a
+      one-ulp difference in 1/base^(2i/D) moves theta by ~1e-3 rad.
+    """
+    torch.manual_seed(0)
+    m = TESM_SISO(d_model=64, d_state=32, ent_rank=16, entanglement_window=8, max_seq_len=64,
+                  kernel_backend="torch").eval()
+    out = {}
+    B, L, D = 2, 100, 32
+    with torch.no_grad():
+        for name, shift, sd in (("small", -1.0, 1.5), ("usual", 3.0, 1.0)):
+            a = torch.sigmoid(randn((B, L, D), 30) * sd + shift)
+            u = randn((B, L, D), 31) * 0.5
+            st = m._parallel_state_scan(a, u)
+            out[f"scan_{name}_a"] = t2n(a)
+            out[f"scan_{name}_u"] = t2n(u)
+            out[f"scan_{name}_states"] = t2n(st)
+            out[f"scan_{name}_final"] = t2n(m._last_scan_state_f64)
+        for R in (64, 48):
+            x = randn((1, 24, R), 32 + R)
+            out[f"rope{R}_x"] = t2n(x)
+            out[f"rope{R}_y"] = t2n(m._apply_rope(x, pos_offset=8000))
+    save("scan_rope", **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(8)
+    if len(sys.argv) > 1:  # regenerate selected groups only, e.g. "scan_rope"
+        for name in sys.argv[1:]:
+            globals()["gen_" + name]()
+        sys.exit(0)
+    gen_scan_rope()
     gen_bitlinear()
     for c in cases.SISO:
         run_siso(c)

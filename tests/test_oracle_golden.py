@@ -101,3 +101,62 @@ def test_model_golden(c):
     for s in range(c["decode"]):
         lg = O.model_forward(P, cfg, g[f"dec{s}_ids"], cache)
         assert max_rel(lg, g[f"dec{s}_logits"]) <= 1e-3, f"decode step {s}"
+
+
+# ------------------------------------------------------------------ scan clamp and RoPE frequencies
+def _scan_clamped_recurrence(a, u, cs=16):
+    """The recurrence the SISO scan kernels run (fp64 here): h_t = a_t h_{t-1} + u_t min(1, P_t/1e-12),
+    P_t the product of max(a, 1e-12) since the last multiple of cs.  It restates the reference's
+    chunk formula h_t = A_t (h_c + sum u_s / max(A_s, 1e-12)) (tesm.py:1085-1088)."""
+    a = np.maximum(np.asarray(a, np.float64), 1e-12)
+    u = np.asarray(u, np.float64)
+    B, L, D = a.shape
+    cs = min(cs, L)
+    h = np.zeros((B, D))
+    P = np.ones((B, D))
+    out = np.empty_like(u)
+    for t in range(L):
+        if t % cs == 0:
+            P = np.ones((B, D))
+        P = P * a[:, t]
+        h = a[:, t] * h + u[:, t] * np.minimum(1.0, P / 1e-12)
+        out[:, t] = h
+    return out
+
+
+@pytest.mark.parametrize("which", ["small", "usual"])
+def test_scan_chunk_clamp_golden(which):
+    """The oracle's chunked scan and the kernels' clamped recurrence both match the reference's
+    _parallel_state_scan, including decays small enough to hit its 1e-12 clamp."""
+    g = golden("scan_rope")
+    a, u = g[f"scan_{which}_a"], g[f"scan_{which}_u"]
+    ref, fin = O.scan_chunked_f64(a, u)
+    assert max_rel(ref, g[f"scan_{which}_states"]) <= 1e-6
+    assert max_rel(fin, g[f"scan_{which}_final"]) <= 1e-6
+    assert max_rel(_scan_clamped_recurrence(a, u), g[f"scan_{which}_states"]) <= 1e-6
+    if which == "small":  # the clamp changes the result: the plain recurrence does not match
+        plain = _scan_clamped_recurrence(a, u, cs=10 ** 9)
+        a64 = np.maximum(a.astype(np.float64), 1e-12)
+        h = np.zeros(a.shape[::2])
+        for t in range(a.shape[1]):
+            h = a64[:, t] * h + u[:, t]
+            plain[:, t] = h
+        assert max_rel(plain, g[f"scan_{which}_states"]) > 1e-2
+
+
+def test_rope_inv_freq_matches_reference_expression():
+    """1 / base^(2i/D) as the reference's fp32 torch expression gives it (tesm.py:787-789),
+    bit for bit, for every even width up to 64; the kernels compute it the same way (the
+    power in fp64 rounded once to fp32, then an fp32 reciprocal)."""
+    from oracle import tesm_oracle
+    for D in range(2, 65, 2):
+        idx = torch.arange(D // 2, dtype=torch.float32)
+        ref = (1.0 / (10000.0 ** (2.0 * idx / D))).numpy()
+        assert np.array_equal(tesm_oracle._inv_freq(D, 10000.0), ref), D
+
+
+@pytest.mark.parametrize("R", [64, 48])
+def test_rope_far_positions_golden(R):
+    g = golden("scan_rope")
+    y = O.rope(g[f"rope{R}_x"], pos_offset=8000)
+    assert max_rel(y, g[f"rope{R}_y"]) <= 2e-6

@@ -4,7 +4,9 @@ tesm_b200_siso_scan_noalloc serves callers that cannot allocate device memory: i
 the look-back scratch in a fixed array inside the library instead of a caller workspace.
 Both entry points are called through the C ABI on the same inputs, twice in a row with
 different inputs (the shared array keeps the previous call's contents, which must not
-leak), and must agree within the scan tolerance (max-rel 1e-5).  This file is collected
+leak), with fp32 projections (shared-memory kernel) and bf16 ones (register-resident
+kernel, whose carry words start from an all-ones "not yet written" pattern inside the
+array), and must agree within the scan tolerance (max-rel 1e-5).  This file is collected
 last so a failing run that stops at the first failure has run every other test.
 """
 import ctypes
@@ -18,11 +20,11 @@ from helpers import max_rel, randn
 pytestmark = pytest.mark.gpu
 
 
-def _scan_both(lib, seed, B, L, D, h0):
-    from tesm_b200 import _lib
+def _scan_both(lib, seed, B, L, D, h0, dtype):
+    from tesm_b200 import _lib, ops
     Dm, R = 32, 16
-    N = 2 * Dm + 3 * D + 2 * R
-    proj = (randn((B * L, N), seed)).cuda()
+    N = 2 * Dm + 3 * D + 2 * R  # even, so bf16 rows keep 4-byte aligned channel pairs
+    proj = (randn((B * L, N), seed)).to(dtype).cuda()
     db = (torch.full((D,), 3.0) + randn((D,), seed + 1) * 0.5).cuda()
     prev = randn((B, D), seed + 2).double().cuda() if h0 else None
     st = torch.cuda.current_stream().cuda_stream
@@ -31,7 +33,7 @@ def _scan_both(lib, seed, B, L, D, h0):
         states = torch.full((B * L, D), float("nan"), device="cuda")
         f32 = torch.empty(B, D, device="cuda")
         f64 = torch.empty(B, D, device="cuda", dtype=torch.float64)
-        args = [proj.data_ptr(), 0, proj.stride(0), B, L, Dm, D, R, db.data_ptr(),
+        args = [proj.data_ptr(), ops.dtype_code(dtype), proj.stride(0), B, L, Dm, D, R, 16, db.data_ptr(),
                 prev.data_ptr() if prev is not None else None, states.data_ptr(), f32.data_ptr(), f64.data_ptr()]
         if variant == "workspace":
             n = ctypes.c_int64(0)
@@ -46,10 +48,11 @@ def _scan_both(lib, seed, B, L, D, h0):
     return outs
 
 
-def test_noalloc_matches_workspace_scan_twice(lib):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_noalloc_matches_workspace_scan_twice(lib, dtype):
     # two calls in a row with different shapes and inputs
     for seed, (B, L, D, h0) in [(100, (2, 1000, 256, True)), (200, (3, 300, 96, False))]:
-        (s_ws, f_ws), (s_na, f_na) = _scan_both(lib, seed, B, L, D, h0)
+        (s_ws, f_ws), (s_na, f_na) = _scan_both(lib, seed, B, L, D, h0, dtype)
         assert np.isfinite(s_na).all()
         assert max_rel(s_na, s_ws) <= 1e-5
         assert max_rel(f_na, f_ws) <= 1e-5
@@ -57,8 +60,9 @@ def test_noalloc_matches_workspace_scan_twice(lib):
 
 def test_noalloc_rejects_oversized_shapes(lib):
     from tesm_b200 import _lib
-    # 64 x 8192 positions x d_state 256 needs ~100 MiB of scratch, above the fixed 8 MiB
-    rc = lib.tesm_b200_siso_scan_noalloc(ctypes.c_void_p(256), 0, 2000, 64, 8192, 16, 256, 16, ctypes.c_void_p(256),
-                                         None, ctypes.c_void_p(256), ctypes.c_void_p(256), ctypes.c_void_p(256),
+    # 64 x 8192 positions x d_state 256 needs ~100 MiB of scratch, above the fixed 8 MiB.  No
+    # device pointers are passed: the size check answers first, and if it ever stopped doing
+    # so the scan's own null-pointer check would refuse the call before any launch.
+    rc = lib.tesm_b200_siso_scan_noalloc(None, 0, 2000, 64, 8192, 16, 256, 16, 16, None, None, None, None, None,
                                          None)
     assert rc == 5 and "above the fixed" in _lib.last_error()
