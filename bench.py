@@ -564,6 +564,20 @@ def run_skinny_case(args):
         print(json.dumps({"kernel": "skinny gemm_i8", "shape": name, "M": M, "N": N, "K": K, "us": t * 1e6,
                           "TOPS": 2.0 * M * N * K / t / 1e12, "weight_GB_s": wbytes / t / 1e9,
                           "hbm_frac": wbytes / t / 1e9 / peaks["hbm_gbs"]}), flush=True)
+        del pws
+    # the SwiGLU gate/up GEMM (2 x 11008 interleaved rows, per-row dequantisation)
+    N, K = 2 * CFG["d_intermediate"], CFG["d_model"]
+    ncopy = max(2, int(3 * 126e6 // (N * K)) + 1)
+    w = torch.randn(N, K, device="cuda") * 0.02
+    pws = [ops.pack_weight(w.roll(i, 0), 1e-5, per_row=True, with_tern=True) for i in range(ncopy)]
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    q = ops.quantize(x, 1e-5)
+    h = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+    t = _graph_time(lambda i: ops.gemm_swiglu(q, pws[i % ncopy], torch.bfloat16, h), inner=ncopy)
+    wbytes = N * K
+    print(json.dumps({"kernel": "skinny gemm_i8 swiglu", "shape": "gate_up", "M": M, "N": N, "K": K, "us": t * 1e6,
+                      "TOPS": 2.0 * M * N * K / t / 1e12, "weight_GB_s": wbytes / t / 1e9,
+                      "hbm_frac": wbytes / t / 1e9 / peaks["hbm_gbs"]}), flush=True)
     return 0
 
 

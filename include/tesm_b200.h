@@ -94,10 +94,15 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
  * TMEM accumulators, TMA-staged operands); same contract as tesm_b200_gemv_int2 but the
  * activation codes are row-major (TESM_LAYOUT_ROWMAJOR, ld_codes multiple of 16) and the
  * weights are the int8 ternary matrix from tesm_b200_pack_ternary (ld_tern multiple of 16).
- * splitk_ws (nullable, caller-owned scratch of ws_bytes): when there are fewer output tiles than
- * SMs (decode batches), K is split across up to 8 CTAs per tile; each split stores its int32
- * partial tile into its own M*N slice of the workspace and a finalize kernel sums the slices in a
- * fixed order (exact integers, deterministic).  The split count is capped so S*M*N*4 <= ws_bytes. */
+ * splitk_ws (nullable, caller-owned scratch of ws_bytes, 16-byte aligned): when the output tiles
+ * do not fill the SMs (decode batches), K is split across up to 8 CTAs (or CTA pairs) per tile.
+ * The first 16 KB of the scratch are 4096 int32 tile counters that must be zero before the first
+ * call (e.g. cudaMemset once at allocation); every call leaves them zero again.  The rest holds
+ * up to 8 int32 M*N slices: each split stores its partial tile into its slice and counts itself;
+ * the split that arrives last adds the others' partials to its own accumulators (exact integers:
+ * the result does not depend on the arrival order) and writes the output.  The split count is
+ * capped so 16 KB + S*M*N*4 <= ws_bytes.  Calls that share one scratch must not overlap on the
+ * GPU. */
 /* tesm_b200_decode_step for one SISO layer (H = 1) with the per-token int8 codes of tanh(ent) and
  * ent - s as outputs instead of the values (tesm.py:1385-1396 then BitLinear.quantized_input
  * tesm.py:206-209 of state_proj / ent_proj): codes (B x ldc, ldc >= 2*Dp, Dp = D rounded up to

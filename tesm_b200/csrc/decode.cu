@@ -42,6 +42,8 @@ struct DecodeParams {
 
 __global__ void k_decode_step(DecodeParams p) {
   extern __shared__ float sm[];
+  pdl_trigger();
+  pdl_wait();
   const int R = p.R, W = p.W, D = p.D, H = p.H;
   float *q = sm;             // R
   float *k = q + R;          // R
@@ -187,8 +189,7 @@ extern "C" int tesm_b200_decode_step(const void *proj, int dtype, int64_t ldp, i
   const int threads = (int)round_up(D < 32 ? 32 : D, 32);
   const size_t smem = sizeof(float) * (2 * R + W) + sizeof(int) * W;
   dim3 grid((unsigned)H, (unsigned)B);
-  k_decode_step<<<grid, threads, smem, (cudaStream_t)stream>>>(p);
-  return check_launch("decode_step");
+  return launch_k("decode_step", k_decode_step, grid, dim3(threads), smem, (cudaStream_t)stream, p);
 }
 
 extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t Dm,
@@ -236,6 +237,6 @@ extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int
   p.inv2 = inv2;
   const int threads = (int)round_up(D < 32 ? 32 : D, 32);
   const size_t smem = sizeof(float) * (2 * R + W) + sizeof(int) * W;
-  k_decode_step<<<dim3(1, (unsigned)B), threads, smem, (cudaStream_t)stream>>>(p);
-  return check_launch("decode_step_codes");
+  return launch_k("decode_step_codes", k_decode_step, dim3(1, (unsigned)B), dim3(threads), smem,
+                  (cudaStream_t)stream, p);
 }

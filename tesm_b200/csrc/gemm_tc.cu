@@ -56,12 +56,34 @@ struct Params {
   int c_local, c_gate;
   int proj_vec;
   int dual_tma;  // bf16 proj and output, 16-byte aligned: local/gate via TMA loads, output via TMA store
-  // split-K (small M): work unit = (tile, split); int32 partials are added atomically into ws
-  // (exact, so the result does not depend on the order), a finalize kernel scales them
-  int splits;
-  int32_t *ws;
+  // split-K (small M).  Work units: the first n_full tiles whole, then every remaining tile
+  // cut into `splits` k-ranges, all of them in one round of the persistent loop.  A split owns
+  // the 32-column chunks c with c % splits == its index: it stores its int32 partials of the
+  // other chunks into its slice of `part`, counts itself in cnt[tile * 2 + pair rank], waits
+  // until every split has counted, adds the other slices to its own chunks (exact integers)
+  // and runs the epilogue on them; a second count resets the counter to zero for the next call.
+  int splits, n_full;
+  int32_t *ws;      // caller scratch: kCounterInts counters (zero between calls), then the slices
   int64_t ws_bytes;
+  int32_t *cnt, *part;
+  int part_rb, part_cb;  // 32-row blocks and 32-column blocks of one partial slice
 };
+
+constexpr int kCounterInts = 4096;  // 16 KB of tile counters at the start of the split-K scratch
+
+// work unit u -> (tile, split, number of splits of that tile)
+__device__ __forceinline__ void unit_info(const Params &p, int u, int &t, int &sp, int &ns) {
+  if (u < p.n_full) {
+    t = u;
+    sp = 0;
+    ns = 1;
+  } else {
+    const int v = u - p.n_full;
+    t = p.n_full + v / p.splits;
+    sp = v - (t - p.n_full) * p.splits;
+    ns = p.splits;
+  }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -262,6 +284,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *pbar = bars + 2 * NST + 6;  // EPI_WARPS * DCH barriers
   uint8_t *sP = sB + NST * B_BYTES + 1024;  // 1024-aligned (swizzled TMA boxes)
   uint8_t *sO = sP + EPI_WARPS * DCH * 2 * 2048;
+  // plain / SwiGLU epilogues: a 4 KB staging block per epilogue warp, through which each 32 x 32
+  // output chunk is transposed so that global stores cover whole row segments
+  uint8_t *sStage = sP;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = PAIR ? cluster_rank() : 0;  // 0: the pair leader
@@ -271,7 +296,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr uint32_t ACC_COLS = DUAL ? 2 * BN : MT * BN;  // TMEM columns of one tile's accumulator(s)
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
 
+  // split-K meeting words of the epilogue warps (see the split-K branch of the epilogue)
+  __shared__ int s_last, s_arrive, s_decided;
   if (threadIdx.x == 0) {
+    s_last = s_arrive = s_decided = 0;
     for (int i = 0; i < NST; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -306,38 +334,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // programmatic dependent launch: the set-up above overlapped the previous kernel; only the
+  // producer's first weight-tile requests (constant data) go out before its completion
+  if (threadIdx.x == 0) pdl_trigger();
+  if (warp != 0) pdl_wait();
 
-  const int total = p.num_m_tiles * p.num_n_tiles * p.splits;
+  const int total = p.n_full + (p.num_m_tiles * p.num_n_tiles - p.n_full) * p.splits;
   const int nk_all = p.num_k_blocks;
 
   if (warp == 0) {
     if (lane == 0) {
+      // weight tiles of the first stages: requested before waiting for the previous kernel
+      int pre = 0;
+      if (ustart < total) {
+        int mt, nt, t, sp, ns;
+        unit_info(p, ustart, t, sp, ns);
+        tile_coords(p, t, mt, nt);
+        const int kb_lo = sp * nk_all / ns, kb_hi = (sp + 1) * nk_all / ns;
+        pre = kb_hi - kb_lo < NST ? kb_hi - kb_lo : NST;
+        for (int i = 0; i < pre; ++i) {  // fresh stages: no empty-barrier wait needed
+          const int kb = kb_lo + i;
+          if (PAIR) {
+            if (crank == 0) mbar_expect_tx(&full[i], 2 * (A_BYTES + B_BYTES));
+            tma_load_2d_pair(sB + i * B_BYTES, &tmB, mapa_shared(smem_u32(&full[i]), 0), kb * BK,
+                             nt * BN + (int)crank * (BN / 2));
+          } else {
+            mbar_expect_tx(&full[i], A_BYTES + B_BYTES);
+            tma_load_2d(sB + i * B_BYTES, &tmB, &full[i], kb * BK, nt * BN);
+          }
+        }
+      }
+      pdl_wait();
       uint32_t it = 0;
       bool ok = true;
       for (int u = ustart; u < total && ok; u += ustride) {
-        int mt, nt;
-        const int t = u / p.splits, sp = u - t * p.splits;
+        int mt, nt, t, sp, ns;
+        unit_info(p, u, t, sp, ns);
         tile_coords(p, t, mt, nt);
-        const int kb_lo = sp * nk_all / p.splits, kb_hi = (sp + 1) * nk_all / p.splits;
+        const int kb_lo = sp * nk_all / ns, kb_hi = (sp + 1) * nk_all / ns;
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const uint32_t stage = it % NST, phase = (it / NST) & 1;
-          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+          const bool b_done = (int)it < pre;  // weight tile already requested above
+          if (!b_done && !mbar_wait(&empty[stage], phase ^ 1)) {
             ok = false;
             break;
           }
           if (PAIR) {
             // the leader's barrier counts both CTAs' bytes; each CTA loads its own halves
-            if (crank == 0) mbar_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+            if (crank == 0 && !b_done) mbar_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             tma_load_2d_pair(sA + stage * A_BYTES, &tmA, fb, kb * BK, (mt * 2 + (int)crank) * BM);
-            tma_load_2d_pair(sB + stage * B_BYTES, &tmB, fb, kb * BK, nt * BN + (int)crank * (BN / 2));
+            if (!b_done) tma_load_2d_pair(sB + stage * B_BYTES, &tmB, fb, kb * BK, nt * BN + (int)crank * (BN / 2));
           } else {
-            mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+            if (!b_done) mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
             tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM * MT);
-            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+            if (!b_done) tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
           }
         }
       }
+    } else {
+      pdl_wait();
     }
   } else if (warp == 1) {
     if (lane == 0 && crank == 0) {  // pair: the leader issues the MMAs for both CTAs
@@ -346,8 +402,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int u = ustart; u < total && ok; u += ustride, ++tile_i) {
         const uint32_t buf = tile_i & 1, use = tile_i >> 1;
-        const int sp = u % p.splits;
-        const int kb_lo = sp * nk_all / p.splits, kb_hi = (sp + 1) * nk_all / p.splits;
+        int t_, sp, ns;
+        unit_info(p, u, t_, sp, ns);
+        const int kb_lo = sp * nk_all / ns, kb_hi = (sp + 1) * nk_all / ns;
         if (!mbar_wait(&tempty[buf], (use & 1) ^ 1)) break;
         fence_after();
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
@@ -421,9 +478,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       else
         mbar_arrive(&tempty[b]);
     };
+    int nsplit = 0;  // split units this CTA's epilogue has handled (the same count in every warp)
     for (int u = ustart; u < total; u += ustride, ++tile_i) {
-      int mt, nt;
-      tile_coords(p, u / p.splits, mt, nt);
+      int mt, nt, t_u, sp_u, ns_u;
+      unit_info(p, u, t_u, sp_u, ns_u);
+      tile_coords(p, t_u, mt, nt);
       const uint32_t buf = tile_i & 1, use = tile_i >> 1;
       if (dual_tma && tile_i == 0) {
 #pragma unroll
@@ -434,30 +493,156 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int sub = MT == 2 ? half : 0;  // skinny tiles: each warp half owns one M sub-tile
       const int row = (PAIR ? mt * 2 + (int)crank : mt * MT + sub) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
-      if (!DUAL && p.splits > 1) {
+      // split-K: the other splits' partial sums of this tile are added to the accumulators read
+      // from TMEM (only in the split that arrives last, see Params)
+      bool fix = false;
+      // A partial slice is stored in 32 x 32 blocks (32 rows of this warp, 32 columns), each
+      // lane-major: int4 jj of lane l holds columns 4jj..4jj+3 of row l, so every warp-wide
+      // access covers 512 contiguous bytes.
+      const int rblk = (row - lane) >> 5;
+      auto part_blk = [&](int slice, int n0) -> int4 * {
+        return reinterpret_cast<int4 *>(p.part) +
+               (((int64_t)slice * p.part_rb + rblk) * p.part_cb + (n0 >> 5)) * 256;
+      };
+      auto acc_fix = [&](uint32_t (&r)[32], int n0) {
+        if (!fix || n0 >= p.N) return;
+        for (int s2 = 0; s2 < ns_u; ++s2) {
+          if (s2 == sp_u) continue;
+          const int4 *blk = part_blk(s2, n0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int4 v4 = __ldcg(blk + j * 32 + lane);
+            r[4 * j] += (uint32_t)v4.x;
+            r[4 * j + 1] += (uint32_t)v4.y;
+            r[4 * j + 2] += (uint32_t)v4.z;
+            r[4 * j + 3] += (uint32_t)v4.w;
+          }
+        }
+      };
+      // Store one 32 x 32 chunk (lane l holds row rbase + l) through the warp's staging block:
+      // bf16 rows of 64 B go out 8 rows per instruction, fp32 rows of 128 B 4 rows per
+      // instruction.  Warp-collective; rows >= M are skipped.  Full chunks only (n0 + 32 <= width).
+      auto stage_store = [&](const float (&v)[32], int rbase, int n0) {
+        const uint32_t st = smem_u32(sStage + ew * 4096);
+        __syncwarp();  // the previous chunk's reads of the block are done
+        if (p.out_dtype == TESM_BF16) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+            const uint4 u4 = *reinterpret_cast<uint4 *>(h);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(st + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)),
+                         "r"(u4.x), "r"(u4.y), "r"(u4.z), "r"(u4.w));
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = i * 8 + (lane >> 2), j = lane & 3;
+            const uint4 u4 = lds128(st + rr * 64 + ((j ^ ((rr >> 1) & 3)) << 4));
+            if (rbase + rr < p.M)
+              *reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + (int64_t)(rbase + rr) * p.ldo +
+                                         n0 + j * 8) = u4;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(st + lane * 128 + ((j ^ (lane & 7)) << 4)),
+                         "f"(v[4 * j]), "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3]));
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = i * 4 + (lane >> 3), j = lane & 7;
+            const uint4 u4 = lds128(st + rr * 128 + ((j ^ (rr & 7)) << 4));
+            if (rbase + rr < p.M)
+              *reinterpret_cast<uint4 *>(reinterpret_cast<float *>(p.out) + (int64_t)(rbase + rr) * p.ldo + n0 +
+                                         j * 4) = u4;
+          }
+        }
+      };
+      if (!DUAL && ns_u > 1) {
+        // split unit: every split finalises the 32-column chunks c with c % ns == its split
+        // index (a reduce-scatter).  Phase 1 stores the chunks the other splits own into this
+        // split's slice; after every split of the tile has stored (counted in cnt), each one adds
+        // the others' slices to its own chunks and runs the epilogue on them.  All splits of a
+        // tile run in the same round of the persistent loop, so the wait always ends.
         const int c_lo = MT == 2 ? 0 : half * (BN / 64), c_hi = MT == 2 ? BN / 32 : (half + 1) * (BN / 64);
 #pragma unroll 1
         for (int c = c_lo; c < c_hi; ++c) {
+          const int owner = (p.swiglu ? (c & 3) : c) % ns_u;
+          if (owner == sp_u) continue;
           uint32_t r[32];
           tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + sub * BN + c * 32, r);
           const int n0 = nt * BN + c * 32;
-          if (!row_ok || n0 >= p.N) continue;
-          // each split owns its slice of the workspace: plain stores, summed by the finalize kernel
-          int32_t *wrow = p.ws + ((int64_t)(u % p.splits) * p.M + row) * p.N + n0;
-          if (n0 + 32 <= p.N && (p.N & 3) == 0) {
+          if (n0 >= p.N) continue;
+          int4 *blk = part_blk(sp_u, n0);  // rows past M and columns past N are stored too (unused)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              reinterpret_cast<int4 *>(wrow)[j] = make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2],
-                                                            (int)r[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) wrow[j] = (int32_t)r[j];
-          }
+          for (int j = 0; j < 8; ++j)
+            __stcg(blk + j * 32 + lane, make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2],
+                                                  (int)r[4 * j + 3]));
         }
-        fence_before();
+        // the epilogue warps meet through shared-memory words with bounded waits (no named
+        // barrier, so a warp that gave up on an earlier wait cannot leave the others blocked)
         __syncwarp();
-        release(buf);
-        continue;
+        ++nsplit;
+        if (lane == 0) {
+          __threadfence();  // this warp's partial stores before the count (cumulative)
+          atomicAdd(&s_arrive, 1);
+        }
+        int ok = 0;
+        if (ew == 0 && lane == 0) {
+          const long long t0 = clock64();
+          bool met = true;
+          while (*(volatile int *)&s_arrive < EPI_WARPS * nsplit) {
+            if (clock64() - t0 > kWaitCycles) {
+              flag_timeout();
+              met = false;
+              break;
+            }
+          }
+          if (met) {
+            __threadfence();
+            int *c = p.cnt + (int64_t)t_u * 2 + (int)crank;
+            atomicAdd(c, 1);
+            const long long t1 = clock64();
+            while (true) {  // every split of the tile has stored its partials
+              int v;
+              asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(c) : "memory");
+              if (v >= ns_u) break;
+              if (clock64() - t1 > kWaitCycles) {
+                flag_timeout();
+                met = false;
+                break;
+              }
+            }
+            if (met) {
+              ok = 1;
+              // second count: the split that completes it resets the counter for the next call
+              // (every split has passed the wait above by then)
+              if (atomicAdd(c, 1) == 2 * ns_u - 1) *c = 0;
+            }
+          }
+          s_last = ok;
+          __threadfence_block();
+          *(volatile int *)&s_decided = nsplit;
+        } else if (lane == 0) {
+          const long long t0 = clock64();
+          while (*(volatile int *)&s_decided < nsplit) {
+            if (clock64() - t0 > kWaitCycles) {
+              flag_timeout();
+              break;
+            }
+          }
+          ok = *(volatile int *)&s_decided >= nsplit ? *(volatile int *)&s_last : 0;
+        }
+        fix = __shfl_sync(0xffffffffu, ok, 0) != 0;
+        if (!fix) {
+          fence_before();
+          __syncwarp();
+          release(buf);
+          continue;
+        }
+        __threadfence_block();
       }
       const float xs = row_ok ? p.inv_scale[row] : 0.f;
       const float wd0 = p.w_deq[0];
@@ -465,7 +650,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float s1 = xs * wd0, s2 = (row_ok ? p.inv_scale2[row] : 0.f) * p.w_deq2[0];
         int mtn = 0, ntn = 0;
         const int un = u + ustride;
-        if (un < total) tile_coords(p, un / p.splits, mtn, ntn);
+        if (un < total) {
+          int tn, spn, nsn;
+          unit_info(p, un, tn, spn, nsn);
+          tile_coords(p, tn, mtn, ntn);
+        }
 #pragma unroll
         for (int cc = 0; cc < DCH; ++cc) {
           const int c = half * DCH + cc;
@@ -580,38 +769,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int c = half * 2; c < half * 2 + 2; ++c) {
           uint32_t rg[32], ru[32];
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+          if (fix && c % ns_u != sp_u) continue;  // split-K: another split finalises this chunk
           tmem_ld32(tbase + c * 32, rg);
           tmem_ld32(tbase + 128 + c * 32, ru);
           const int ng = nt * BN + c * 32;    // weight row of the first gate column
           const int no = nt * 128 + c * 32;   // output column
-          if (!row_ok || ng >= p.N) continue;
+          if (ng >= p.N) continue;
+          acc_fix(rg, ng);
+          acc_fix(ru, ng + 128);
           float v[32];
+          // per-row dequantisation factors of the chunk's 32 gate and 32 up rows: one coalesced
+          // load each, handed to the lanes by shuffles
+          // (the conversion and transcendental unit is the epilogue's bottleneck: accumulators
+          // are converted with integer adds when |acc| < 2^22, and silu takes one exp2 and one
+          // reciprocal, relative error a few ulp)
+          const float dg = p.w_deq[ng + lane], du = p.w_deq[ng + 128 + lane];
+          const bool small_acc = p.K < 32768;  // |acc| <= 128 K < 2^22
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float g = (float)(int32_t)rg[j] * xs * p.w_deq[ng + j];
-            const float u = (float)(int32_t)ru[j] * xs * p.w_deq[ng + 128 + j];
-            v[j] = (g / (1.f + expf(-g))) * u;
+            const float ag = small_acc ? acc_to_f(rg[j]) : (float)(int32_t)rg[j];
+            const float au = small_acc ? acc_to_f(ru[j]) : (float)(int32_t)ru[j];
+            const float g = ag * xs * __shfl_sync(0xffffffffu, dg, j);
+            const float u = au * xs * __shfl_sync(0xffffffffu, du, j);
+            v[j] = __fdividef(g, 1.f + __expf(-g)) * u;
           }
           const int nout = p.N / 2;
           if (p.vec_store && no + 32 <= nout) {
-            if (p.out_dtype == TESM_BF16) {
-              uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) + (int64_t)row * p.ldo + no);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                __nv_bfloat162 h[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
-                dst[j] = *reinterpret_cast<uint4 *>(h);
-              }
-            } else {
-              float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + (int64_t)row * p.ldo + no);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (no + j < nout) store_f(p.out, p.out_dtype, (int64_t)row * p.ldo + no + j, v[j]);
+            stage_store(v, row - lane, no);
+            continue;
           }
+          if (!row_ok) continue;
+          for (int j = 0; j < 32; ++j)
+            if (no + j < nout) store_f(p.out, p.out_dtype, (int64_t)row * p.ldo + no + j, v[j]);
         }
         fence_before();
         __syncwarp();
@@ -621,17 +810,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int c_lo = MT == 2 ? 0 : half * (BN / 64), c_hi = MT == 2 ? BN / 32 : (half + 1) * (BN / 64);
 #pragma unroll 1
       for (int c = c_lo; c < c_hi; ++c) {
+        if (fix && c % ns_u != sp_u) continue;  // split-K: another split finalises this chunk
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + sub * BN + c * 32;
         tmem_ld32(taddr, r);
         const int n0 = nt * BN + c * 32;
-        if (!row_ok || n0 >= p.N) continue;
+        if (n0 >= p.N) continue;
+        acc_fix(r, n0);
         float v[32];
+        const float wdl = p.per_row ? (n0 + lane < p.N ? p.w_deq[n0 + lane] : 0.f) : wd0;
+        const bool small_acc = p.K < 32768;  // |acc| <= 128 K < 2^22: convert without the XU pipe
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float wd = p.per_row ? (n0 + j < p.N ? p.w_deq[n0 + j] : 0.f) : wd0;
-          v[j] = (float)(int32_t)r[j] * xs * wd;
+          const float wd = p.per_row ? __shfl_sync(0xffffffffu, wdl, j) : wd0;
+          v[j] = (small_acc ? acc_to_f(r[j]) : (float)(int32_t)r[j]) * xs * wd;
         }
+        if (p.out && p.vec_store && n0 + 32 <= p.N && !p.acc_out) {
+          stage_store(v, row - lane, n0);
+          continue;
+        }
+        if (!row_ok) continue;
         if (p.acc_out) {
           int32_t *arow = p.acc_out + (int64_t)row * p.ld_acc;
           for (int j = 0; j < 32; ++j)
@@ -685,6 +883,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 __global__ void k_splitk_finalize(const int32_t *ws, int splits, int M, int N, const float *inv_scale,
                                   const float *w_deq, int per_row, int swiglu, void *out, int out_dtype, int64_t ldo,
                                   int32_t *acc_out, int64_t ld_acc) {
+  pdl_trigger();
+  pdl_wait();
   const int nout = swiglu ? N / 2 : N;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * nout) return;
@@ -773,7 +973,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   }
   constexpr int NST = PAIR ? 6 : STAGES;
   const size_t smem = 1024 + (size_t)NST * (MT * BM * BK + (PAIR ? BN / 2 : BN) * BK) +
-                      (DUAL ? 1024 + (size_t)EPI_WARPS * (BN / 64) * 3 * 2048 : 256);
+                      (DUAL ? 1024 + (size_t)EPI_WARPS * (BN / 64) * 3 * 2048 : 1024 + (size_t)EPI_WARPS * 4096);
   auto kern = k_gemm_i8<BN, DUAL, MT, PAIR>;
   static bool attr = false;
   static int max_clusters = 0;
@@ -786,16 +986,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   p.num_k_blocks = (int)ceil_div(p.K, BK);
   p.group_m = PAIR ? 8 : 16;
   const int tiles = p.num_m_tiles * p.num_n_tiles;
-  p.splits = 1;
-  if (!PAIR && !DUAL && MT == 1 && p.ws && tiles < sm_count() && p.num_k_blocks >= 8) {
-    int s = (int)ceil_div(sm_count(), tiles);
-    if (s > 8) s = 8;
-    if (s > p.num_k_blocks / 4) s = p.num_k_blocks / 4;
-    while (s >= 2 && (int64_t)s * p.M * p.N * 4 > p.ws_bytes) --s;
-    if (s >= 2) p.splits = s;
-  }
-  const int total = tiles * p.splits;
-  if (PAIR) {
+  if (PAIR && !max_clusters) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -804,18 +995,61 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
     at[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (!max_clusters) {
-      cfg.gridDim = dim3(2 * (sm_count() / 2));
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        n = sm_count() / 2;
-      }
-      max_clusters = n;
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
     }
+    max_clusters = n;
+  }
+  // split-K when the tiles do not fill the machine (small M): whole tiles first, the tail (or,
+  // with fewer tiles than workers, every tile) cut into k-ranges so the units fill the workers
+  p.splits = 1;
+  p.n_full = tiles;
+  const int workers = PAIR ? max_clusters : sm_count();
+  if (!DUAL && MT == 1 && p.ws && p.ws_bytes > (int64_t)kCounterInts * 4 && p.num_k_blocks >= 4 &&
+      tiles * 2 <= kCounterInts) {
+    const int nfull = tiles >= workers ? (tiles / workers) * workers : 0;
+    const int rem = tiles - nfull;
+    static const int smax = [] {
+      const char *e = getenv("TESM_SPLITK_MAX");  // tuning override: most splits per tile
+      return e ? atoi(e) : 8;
+    }();
+    if (rem > 0) {
+      int s = workers / rem;
+      if (s > smax) s = smax;
+      if (s > BN / 32 / (p.swiglu ? 2 : 1)) s = BN / 32 / (p.swiglu ? 2 : 1);  // chunks a split owns
+      if (s > p.num_k_blocks / 2) s = p.num_k_blocks / 2;
+      p.part_rb = p.num_m_tiles * (BM * MT * (PAIR ? 2 : 1)) / 32;
+      p.part_cb = (int)ceil_div(p.N, 32);
+      const int64_t slice = (int64_t)p.part_rb * 32 * p.part_cb * 32 * 4;
+      while (s >= 2 && s * slice > p.ws_bytes - (int64_t)kCounterInts * 4) --s;
+      if (s >= 2) {
+        p.splits = s;
+        p.n_full = nfull;
+        p.cnt = p.ws;
+        p.part = p.ws + kCounterInts;
+      }
+    }
+  }
+  const int total = p.n_full + (tiles - p.n_full) * p.splits;
+  if (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     const int clusters = total < max_clusters ? total : max_clusters;
     cfg.gridDim = dim3(2 * clusters);
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, ml, mg, mo, p);
@@ -823,14 +1057,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
     return check_launch("gemm_i8 (CTA pairs)");
   }
   const int grid = total < sm_count() ? total : sm_count();
-  kern<<<grid, NUM_THREADS, smem, st>>>(ma, mb, ml, mg, mo, p);
-  int rc2 = check_launch("gemm_i8");
-  if (rc2 || p.splits == 1) return rc2;
-  const int64_t n = (int64_t)p.M * (p.swiglu ? p.N / 2 : p.N);
-  k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(p.ws, p.splits, p.M, p.N, p.inv_scale, p.w_deq,
-                                                                p.per_row, p.swiglu, p.out, p.out_dtype, p.ldo,
-                                                                p.acc_out, p.ld_acc);
-  return check_launch("gemm_i8 split-K finalize");
+  return launch_k("gemm_i8", kern, dim3(grid), dim3(NUM_THREADS), smem, st, ma, mb, ml, mg, mo, p);
 }
 
 // CTA pairs for large plain / SwiGLU GEMMs: enough 256 x 256 tiles to fill every SM pair.
@@ -878,7 +1105,10 @@ extern "C" int tesm_b200_gemm_i8_swiglu(const int8_t *codes, int64_t ld_codes, c
   }
   const int esz = out_dtype == TESM_BF16 ? 2 : 4;
   p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
-  if (tc::use_pairs(M, 2 * F)) return tc::launch<256, false, 1, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
+  // CTA pairs when the 256 x 256 tiles fill the SM pairs, and for decode batches (129..256 rows,
+  // where split-K fills them)
+  if (tc::use_pairs(M, 2 * F) || (M > 128 && M <= 256 && p.ws))
+    return tc::launch<256, false, 1, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
   return tc::launch<256>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
 }
 
@@ -968,6 +1198,15 @@ extern "C" int tesm_b200_gemm_i8(const int8_t *codes, int64_t ld_codes, const fl
     // up to 128 rows leave half of each pair tile empty: pairs still win when N is small (fewer,
     // longer-K tiles: 4096 x 11008 at M = 128, 34.5 vs 43.7 us) but not for wide N
     // (11008 x 4096: 29.3 vs 24.8 us)
+    // 129..256 rows: 256 x 256 pair tiles (the activation block is re-read once per 256 output
+    // columns instead of once per 64 / 128) with split-K filling the SM pairs
+    // (TESM_SKINNY_WIDE=0 selects the narrow pair tiles below)
+    static const int wide = [] {
+      const char *e = getenv("TESM_SKINNY_WIDE");
+      return e ? atoi(e) : 1;
+    }();
+    if (pair && forced == 0 && wide && M > 128 && p.ws)
+      return tc::launch<256, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
     if (pair && forced == 0 && (M > 128 || N < 8192)) {
       if (N >= 8192) return tc::launch<128, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);
       return tc::launch<64, false, 1, true>(codes, ld_codes, tern, ld_tern, p, st);

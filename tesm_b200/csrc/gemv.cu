@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(WPC * 32, (NT >= 4 ? 1 : NT == 2 ? (WPC == 8 ?
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int row0 = blockIdx.x * 16;
+  pdl_trigger();
   const int rA = min(row0 + g, p.N - 1), rB = min(row0 + g + 8, p.N - 1);
   const int spw = (p.steps_total + WPC - 1) / WPC;  // steps per warp
   const int s_begin = warp * spw, s_end = min(s_begin + spw, p.steps_total);
@@ -158,7 +159,7 @@ static int launch_gemv_rows(const GemvParams &p, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddepcontrol.wait
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_rows<NT, WPC, PF>, p);
   if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemv_int2 launch: ") + cudaGetErrorString(e));
   return TESM_OK;

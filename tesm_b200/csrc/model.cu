@@ -11,6 +11,8 @@ namespace tesm {
 // hidden[m] = E[ids[m]] + P[pos0 + m % L]  (mixer_seq_simple.py:183-184)
 __global__ void k_embed(const int64_t *ids, int64_t M, int L, const void *emb, const void *pemb, int wdtype, int Dm,
                         const int *pos_dev, int pos_host, void *out, int odtype) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t m = blockIdx.x;
   const int pos = (pos_dev ? pos_dev[0] : pos_host) + (int)(m % L);
   const int64_t id = ids[m];
@@ -30,6 +32,8 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
                                     int ydtype, int vec) {
   __shared__ float redf[32];
   __shared__ int redi[32];
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int64_t groups_in = (K + 15) / 16;
   const int xsz = xdtype == TESM_BF16 ? 2 : 4, ysz = ydtype == TESM_BF16 ? 2 : 4;
@@ -101,6 +105,8 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
 // bf16 / 32-byte fp32 vectors when aligned; blk is a multiple of 8, so a group never straddles
 // an interleave block.
 __global__ void k_silu_mul(const void *gu, int dtype, int64_t M, int F, void *out, int odtype, int blk, int vec) {
+  pdl_trigger();
+  pdl_wait();
   const int f0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (f0 >= F) return;
   int gcol, ucol;
@@ -158,9 +164,8 @@ extern "C" int tesm_b200_embed(const int64_t *ids, int64_t B, int64_t L, const v
                                int wdtype, int64_t Dm, const int *pos_dev, int64_t pos_host, void *out, int odtype,
                                tesm_stream_t stream) {
   TESM_REQUIRE(ids && emb && pos_emb && out && B > 0 && L > 0 && Dm > 0, "embed: bad argument");
-  k_embed<<<(unsigned)(B * L), 256, 0, (cudaStream_t)stream>>>(ids, B * L, (int)L, emb, pos_emb, wdtype, (int)Dm,
-                                                               pos_dev, (int)pos_host, out, odtype);
-  return check_launch("embed");
+  return launch_k("embed", k_embed, dim3((unsigned)(B * L)), dim3(256), 0, (cudaStream_t)stream, ids, B * L, (int)L,
+                  emb, pos_emb, wdtype, (int)Dm, pos_dev, (int)pos_host, out, odtype);
 }
 
 extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const float *residual, float *residual_out,
@@ -186,15 +191,10 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
   int64_t threads = round_up(ceil_div(groups_out, gpt), 32);
   if (threads < 32) threads = 32;
   TESM_REQUIRE(threads <= 1024, "add_rmsnorm_quant: K too large");
-  if (gpt == 1)
-    k_add_rmsnorm_quant<1><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-        x, xdtype, residual, residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale,
-        rowsum, y_out, ydtype, vec);
-  else
-    k_add_rmsnorm_quant<4><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-        x, xdtype, residual, residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale,
-        rowsum, y_out, ydtype, vec);
-  return check_launch("add_rmsnorm_quant");
+  return launch_k("add_rmsnorm_quant", gpt == 1 ? k_add_rmsnorm_quant<1> : k_add_rmsnorm_quant<4>,
+                  dim3((unsigned)M), dim3((unsigned)threads), 0, (cudaStream_t)stream, x, xdtype, residual,
+                  residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale, rowsum,
+                  y_out, ydtype, vec);
 }
 
 extern "C" int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t F, int64_t blk, void *out,
@@ -209,8 +209,8 @@ extern "C" int tesm_b200_silu_mul(const void *gu, int dtype, int64_t M, int64_t 
   const int64_t groups = ceil_div(F, 8);
   const int threads = groups >= 128 ? 128 : (int)round_up(groups, 32);
   dim3 grid((unsigned)ceil_div(groups, threads), (unsigned)(M < 65535 ? M : 65535));
-  k_silu_mul<<<grid, threads, 0, (cudaStream_t)stream>>>(gu, dtype, M, (int)F, out, odtype, (int)blk, vec);
-  return check_launch("silu_mul");
+  return launch_k("silu_mul", k_silu_mul, grid, dim3(threads), 0, (cudaStream_t)stream, gu, dtype, M, (int)F, out,
+                  odtype, (int)blk, vec);
 }
 
 extern "C" int tesm_b200_cache_fill(const void *proj, int dtype, int64_t ldp, const float *states, int64_t RM,

@@ -118,9 +118,10 @@ __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, in
                             const float *__restrict__ amax_in) {
   __shared__ float redf[32];
   __shared__ int redi[32];
-  // let a programmatically serialized consumer (the GEMV) start its weight prefetch now; it
-  // still waits for this whole grid before reading the codes
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  // let a programmatically serialized consumer (the GEMV, the GEMM) start its weight prefetch
+  // now; it still waits for this whole grid before reading the codes
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int64_t groups_in = (K + 15) / 16;
   const int esz = dtype == TESM_BF16 ? 2 : 4;
@@ -242,13 +243,9 @@ static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_
   TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
   const int esz = dtype == TESM_BF16 ? 2 : 4;
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
-  if (gpt == 1)
-    k_quant_act<1><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-        x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
-  else
-    k_quant_act<kQuantGPT><<<(unsigned)M, (unsigned)threads, 0, (cudaStream_t)stream>>>(
-        x, dtype, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
-  return check_launch("quant_act");
+  return launch_k("quant_act", gpt == 1 ? k_quant_act<1> : k_quant_act<kQuantGPT>, dim3((unsigned)M),
+                  dim3((unsigned)threads), 0, (cudaStream_t)stream, x, dtype, K, ldx, eps, codes, ld_codes, layout,
+                  groups_out, inv_scale, rowsum, vec, amax);
 }
 
 extern "C" int tesm_b200_quant_act(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,

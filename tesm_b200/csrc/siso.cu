@@ -158,6 +158,8 @@ static int launch_global(GlobalEntParams &p, cudaStream_t st) {
 // Thread = 8 consecutive columns of one row (grid.y strides over rows).
 __global__ void k_combine(ProjCols pc, const void *sp, const void *ep, int sdtype, int64_t M, int Dm, void *y,
                           int ydtype, int vec) {
+  pdl_trigger();
+  pdl_wait();
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= Dm) return;
   const int psz = pc.dtype == TESM_BF16 ? 2 : 4, ssz = sdtype == TESM_BF16 ? 2 : 4, ysz = ydtype == TESM_BF16 ? 2 : 4;
@@ -355,6 +357,6 @@ extern "C" int tesm_b200_combine(const void *proj, int dtype, int64_t ldp, int64
   const int64_t groups = ceil_div(Dm, 8);
   const int threads = groups >= 128 ? 128 : (int)round_up(groups, 32);
   dim3 grid((unsigned)ceil_div(groups, threads), (unsigned)(M < 65535 ? M : 65535));
-  k_combine<<<grid, threads, 0, (cudaStream_t)stream>>>(pc, sp, ep, sdtype, M, (int)Dm, y, ydtype, vec);
-  return check_launch("combine");
+  return launch_k("combine", k_combine, grid, dim3(threads), 0, (cudaStream_t)stream, pc, sp, ep, sdtype, M, (int)Dm, y,
+                  ydtype, vec);
 }

@@ -7,6 +7,7 @@ device; ownership stays with torch.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -148,17 +149,22 @@ _SPLITK = {}
 SPLITK_MAX_M = 1024
 
 
+SPLITK_COUNTERS = 4096  # int32 tile counters at the start of the scratch (zero between calls)
+
+
 def splitk_workspace(M: int, N: int, device):
-    """int32 split-K scratch shared by the small-M tensor-core GEMMs of a device (room for 8
-    partial M x N slices; every split writes its slice before the finalize reads it, so no
-    initialisation is needed).  None for large M, where split-K is never chosen."""
+    """int32 split-K scratch shared by the small-M tensor-core GEMMs of a device: tile counters
+    (zero-initialised here; every GEMM call leaves them zero again) followed by room for 8
+    partial M x N slices.  None for large M, where split-K is never chosen."""
     if M > SPLITK_MAX_M:
         return None
-    need = 8 * M * N
+    need = SPLITK_COUNTERS + 8 * round_up(M, 256) * round_up(N, 32)  # slices cover whole tiles
     key = torch.device(device).index
     buf = _SPLITK.get(key)
     if buf is None or buf.numel() < need:
-        buf = torch.empty(max(need, 1 << 20), device=device, dtype=torch.int32)
+        if buf is not None:
+            torch.cuda.current_stream(device).synchronize()  # the old buffer may still be in use
+        buf = torch.zeros(max(need, 1 << 20), device=device, dtype=torch.int32)
         _SPLITK[key] = buf
     return buf
 
@@ -408,11 +414,15 @@ def silu_mul(gu, F, out, blk=0):
               dtype_code(out.dtype), _stream())
 
 
+_SWIGLU_WIDE = os.environ.get("TESM_SKINNY_WIDE", "1") != "0"
+
+
 def gemm_swiglu(q: QuantAct, pw: PackedWeight, out_dtype, out=None):
     """Interleaved gate/up weight (blocks of 128 rows) -> silu(gate) * up, width pw.N // 2."""
     F = pw.N // 2
     out = out if out is not None else torch.empty(q.M, F, device=q.codes.device, dtype=out_dtype)
-    if q.M <= 256:  # decode batches: skinny-tile GEMM, then the gate on the interleaved output
+    if q.M <= 128 or (q.M <= 256 and not _SWIGLU_WIDE):
+        # small batches: skinny-tile GEMM, then the gate on the interleaved output
         gu = gemm(q.codes, q.inv, pw, q.M, out_dtype)
         silu_mul(gu, F, out, 128)
         return out
