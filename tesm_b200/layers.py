@@ -582,19 +582,23 @@ def lm_forward(lm, input_ids, labels=None, inference_params=None, prev_states=No
 
 
 class DecodeGraph:
-    """One greedy decode step of a TESMLMHeadModel captured in a CUDA graph.
+    """One decode step of a TESMLMHeadModel captured in a CUDA graph.
 
-    ``step()`` replays embedding -> every layer's incremental step -> lm_head -> argmax and
-    writes the chosen tokens back into the static input buffer; the host mirrors of each
+    The graph replays embedding -> every layer's incremental step -> lm_head for the tokens in
+    a static input buffer.  ``greedy=True`` also captures the argmax and writes the chosen tokens
+    back into that buffer, so ``step()`` chains steps on the device; ``greedy=False`` leaves the
+    next-token choice to the caller (sampling outside the graph): ``step_logits(tokens)`` copies
+    the tokens in, replays and returns the last-position logits.  The host mirrors of each
     layer's ``seq_pos`` / ``cache_idx`` are advanced after every replay (the device copies are
     advanced inside the graph by the decode kernels).
     """
 
-    def __init__(self, lm, inference_params, first_tokens):
+    def __init__(self, lm, inference_params, first_tokens, greedy=True):
         self.lm = lm
         self.ip = inference_params
         self.caches = inference_params["state_cache"]
         self.ids = first_tokens.clone()
+        self.greedy = greedy
         for c in self.caches.values():
             _prepare_cache(c, self.ids.device)
         # warm-up outside capture (allocates the split-K workspace, packs nothing new)
@@ -610,23 +614,52 @@ class DecodeGraph:
         with torch.cuda.graph(self.graph):
             out, _ = self.lm(self.ids, inference_params=self.ip)
             self.logits = out.logits
-            self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1, keepdim=True))
+            if greedy:
+                self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1, keepdim=True))
         for c, h in zip(self.caches.values(), hosts):  # capture ran no kernel; restore the mirrors
             c["seq_pos"], c["cache_idx"], c["_ctl_host"] = h
 
-    def step(self):
+    def _replay(self):
         for c in self.caches.values():  # paged snapshots are host-driven, outside the graph
             snapshot_if_due(c)
         self.graph.replay()
         for c in self.caches.values():
             _advance_host(c, c["ent_k_cache"].shape[1])
+
+    def step(self):
+        """Greedy graphs: one step on the tokens in the buffer; returns the next tokens."""
+        self._replay()
         return self.ids
+
+    def step_logits(self, tokens):
+        """One step on ``tokens`` (B, 1); returns the (B, vocab) logits of that position."""
+        self.ids.copy_(tokens)
+        self._replay()
+        return self.logits[:, -1, :]
+
+
+def _sample(logits, temperature, top_k):
+    """Next-token choice of ``TESMLMHeadModel.generate`` (mixer_seq_simple.py:659-668)."""
+    if temperature <= 0:
+        return logits.argmax(dim=-1, keepdim=True)
+    if temperature != 1.0:
+        logits = logits / temperature
+    if top_k > 0:
+        v, _ = torch.topk(logits, min(top_k, logits.size(-1)))
+        logits = logits.masked_fill(logits < v[:, [-1]], float("-inf"))
+    return torch.multinomial(torch.softmax(logits.float(), dim=-1), num_samples=1)
+
+
+GRAPH_MIN_TOKENS = 8  # fewer new tokens than this: eager steps (capturing a graph costs more)
 
 
 @torch.no_grad()
-def generate(lm, input_ids, max_new_tokens=64, temperature=1.0, top_k=0, use_cache=True):
+def generate(lm, input_ids, max_new_tokens=64, temperature=1.0, top_k=0, use_cache=True, use_graph=None):
     """``TESMLMHeadModel.generate`` (mixer_seq_simple.py:617-703) without vocabulary
-    suppression: prefill with the cache, then one incremental step per new token."""
+    suppression: prefill with the cache, then one incremental step per new token.  The steps
+    replay a captured decode graph (``DecodeGraph(greedy=False)``); sampling (temperature, top-k,
+    multinomial) and the EOS test run between replays, as the reference runs them between its
+    forward calls.  ``use_graph=False`` runs every step eagerly (same results)."""
     lm.eval()
     generated = input_ids
     cfg = lm.tesm_config
@@ -635,22 +668,24 @@ def generate(lm, input_ids, max_new_tokens=64, temperature=1.0, top_k=0, use_cac
     out, _ = lm(input_ids, inference_params=ip)
     logits = out.logits[:, -1, :]
     eos = getattr(cfg, "eos_token_id", None)
-    for _ in range(max_new_tokens):
-        if temperature <= 0:
-            nxt = logits.argmax(dim=-1, keepdim=True)
-        else:
-            if temperature != 1.0:
-                logits = logits / temperature
-            if top_k > 0:
-                v, _ = torch.topk(logits, min(top_k, logits.size(-1)))
-                logits = logits.masked_fill(logits < v[:, [-1]], float("-inf"))
-            nxt = torch.multinomial(torch.softmax(logits.float(), dim=-1), num_samples=1)
+    if use_graph is None:
+        use_graph = use_cache and max_new_tokens >= GRAPH_MIN_TOKENS
+    graph = None
+    for i in range(max_new_tokens):
+        nxt = _sample(logits, temperature, top_k)
         generated = torch.cat([generated, nxt], dim=1)
         if eos is not None and (nxt == eos).all():
             break
-        if use_cache:
+        if i == max_new_tokens - 1:
+            break  # the reference computes one more step whose logits it never uses
+        if use_cache and use_graph:
+            if graph is None:
+                graph = DecodeGraph(lm, ip, nxt, greedy=False)
+            logits = graph.step_logits(nxt)
+        elif use_cache:
             out, _ = lm(nxt, inference_params=ip)
+            logits = out.logits[:, -1, :]
         else:
             out, _ = lm(generated[:, -cfg.max_seq_len:])
-        logits = out.logits[:, -1, :]
+            logits = out.logits[:, -1, :]
     return generated

@@ -213,9 +213,13 @@ class TESMLMHeadModel(nn.Module):
 
     @torch.no_grad()
     def generate(self, input_ids, max_new_tokens: int = 64, temperature: float = 1.0, top_k: int = 0,
-                 use_cache: bool = True, **kwargs):
-        """Token generation with the recurrent-state cache (mixer_seq_simple.py:617-703)."""
-        return layers.generate(self, input_ids, max_new_tokens, temperature, top_k, use_cache)
+                 use_cache: bool = True, sparse_inference: bool = False, dynamic_activation: bool = True,
+                 use_graph=None):
+        """Token generation with the recurrent-state cache (mixer_seq_simple.py:617-703); the
+        incremental steps replay a captured CUDA graph.  ``sparse_inference`` /
+        ``dynamic_activation`` only act with vocabulary suppression, which is outside the b200
+        path (this model raises for it), so they are accepted and have no effect."""
+        return layers.generate(self, input_ids, max_new_tokens, temperature, top_k, use_cache, use_graph)
 
 
 def _init_weights(module, n_layer, initializer_range=0.02, rescale_prenorm_residual=True, n_residuals_per_layer=1):

@@ -317,3 +317,21 @@ def test_decode_graph_matches_eager(lib, B):
         assert max_rel(b, a) <= 1e-5
     for a, b in zip(t0, t1):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("temperature,top_k", [(0.0, 0), (0.8, 40), (1.0, 0)])
+def test_generate_graph_matches_eager(lib, temperature, top_k):
+    """generate() (mixer_seq_simple.py:617-703) replays a captured decode graph for its steps,
+    sampling between replays: under the same torch seed it yields exactly the tokens of the
+    eager step-by-step loop (temperature / top-k / multinomial as the reference samples)."""
+    cfg = dict(n_layer=2, d_model=256, d_state=64, ent_rank=16, d_intermediate=512, vocab_size=512, max_seq_len=128,
+               entanglement_window=8)
+    m = build_model(cfg).cuda().eval()
+    ids = torch.randint(0, 512, (4, 10), generator=torch.Generator().manual_seed(7)).cuda()
+    outs = []
+    for use_graph in (False, True):
+        torch.manual_seed(123)
+        outs.append(m.generate(ids, max_new_tokens=12, temperature=temperature, top_k=top_k, use_graph=use_graph))
+    assert outs[0].shape == (4, 22)
+    assert torch.equal(outs[0][:, :10], ids)
+    assert torch.equal(outs[0], outs[1])
