@@ -400,10 +400,11 @@ def run_gpu(args, rank, world, local_rank):
                    "ms_per_step": t_dec / args.decode_steps * 1e3, "cuda_graph": True, "sampling": "greedy argmax"}
             del dg, ip
             if world > 1:
-                # tensor-parallel decode over all ranks (FFN column/row split, out_proj row split,
-                # NCCL all-reduces inside the captured graph): one batch of 256 shared by the ranks
+                # tensor-parallel decode over all ranks (FFN column/row split, SISO mixer channel-
+                # parallel with all-gathers, NCCL collectives inside the captured graph): one batch
+                # of 256 shared by the ranks
                 from tesm_b200 import parallel
-                parallel.enable_tensor_parallel(model)
+                parallel.enable_mixer_parallel(model)
                 torch.cuda.empty_cache()
                 ip = {"state_cache": model.backbone.allocate_inference_cache(Bd, CFG["max_seq_len"])}
                 o, _ = model(prompt, inference_params=ip, logits_to_keep=1)
@@ -722,18 +723,31 @@ def run_cfg4(args, peaks, rank=0, world=1):
     import torch
     from tesm_b200 import ops
     from tesm_b200.modules import TESMMIMO_Optimized
+    import math
     torch.manual_seed(0)
     B, L = 4, 16384
-    if B % world:
-        raise SystemExit(f"config 4 splits its batch of {B} over the ranks (2 or 4 GPUs); "
-                         f"{world} does not divide it (the batch x head split is not built)")
-    B //= world
+    # (b, h) units: the batch over gcd(4, world) rank groups, the 16 heads over the ranks of a
+    # group (8 GPUs: 4 sequences x 2 head halves), head-parallel through NCCL within a group
+    bsplit = math.gcd(B, world)
+    hsplit = world // bsplit
+    if 16 % hsplit:
+        raise SystemExit(f"config 4 at {world} GPUs: 16 heads do not split over {hsplit} ranks")
+    B //= bsplit
     with torch.device("cuda"):
         m = TESMMIMO_Optimized(d_model=2048, n_heads=16, d_state=64, entanglement_window=16, max_seq_len=L,
                                kernel_backend="b200").eval()
-    x = torch.randn(B, L, 2048, device="cuda").to(torch.bfloat16)
+    if hsplit > 1:
+        import torch.distributed as dist
+        from tesm_b200 import parallel
+        groups = [dist.new_group(list(range(g * hsplit, (g + 1) * hsplit))) for g in range(bsplit)]
+        parallel.enable_mimo_head_parallel(m, parallel.TPGroup(rank % hsplit, hsplit, groups[rank // hsplit]))
+    g = torch.Generator(device="cuda").manual_seed(100 + rank // hsplit)
+    x = torch.randn(B, L, 2048, device="cuda", generator=g).to(torch.bfloat16)
     with torch.no_grad():
         t = _max_over_ranks(_graph_time(lambda i: m(x), reps=5, inner=2), world)
+        if hsplit > 1:  # the kernel-level lines below are single-GPU measurements
+            return [{"workload": "cfg4 MIMO layer", "n_gpus": world, "split": f"batch {bsplit} x heads {hsplit}",
+                     "tokens_per_s": B * bsplit * L / t, "ms": t * 1e3}]
         H, D, R, RM, Dm = 16, 64, 48, 4, 2048
         proj = torch.randn(B * L, 2 * Dm + 3 * H * D + 2 * H * R, device="cuda").to(torch.bfloat16)
         states = torch.empty(B * L, RM, H * D, device="cuda")
@@ -752,7 +766,8 @@ def run_cfg4(args, peaks, rank=0, world=1):
                                          inner=2), world)
     E = B * L * H * D * world  # whole job
     ent_bytes = E * (16 + 4) + B * world * L * H * R * 4
-    return [{"workload": "cfg4 MIMO layer", "n_gpus": world, "tokens_per_s": B * world * L / t, "ms": t * 1e3},
+    return [{"workload": "cfg4 MIMO layer", "n_gpus": world, "split": f"batch {bsplit}",
+             "tokens_per_s": B * world * L / t, "ms": t * 1e3},
             {"kernel": "k_scan (MIMO, 4 ranks)", "n_gpus": world, "ms": ts * 1e3, "GB_s": E * (6 + 16) / ts / 1e9,
              "hbm_frac": E * (6 + 16) / ts / 1e9 / world / peaks["hbm_gbs"], "algorithmic_bytes": E * 22},
             {"kernel": "k_win_ent<16,4> MIMO local entanglement", "n_gpus": world, "ms": te * 1e3, "GB_s": ent_bytes / te / 1e9,

@@ -227,6 +227,9 @@ def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, ac
     Dm, D, R, W = mod.d_model, mod.d_state, mod.ent_rank, mod.entanglement_window
     M = B * L
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(M, Dm))
+    tp = parallel.mixer_tp(mod)
+    if tp is not None:
+        return parallel.siso_prefill_tp(mod, q, (B, L), cross_layer_state, prev_state, cache, act_dtype, tp)
     dev = q.codes.device
     proj = linear_q(mod.in_proj, q, act_dtype)
     cross_bias = None
@@ -280,6 +283,9 @@ def siso_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     act_dtype = act_dtype or u.dtype
     Dm, D, R = mod.d_model, mod.d_state, mod.ent_rank
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(B, Dm))
+    tp = parallel.mixer_tp(mod)
+    if tp is not None:
+        return parallel.siso_decode_tp(mod, q, B, cache, cross_layer_state, act_dtype, tp)
     dev = q.codes.device
     _prepare_cache(cache, dev)
     snapshot_if_due(cache)
@@ -313,6 +319,9 @@ def mimo_prefill(mod, u, cache=None, act_dtype=None, shape=None):
     Dm, D, R, H, RM, W = mod.d_model, mod.d_state, mod.ent_rank, mod.n_heads, mod.mimo_rank, mod.entanglement_window
     C, M = H * D, B * L
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(M, Dm))
+    tp = parallel.mixer_tp(mod)
+    if tp is not None:
+        return parallel.mimo_prefill_tp(mod, q, (B, L), cache, act_dtype, tp)
     dev = q.codes.device
     proj = linear_q(mod.in_proj, q, act_dtype)
     states = torch.empty(M, RM, C, device=dev, dtype=torch.float32)
@@ -351,6 +360,9 @@ def mimo_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     Dm, D, R, H = mod.d_model, mod.d_state, mod.ent_rank, mod.n_heads
     C = H * D
     q = _as_quant(mod, u if isinstance(u, ops.QuantAct) else u.reshape(B, Dm))
+    tp = parallel.mixer_tp(mod)
+    if tp is not None:
+        return parallel.mimo_decode_tp(mod, q, B, cache, cross_layer_state, act_dtype, tp)
     dev = q.codes.device
     _prepare_cache(cache, dev)
     snapshot_if_due(cache)
@@ -603,11 +615,16 @@ class DecodeGraph:
             _prepare_cache(c, self.ids.device)
         # warm-up outside capture (allocates the split-K workspace, packs nothing new)
         snap = [(c["state"].clone(), c["ent_k_cache"].clone(), c["ent_v_cache"].clone(), c["_ctl"].clone(),
-                 c["seq_pos"], c["cache_idx"], c["_ctl_host"]) for c in self.caches.values()]
+                 c["seq_pos"], c["cache_idx"], c["_ctl_host"],
+                 {k: v.clone() for k, v in c["_tp"].items()} if "_tp" in c else None)
+                for c in self.caches.values()]
         self.lm(self.ids, inference_params=self.ip)
         for c, s in zip(self.caches.values(), snap):
             c["state"].copy_(s[0]); c["ent_k_cache"].copy_(s[1]); c["ent_v_cache"].copy_(s[2]); c["_ctl"].copy_(s[3])
             c["seq_pos"], c["cache_idx"], c["_ctl_host"] = s[4], s[5], s[6]
+            if s[7] is not None:  # channel-parallel mixers keep their shard of the cache apart
+                for k, v in s[7].items():
+                    c["_tp"][k].copy_(v)
         torch.cuda.synchronize()
         hosts = [(c["seq_pos"], c["cache_idx"], c["_ctl_host"]) for c in self.caches.values()]
         self.graph = torch.cuda.CUDAGraph()

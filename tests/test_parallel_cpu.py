@@ -65,3 +65,78 @@ def _worker(rank, world, port, out_dir):
 def test_row_parallel_decomposition_exact(tmp_path):
     mp.spawn(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
     assert [open(tmp_path / f"r{r}").read() for r in range(2)] == ["1", "1"]
+
+
+def _mixer_worker(rank, world, port, out_dir):
+    """The channel-parallel SISO layer on the oracle: this rank's in_proj rows (local / gate on a
+    d_model range, value / decay / write on a d_state range, q / k replicated), scan and window
+    on its channels, all-gather, column-parallel combine, row-parallel out_proj -- against the
+    oracle's whole layer (tesm.py:1195-1261), exactly."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rng = np.random.default_rng(9)
+    B, L, Dm, D, R, W = 2, 40, 64, 32, 16, 8
+    eps, thr, es = 1e-5, 0.1, 0.2
+    x = rng.standard_normal((B, L, Dm)).astype(np.float32)
+    P = {"in_proj.weight": (rng.standard_normal((2 * Dm + 3 * D + 2 * R, Dm)) * 0.05).astype(np.float32),
+         "state_proj.weight": (rng.standard_normal((Dm, D)) * 0.05).astype(np.float32),
+         "ent_proj.weight": (rng.standard_normal((Dm, D)) * 0.05).astype(np.float32),
+         "out_proj.weight": (rng.standard_normal((Dm, Dm)) * 0.05).astype(np.float32),
+         "decay_bias": np.full(D, 3.0, np.float32) + rng.standard_normal(D).astype(np.float32) * 0.3,
+         "local_entanglement_bias": (rng.standard_normal(W) * 0.3).astype(np.float32)}
+    cfg = dict(d_model=Dm, d_state=D, ent_rank=R, entanglement_window=W, entanglement_threshold=thr,
+               entanglement_scale=es, bit_eps=eps, rope_base=1e4, state_scan_chunk_size=16)
+    y_ref, _, st_ref = O.siso_forward(P, cfg, x)
+    dm0, dm1 = shard_range(Dm, world, rank, 16)
+    d0, d1 = shard_range(D, world, rank, 8)
+    # in_proj rows of this rank, quantised with the full weight's ternary codes and scale
+    t_in, _, deq_in = O.ternary_weight(P["in_proj.weight"], eps)
+    rows = np.concatenate([np.arange(dm0, dm1), Dm + np.arange(d0, d1), Dm + D + np.arange(d0, d1),
+                           Dm + 2 * D + np.arange(d0, d1), Dm + 3 * D + np.arange(dm0, dm1),
+                           2 * Dm + 3 * D + np.arange(2 * R)])
+    c, s = O.quant_act(x, eps)
+    proj = (O.int_gemm(c, t_in[rows]).astype(np.float64) * (1.0 / s.astype(np.float64))[..., None]
+            * np.float64(deq_in)).astype(np.float32)
+    Dm_r, D_r = dm1 - dm0, d1 - d0
+    local, value, decay, write, gate, q, k = np.split(proj, np.cumsum([Dm_r, D_r, D_r, D_r, Dm_r, R])[:], axis=-1)
+    a = O.sigmoid(decay + P["decay_bias"][d0:d1])
+    u = (O.sigmoid(write) * np.tanh(value).astype(np.float32)).astype(np.float32)
+    st64, _ = O.scan_chunked_f64(a, u)
+    st = st64.astype(np.float32)
+    avg = O.local_ent(O.rope(q), O.rope(k), st, P["local_entanglement_bias"], thr)
+    ent = (st + np.float32(es) * (avg - st)).astype(np.float32)
+
+    def gather(v):
+        t = torch.from_numpy(np.ascontiguousarray(v))
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return torch.cat(parts, -1).numpy()
+
+    tanh_full = gather(np.tanh(ent).astype(np.float32))
+    chg_full = gather((ent - st).astype(np.float32))
+    st_full = gather(st)
+    t_s, _, deq_s = O.ternary_weight(P["state_proj.weight"], eps)
+    t_e, _, deq_e = O.ternary_weight(P["ent_proj.weight"], eps)
+    c1, s1 = O.quant_act(tanh_full, eps)
+    c2, s2 = O.quant_act(chg_full, eps)
+    sp = (O.int_gemm(c1, t_s[dm0:dm1]) * (1.0 / s1.astype(np.float64))[..., None] * np.float64(deq_s)).astype(np.float32)
+    ep = (O.int_gemm(c2, t_e[dm0:dm1]) * (1.0 / s2.astype(np.float64))[..., None] * np.float64(deq_e)).astype(np.float32)
+    y_r = (local + O.sigmoid(gate) * sp + ep).astype(np.float32)
+    # out_proj row-parallel: MAX of row maxima, codes of this rank's columns, SUM of int32 partials
+    amax = torch.from_numpy(np.abs(y_r).max(-1))
+    dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+    cy, sy = O.quant_act(y_r, eps, amax=amax.numpy())
+    t_o, _, deq_o = O.ternary_weight(P["out_proj.weight"], eps)
+    acc = torch.from_numpy(O.int_gemm(cy, t_o[:, dm0:dm1]).astype(np.int64))
+    dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+    out = (acc.numpy().astype(np.float64) * (1.0 / sy.astype(np.float64))[..., None]
+           * np.float64(deq_o)).astype(np.float32)
+    ok = np.array_equal(st_full, st_ref) and np.allclose(out, y_ref, rtol=0, atol=1e-6 * np.abs(y_ref).max())
+    with open(os.path.join(out_dir, f"m{rank}"), "w") as f:
+        f.write("1" if ok else f"0 {np.abs(st_full - st_ref).max()} {np.abs(out - y_ref).max()}")
+    dist.destroy_process_group()
+
+
+def test_channel_parallel_mixer_decomposition(tmp_path):
+    mp.spawn(_mixer_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    assert [open(tmp_path / f"m{r}").read() for r in range(2)] == ["1", "1"]

@@ -1,8 +1,9 @@
 """Worker for the tensor-parallel GPU test: one process per GPU (torch.multiprocessing spawn).
 
-Every rank builds the same seeded model, runs it once on its own GPU without tensor parallelism
-and once with the FeedForward / out_proj split over all ranks (NCCL), and checks that the logits
-of prefill and of three greedy decode steps are bit-identical.  Rank 0 writes the verdict."""
+Every rank builds the same seeded model, runs it once on its own GPU without tensor parallelism,
+once with the FeedForward / out_proj split over all ranks (NCCL) and once with the whole mixer split
+too (SISO channel-parallel, MIMO head-parallel), and checks that the logits of prefill and of three greedy decode
+steps are bit-identical.  Rank 0 writes the verdict."""
 import json
 import os
 import sys
@@ -42,10 +43,19 @@ def run(rank, world, port, out_path, cfg_kw, batch, seqlen):
     # the sharded path really ran: every block holds its FFN and out_proj shards
     used = all("_b200_tp_shards" in b.mlp.__dict__ and "_b200_tp_out" in b.mixer.__dict__
                for b in model.backbone.layers)
-    same = torch.equal(ref, tp) and used
+    # then the whole SISO layer channel-parallel as well (in_proj by segment, channel-sharded
+    # scan / window / decode cache, all-gathers, column-parallel combine, row-parallel out_proj)
+    parallel.enable_mixer_parallel(model)
+    mix = run_model()
+    used_mix = all(("_b200_tp_mix" in b.mixer.__dict__ or "_b200_tp_mimo" in b.mixer.__dict__)
+                   for b in model.backbone.layers)
+    same = torch.equal(ref, tp) and used and torch.equal(ref, mix) and used_mix
     diff = (ref - tp).abs().max().item()
+    diff_mix = (ref - mix).abs().max().item()
     ok = torch.tensor([1 if same else 0], device="cuda")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    used = used and used_mix
+    diff = max(diff, diff_mix)
     if rank == 0:
         with open(out_path, "w") as f:
             json.dump({"bit_identical": bool(ok.item()), "sharded_path_used": used, "max_abs_diff_rank0": diff,
