@@ -103,6 +103,13 @@ int tesm_b200_gemv_int2(const int8_t *codes, int64_t ld_codes, const float *inv_
  * the result does not depend on the arrival order) and writes the output.  The split count is
  * capped so 16 KB + S*M*N*4 <= ws_bytes.  Calls that share one scratch must not overlap on the
  * GPU. */
+/* Dense bf16 GEMM on the tensor cores (tcgen05.mma kind::f16, fp32 accumulators in TMEM, TMA
+ * staged operands): out[m, n] = sum_k a[m, k] * b[n, k], written as out_dtype.  The tied lm_head
+ * of a bf16 model (mixer_seq_simple.py:250-252, :334: F.linear(hidden, embedding.weight)).
+ * Rows of a and b 16-byte aligned (lda, ldb multiples of 8). */
+int tesm_b200_gemm_bf16(const void *a, int64_t lda, const void *b, int64_t ldb, int64_t M, int64_t N, int64_t K,
+                        void *out, int out_dtype, int64_t ldo, tesm_stream_t stream);
+
 /* tesm_b200_decode_step for one SISO layer (H = 1) with the per-token int8 codes of tanh(ent) and
  * ent - s as outputs instead of the values (tesm.py:1385-1396 then BitLinear.quantized_input
  * tesm.py:206-209 of state_proj / ent_proj): codes (B x ldc, ldc >= 2*Dp, Dp = D rounded up to

@@ -34,6 +34,7 @@ SIGNATURES = {
                             c_i64, c_vp, c_i64, c_vp],
     "tesm_b200_gemm_i8": [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int, c_i64,
                           c_vp, c_i64, c_vp, c_i64, c_vp],
+    "tesm_b200_gemm_bf16": [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_vp],
     "tesm_b200_scan_workspace": [c_i64, c_i64, c_i64, c_i64, c_vp],
     "tesm_b200_siso_scan": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,
                             c_vp, c_vp, c_i64, c_vp],

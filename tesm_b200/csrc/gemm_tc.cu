@@ -177,6 +177,27 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// kind::f16 with bf16 operands and an fp32 accumulator (the dense lm_head).
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, int m = BM) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
@@ -256,7 +277,9 @@ __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int
   mt = first_m + (r - nt * gm);
 }
 
-template <int BN, bool DUAL, int MT, bool PAIR>
+// BF: bf16 operands (kind::f16, K counted in bytes, 64 elements per k-block), fp32 accumulators
+// written unscaled (plain tiles only, no split-K).
+template <int BN, bool DUAL, int MT, bool PAIR, bool BF = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmG,
@@ -397,7 +420,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && crank == 0) {  // pair: the leader issues the MMAs for both CTAs
-      constexpr uint32_t idesc = idesc_i8(BN, PAIR ? 2 * BM : BM);
+      constexpr uint32_t idesc = BF ? idesc_bf16(BN, PAIR ? 2 * BM : BM) : idesc_i8(BN, PAIR ? 2 * BM : BM);
       uint32_t it = 0, tile_i = 0;
       bool ok = true;
       for (int u = ustart; u < total && ok; u += ustride, ++tile_i) {
@@ -423,12 +446,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kk = 0; kk < BK / 32; ++kk) {
             // advance 32 bytes along K inside the swizzle atom: +2 in 16-byte units
             if (PAIR) {
-              mma_i8_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
+              if (BF)
+                mma_bf16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
+              else
+                mma_i8_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb0 | kk) != 0);
             } else {
 #pragma unroll
               for (int s = 0; s < MT; ++s)  // second M sub-tile: +16 KB = +1024 in 16-byte units
-                mma_i8(d_tmem + s * BN, adesc + 2 * kk + s * (BM * BK / 16), bdesc + 2 * kk, idesc,
-                       (kb0 | kk) != 0);
+                if (BF)
+                  mma_bf16(d_tmem + s * BN, adesc + 2 * kk + s * (BM * BK / 16), bdesc + 2 * kk, idesc,
+                           (kb0 | kk) != 0);
+                else
+                  mma_i8(d_tmem + s * BN, adesc + 2 * kk + s * (BM * BK / 16), bdesc + 2 * kk, idesc,
+                         (kb0 | kk) != 0);
             }
           }
           if (PAIR)
@@ -644,8 +674,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __threadfence_block();
       }
-      const float xs = row_ok ? p.inv_scale[row] : 0.f;
-      const float wd0 = p.w_deq[0];
+      const float xs = BF ? 1.f : (row_ok ? p.inv_scale[row] : 0.f);
+      const float wd0 = BF ? 1.f : p.w_deq[0];
       if (DUAL && dual_tma) {
         const float s1 = xs * wd0, s2 = (row_ok ? p.inv_scale2[row] : 0.f) * p.w_deq2[0];
         int mtn = 0, ntn = 0;
@@ -823,7 +853,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float wd = p.per_row ? __shfl_sync(0xffffffffu, wdl, j) : wd0;
-          v[j] = (small_acc ? acc_to_f(r[j]) : (float)(int32_t)r[j]) * xs * wd;
+          v[j] = BF ? __uint_as_float(r[j]) : (small_acc ? acc_to_f(r[j]) : (float)(int32_t)r[j]) * xs * wd;
         }
         if (p.out && p.vec_store && n0 + 32 <= p.N && !p.acc_out) {
           stage_store(v, row - lane, n0);
@@ -957,7 +987,7 @@ static int make_map_bf16_32(CUtensorMap *map, const void *ptr, int64_t inner, in
   return TESM_OK;
 }
 
-template <int BN, bool DUAL = false, int MT = 1, bool PAIR = false>
+template <int BN, bool DUAL = false, int MT = 1, bool PAIR = false, bool BF = false>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
   CUtensorMap ma, mb, ml, mg, mo;
   int rc = make_map(&ma, A, p.K, p.M, lda, BM * MT);
@@ -974,7 +1004,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   constexpr int NST = PAIR ? 6 : STAGES;
   const size_t smem = 1024 + (size_t)NST * (MT * BM * BK + (PAIR ? BN / 2 : BN) * BK) +
                       (DUAL ? 1024 + (size_t)EPI_WARPS * (BN / 64) * 3 * 2048 : 1024 + (size_t)EPI_WARPS * 4096);
-  auto kern = k_gemm_i8<BN, DUAL, MT, PAIR>;
+  auto kern = k_gemm_i8<BN, DUAL, MT, PAIR, BF>;
   static bool attr = false;
   static int max_clusters = 0;
   if (!attr) {
@@ -1010,7 +1040,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
   p.splits = 1;
   p.n_full = tiles;
   const int workers = PAIR ? max_clusters : sm_count();
-  if (!DUAL && MT == 1 && p.ws && p.ws_bytes > (int64_t)kCounterInts * 4 && p.num_k_blocks >= 4 &&
+  if (!BF && !DUAL && MT == 1 && p.ws && p.ws_bytes > (int64_t)kCounterInts * 4 && p.num_k_blocks >= 4 &&
       tiles * 2 <= kCounterInts) {
     const int nfull = tiles >= workers ? (tiles / workers) * workers : 0;
     const int rem = tiles - nfull;
@@ -1237,4 +1267,29 @@ extern "C" int tesm_b200_acc_scale(const int32_t *acc, int64_t M, int64_t N, con
   tc::k_splitk_finalize<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
       acc, 1, (int)M, (int)N, inv_scale, w_deq, per_row, 0, out, out_dtype, ldo, nullptr, 0);
   return check_launch("acc_scale");
+}
+
+extern "C" int tesm_b200_gemm_bf16(const void *a, int64_t lda, const void *b, int64_t ldb, int64_t M, int64_t N,
+                                   int64_t K, void *out, int out_dtype, int64_t ldo, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;
+  TESM_REQUIRE(a && b && out, "gemm_bf16: null pointer");
+  TESM_REQUIRE(M > 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31), "gemm_bf16: bad shape");
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "gemm_bf16: out dtype");
+  TESM_REQUIRE(lda >= K && (lda * 2) % 16 == 0 && ((uintptr_t)a & 15) == 0, "gemm_bf16: A rows must be 16-byte aligned");
+  TESM_REQUIRE(ldb >= K && (ldb * 2) % 16 == 0 && ((uintptr_t)b & 15) == 0, "gemm_bf16: B rows must be 16-byte aligned");
+  TESM_REQUIRE(ldo >= N, "gemm_bf16: ldo < N");
+  tc::Params p = {};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)(K * 2);  // bytes: the operand tiles are moved and described as bytes
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.ldo = ldo;
+  const int esz = out_dtype == TESM_BF16 ? 2 : 4;
+  p.vec_store = ((uintptr_t)out % 16 == 0) && ((ldo * esz) % 16 == 0);
+  const int8_t *A = reinterpret_cast<const int8_t *>(a), *B = reinterpret_cast<const int8_t *>(b);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M > 128)  // 256-row tiles on CTA pairs
+    return tc::launch<256, false, 1, true, true>(A, lda * 2, B, ldb * 2, p, st);
+  return tc::launch<256, false, 1, false, true>(A, lda * 2, B, ldb * 2, p, st);
 }

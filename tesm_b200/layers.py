@@ -573,6 +573,26 @@ def mixer_model_forward(model, input_ids, inference_params=None, prev_states=Non
     return hf.view(B, L, -1), [], None, final_states
 
 
+def lm_head(lm, hs):
+    """The dense tied lm_head (mixer_seq_simple.py:250-252, :334).  bf16 models: the tcgen05
+    bf16 GEMM (tesm_b200_gemm_bf16); under tensor parallelism every rank computes its vocabulary
+    range and the logits are all-gathered.  fp32 models: torch's F.linear (cuBLAS)."""
+    w = lm.lm_head.weight
+    shp = hs.shape
+    x = hs.reshape(-1, shp[-1]).to(w.dtype)
+    if w.dtype != torch.bfloat16 or shp[-1] % 8 or w.stride(0) % 8 or w.stride(1) != 1:
+        return F.linear(x, w).view(*shp[:-1], w.shape[0])
+    x = x.contiguous()
+    V = w.shape[0]
+    tp = parallel.get_tp(lm.backbone.layers[0].mlp)
+    if tp is not None and V % tp.world == 0:
+        v0, v1 = parallel.shard_range(V, tp.world, tp.rank)
+        logits = parallel._gather_cols(ops.gemm_bf16(x, w[v0:v1]), tp)
+    else:
+        logits = ops.gemm_bf16(x, w)
+    return logits.view(*shp[:-1], V)
+
+
 def lm_forward(lm, input_ids, labels=None, inference_params=None, prev_states=None, logits_to_keep=0, **kwargs):
     """``TESMLMHeadModel.forward`` (mixer_seq_simple.py:290-345) without vocabulary suppression."""
     if getattr(lm, "vocab_suppression", False):
@@ -580,8 +600,7 @@ def lm_forward(lm, input_ids, labels=None, inference_params=None, prev_states=No
     hidden, maps, stats, final_states = mixer_model_forward(lm.backbone, input_ids, inference_params, prev_states)
     sl = slice(-logits_to_keep, None) if isinstance(logits_to_keep, int) and logits_to_keep > 0 else slice(None)
     hs = hidden[:, sl, :]
-    w = lm.lm_head.weight
-    logits = F.linear(hs.to(w.dtype), w)  # dense tied lm_head: a plain cuBLAS GEMM
+    logits = lm_head(lm, hs)
     loss = None
     if labels is not None:
         shift_logits = logits[..., :-1, :].contiguous()

@@ -181,6 +181,16 @@ def gemm(codes, inv, pw: PackedWeight, M: int, out_dtype: torch.dtype, out=None,
     return (out, accb) if acc else out
 
 
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, out=None):
+    """a (M, K) @ b (N, K)^T on the tensor cores (bf16 in, fp32 accumulate)."""
+    M, K = a.shape
+    N = b.shape[0]
+    out = out if out is not None else torch.empty(M, N, device=a.device, dtype=out_dtype)
+    _lib.call("tesm_b200_gemm_bf16", a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), M, N, K, out.data_ptr(),
+              dtype_code(out.dtype), out.stride(0), _stream())
+    return out
+
+
 def gemm_acc(codes, inv, pw: PackedWeight, M: int, acc: torch.Tensor):
     """int32 accumulators only (no scaled output): the partial product of a row-parallel shard."""
     ws = splitk_workspace(M, pw.N, codes.device)

@@ -218,3 +218,19 @@ def test_gemm_combine_epilogue(ops, dtype, MNK):
     tol = 1e-5 if dtype == "float32" else 8e-3
     err = ((got - ref).abs() / (ref.abs() + 1.0)).max().item()
     assert err <= tol, err
+
+
+@pytest.mark.parametrize("MNK", [(1, 32000, 4096), (32, 32000, 4096), (256, 32000, 4096), (300, 1000, 520),
+                                 (77, 130, 72)], ids=lambda s: "x".join(map(str, s)))
+def test_gemm_bf16_lm_head(ops, MNK):
+    """The tied lm_head GEMM (mixer_seq_simple.py:334) on tcgen05 kind::f16: bf16 operands, fp32
+    accumulation, against an fp64 product of the same bf16 values (fp32 output at 1e-5 of the
+    range; bf16 output within its rounding)."""
+    M, N, K = MNK
+    a = (randn((M, K), 91)).to(torch.bfloat16)
+    b = (randn((N, K), 92) * 0.02).to(torch.bfloat16)
+    ref = a.double() @ b.double().T
+    y32 = ops.gemm_bf16(a.cuda(), b.cuda(), torch.float32)
+    y16 = ops.gemm_bf16(a.cuda(), b.cuda(), torch.bfloat16)
+    assert max_rel(y32.cpu().numpy(), ref.numpy()) <= 1e-5
+    assert max_rel(y16.float().cpu().numpy(), ref.numpy()) <= 8e-3
