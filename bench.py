@@ -347,7 +347,7 @@ def run_gpu(args, rank, world, local_rank):
             a.record()
             r = orig(codes, inv, pw, M, out_dtype, out, acc)
             b.record()
-            rec.append((a, b, 2.0 * M * pw.N * pw.K, M * pw.K + pw.N * pw.K + M * pw.N * 2))
+            rec.append((a, b, 2.0 * M * pw.N * pw.K, M * pw.K + pw.N * pw.K + M * pw.N * 2, pw.N, pw.K))
             return r
 
         orig_sw = ops.gemm_swiglu
@@ -359,7 +359,7 @@ def run_gpu(args, rank, world, local_rank):
             a.record()
             r = orig_sw(q, pw, out_dtype, out)
             b.record()
-            rec.append((a, b, 2.0 * q.M * pw.N * pw.K, q.M * pw.K + pw.N * pw.K + q.M * (pw.N // 2) * 2))
+            rec.append((a, b, 2.0 * q.M * pw.N * pw.K, q.M * pw.K + pw.N * pw.K + q.M * (pw.N // 2) * 2, pw.N, pw.K))
             return r
 
         ops.gemm, ops.gemm_swiglu = timed_gemm, timed_swiglu
@@ -369,9 +369,9 @@ def run_gpu(args, rank, world, local_rank):
         s1.record()
         torch.cuda.synchronize()
         ops.gemm, ops.gemm_swiglu = orig, orig_sw
-        g_ms = sum(a.elapsed_time(b) for a, b, _, _ in rec)
-        g_ops = sum(o for _, _, o, _ in rec)
-        g_bytes = sum(bb for _, _, _, bb in rec)
+        g_ms = sum(a.elapsed_time(b) for a, b, *_ in rec)
+        g_ops = sum(r[2] for r in rec)
+        g_bytes = sum(r[3] for r in rec)
         step_ms = s0.elapsed_time(s1)
 
         # decode (config 5): batch 256, 16-token prompt, greedy steps replayed from a CUDA graph
@@ -450,9 +450,16 @@ def run_gpu(args, rank, world, local_rank):
     traffic = None
     tp = os.path.join(ROOT, "profiles", "gemm_i8_traffic.json")
     if os.path.exists(tp):
+        # ncu DRAM bytes measured per GEMM shape at this M (bench.py --kernel prefill_gemms),
+        # averaged over the step's launches of those shapes (the small cross_layer_q_proj
+        # launches, not captured, count as their algorithmic bytes)
         with open(tp) as f:
             tj = json.load(f)
-        traffic = tj["dram_bytes"] / tj["ops"] * g_ops / len(rec)  # ncu bytes per op, scaled to one launch
+        meas = {(sh["N"], sh["K"]): sh["dram_read"] + sh["dram_write"] for sh in tj["shapes"] if tj["M"] == BATCH * SEQ}
+        tot = 0.0
+        for (_, _, _, bb, n, k) in rec:
+            tot += meas.get((n, k), bb)
+        traffic = tot / len(rec)
     tokens = BATCH * SEQ * world
     try:  # the reference's own torch path on the host cores, 3 timed 32-layer steps
         ref = ReferenceCPU()
@@ -541,6 +548,35 @@ def run_kernel_case(args):
     t = a.elapsed_time(b) / args.steps / 1e3
     print(json.dumps({"kernel": "gemm_i8", "M": M, "N": N, "K": K, "ms": t * 1e3, "TOPS": 2.0 * M * N * K / t / 1e12,
                       "algorithmic_bytes": M * K + N * K + M * N * 2, "ops": 2.0 * M * N * K}), flush=True)
+    return 0
+
+
+PREFILL_GEMMS = [("in_proj", 9088, 4096), ("out_proj", 4096, 4096), ("gate_up", 22016, 4096), ("down_proj", 4096, 11008)]
+
+
+def run_prefill_gemms_case(args):
+    """The four BitLinear GEMMs of one config-5 prefill layer at the benchmark's M = 32 x 4096 rows,
+    one launch each (in_proj, out_proj, the SwiGLU gate/up GEMM, down_proj), for the ncu traffic
+    capture that bench.py's roofline object reads (profiles/gemm_i8_traffic.json)."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    M = BATCH * SEQ
+    for name, N, K in PREFILL_GEMMS:
+        w = torch.randn(N, K, device="cuda") * 0.02
+        pw = ops.pack_weight(w, 1e-5, per_row=name == "gate_up", with_tern=True)
+        del w
+        codes = torch.randint(-127, 128, (M, K), device="cuda", dtype=torch.int8)
+        inv = torch.rand(M, device="cuda") * 0.01
+        q = ops.QuantAct(codes, inv, None, ops.LAYOUT_ROWMAJOR, M)
+        if name == "gate_up":
+            out = ops.gemm_swiglu(q, pw, torch.bfloat16)
+        else:
+            out = ops.gemm(codes, inv, pw, M, torch.bfloat16)
+        torch.cuda.synchronize()
+        print(json.dumps({"gemm": name, "M": M, "N": N, "K": K}), flush=True)
+        del pw, codes, inv, q, out
+        torch.cuda.empty_cache()
     return 0
 
 
@@ -821,7 +857,7 @@ def main():
     ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg4"],
                     help="supplementary measurements of BASELINE configs 2-4 (one JSON line per measurement)")
     ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
-    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine", "skinny"],
+    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine", "skinny", "prefill_gemms"],
                     help="run a small ncu case")
     args = ap.parse_args()
     if args.workload:
@@ -832,6 +868,8 @@ def main():
         return run_combine_case(args)
     if args.kernel == "skinny":
         return run_skinny_case(args)
+    if args.kernel == "prefill_gemms":
+        return run_prefill_gemms_case(args)
     if args.kernel:
         return run_kernel_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
