@@ -10,7 +10,7 @@
  *
  * Each function names the reference interface (WANGLILIN360/tesm, path:line)
  * whose computation it replaces; the Python bindings of the reference call these
- * through ctypes (see INTEGRATION.md).
+ * through ctypes.
  */
 #ifndef TESM_B200_H_
 #define TESM_B200_H_
