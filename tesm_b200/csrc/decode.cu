@@ -27,6 +27,7 @@ struct DecodeParams {
   int *ctl;                   // [seq_pos, cache_idx, done_counter]
   int B, H, D, R, W;
   float thr, es, sqrt_r, rope_base;
+  RopeTab rt;
   void *out_tanh, *out_chg;   // (B, H*D)
   int out_dtype;
   float *new_state;           // (B, H*D) fp32 (cross-layer state for the next layer)
@@ -40,7 +41,7 @@ struct DecodeParams {
   float *inv1, *inv2;
 };
 
-__global__ void k_decode_step(DecodeParams p) {
+__global__ void k_decode_step(const __grid_constant__ DecodeParams p) {
   extern __shared__ float sm[];
   pdl_trigger();
   pdl_wait();
@@ -55,9 +56,9 @@ __global__ void k_decode_step(DecodeParams p) {
   const int64_t row = b;
   const int C = H * D;
   const int tid = threadIdx.x;
-  load_rope_row(q, p.pc, p.pc.c_q + h * R, row, R, pos, p.rope_base, p.cross ? p.cross + row * H * R + h * R : nullptr,
+  load_rope_row(q, p.pc, p.pc.c_q + h * R, row, R, pos, p.rt.v, p.cross ? p.cross + row * H * R + h * R : nullptr,
                 tid, blockDim.x);
-  load_rope_row(k, p.pc, p.pc.c_k + h * R, row, R, pos, p.rope_base, nullptr, tid, blockDim.x);
+  load_rope_row(k, p.pc, p.pc.c_k + h * R, row, R, pos, p.rt.v, nullptr, tid, blockDim.x);
   __syncthreads();
   float *kslot = p.kc + (((int64_t)b * W + idx) * H + h) * R;
   for (int i = tid; i < R; i += blockDim.x) kslot[i] = k[i];
@@ -181,6 +182,8 @@ extern "C" int tesm_b200_decode_step(const void *proj, int dtype, int64_t ldp, i
   p.es = es;
   p.sqrt_r = (float)sqrt((double)R);
   p.rope_base = rope_base;
+  TESM_REQUIRE(R <= 256, "decode_step: ent_rank above 256");
+  p.rt = rope_table((int)R, rope_base);
   p.out_tanh = out_tanh;
   p.out_chg = out_chg;
   p.out_dtype = out_dtype;
@@ -224,6 +227,8 @@ extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int
   p.es = es;
   p.sqrt_r = (float)sqrt((double)R);
   p.rope_base = rope_base;
+  TESM_REQUIRE(R <= 256, "decode_step: ent_rank above 256");
+  p.rt = rope_table((int)R, rope_base);
   p.out_tanh = p.out_chg = nullptr;
   p.out_dtype = act_dtype;
   p.new_state = new_state;

@@ -361,15 +361,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // q (RoPE + cross-layer bias) and k (RoPE) of every row as fp16 hi / lo, zero-padded to RP columns.
-__global__ void k_gtc_prep_qk(ProjCols pc, const float *cross, int64_t M, int L, int R, float base, __half *qh,
+__global__ void k_gtc_prep_qk(ProjCols pc, const float *cross, int64_t M, int L, int R, const __grid_constant__ RopeTab rt, __half *qh,
                               __half *ql, __half *kh, __half *kl) {
   __shared__ float sq[8][RP], sk[8][RP];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + w;
   if (row >= M) return;
   const int t = (int)(row % L);
-  load_rope_row(sq[w], pc, pc.c_q, row, R, t, base, cross ? cross + row * R : nullptr, lane, 32);
-  load_rope_row(sk[w], pc, pc.c_k, row, R, t, base, nullptr, lane, 32);
+  load_rope_row(sq[w], pc, pc.c_q, row, R, t, rt.v, cross ? cross + row * R : nullptr, lane, 32);
+  load_rope_row(sk[w], pc, pc.c_k, row, R, t, rt.v, nullptr, lane, 32);
   __syncwarp();
   for (int c = lane; c < RP; c += 32) {
     const float x = c < R ? sq[w][c] : 0.f, y = c < R ? sk[w][c] : 0.f;
@@ -473,7 +473,7 @@ extern "C" int tesm_b200_siso_global_ent_tc(const void *proj, int dtype, int64_t
          *vtl = reinterpret_cast<__half *>(ws + 4 * lay.qk_bytes + lay.vt_bytes);
   const int64_t M = B * L;
   ProjCols pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
-  gtc::k_gtc_prep_qk<<<(unsigned)ceil_div(M, 8), 256, 0, st>>>(pc, cross, M, (int)L, (int)R, rope_base, qh, ql, kh,
+  gtc::k_gtc_prep_qk<<<(unsigned)ceil_div(M, 8), 256, 0, st>>>(pc, cross, M, (int)L, (int)R, rope_table((int)R, rope_base), qh, ql, kh,
                                                                kl);
   int rc = check_launch("global_ent_tc prep q/k");
   if (rc) return rc;

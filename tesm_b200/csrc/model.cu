@@ -134,7 +134,7 @@ __global__ void k_silu_mul(const void *gu, int dtype, int64_t M, int F, void *ou
 // Prefill -> cache (tesm.py:1235-1253): last min(L, W) positions of rope(k) and of the
 // (rank-0) states; L >= W fills slots 0..W-1, L < W fills slots W-L..W-1; cache_idx = 0.
 __global__ void k_cache_fill(ProjCols pc, const float *states, int RM, int B, int L, int H, int D, int R, int W,
-                             float rope_base, const double *final_f64, double *state, float *kc, float *vc,
+                             const __grid_constant__ RopeTab rt, const double *final_f64, double *state, float *kc, float *vc,
                              int *ctl) {
   const int b = blockIdx.y, n = min(L, W), i = blockIdx.x;
   if (i >= n) return;
@@ -143,7 +143,7 @@ __global__ void k_cache_fill(ProjCols pc, const float *states, int RM, int B, in
   const int64_t row = (int64_t)b * L + t;
   const int C = H * D;
   for (int h = 0; h < H; ++h)
-    load_rope_row(kc + (((int64_t)b * W + slot) * H + h) * R, pc, pc.c_k + h * R, row, R, t, rope_base, nullptr,
+    load_rope_row(kc + (((int64_t)b * W + slot) * H + h) * R, pc, pc.c_k + h * R, row, R, t, rt.v, nullptr,
                   threadIdx.x, blockDim.x);
   for (int c = threadIdx.x; c < C; c += blockDim.x) vc[((int64_t)b * W + slot) * C + c] = states[row * RM * C + c];
   if (i == 0) {
@@ -222,6 +222,6 @@ extern "C" int tesm_b200_cache_fill(const void *proj, int dtype, int64_t ldp, co
   ProjCols pc = make_cols(proj, dtype, ldp, (int)Dm, (int)(H * D), (int)(H * R));
   dim3 grid((unsigned)(L < W ? L : W), (unsigned)B);
   k_cache_fill<<<grid, 128, 0, (cudaStream_t)stream>>>(pc, states, (int)RM, (int)B, (int)L, (int)H, (int)D, (int)R,
-                                                       (int)W, rope_base, final_f64, state, k_cache, v_cache, ctl);
+                                                       (int)W, rope_table((int)R, rope_base), final_f64, state, k_cache, v_cache, ctl);
   return check_launch("cache_fill");
 }

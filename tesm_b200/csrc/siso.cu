@@ -42,6 +42,7 @@ struct GlobalEntParams {
   int rope_heads;       // RoPE applied per head on R / rope_heads columns
   int dslice;           // channels per CTA (blockIdx.z)
   float thr, es, sqrt_r, rope_base;
+  RopeTab rt;
   void *out_tanh, *out_chg;
   int out_dtype;
   // MIMO rank accumulation (tesm_mimo.py:1007-1017 with the global rung :669-687, no lerp)
@@ -51,7 +52,7 @@ struct GlobalEntParams {
 };
 
 // One CTA per (query tile of 32 rows, batch, channel slice); loops over causal key tiles of 32.
-__global__ void __launch_bounds__(256) k_siso_global_ent(GlobalEntParams p) {
+__global__ void __launch_bounds__(256) k_siso_global_ent(const __grid_constant__ GlobalEntParams p) {
   extern __shared__ float sm[];
   constexpr int TQ = 32, TK = 32;
   const int R = p.R, RP = R + 1, DS = p.dslice;
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(256) k_siso_global_ent(GlobalEntParams p) {
   for (int r = warp; r < nq; r += nwarp) {
     const int64_t row = row0 + q0 + r;
     for (int h = 0; h < p.rope_heads; ++h)
-      load_rope_row(qs + r * RP + h * Rh, p.pc, p.pc.c_q + h * Rh, row, Rh, q0 + r, p.rope_base,
+      load_rope_row(qs + r * RP + h * Rh, p.pc, p.pc.c_q + h * Rh, row, Rh, q0 + r, p.rt.v,
                     p.cross ? p.cross + row * R + h * Rh : nullptr, lane, 32);
   }
   for (int i = threadIdx.x; i < TQ * DS; i += blockDim.x) acc[i] = 0.f;
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(256) k_siso_global_ent(GlobalEntParams p) {
     __syncthreads();
     for (int r = warp; r < nk; r += nwarp)
       for (int h = 0; h < p.rope_heads; ++h)
-        load_rope_row(ks + r * RP + h * Rh, p.pc, p.pc.c_k + h * Rh, row0 + k0 + r, Rh, k0 + r, p.rope_base,
+        load_rope_row(ks + r * RP + h * Rh, p.pc, p.pc.c_k + h * Rh, row0 + k0 + r, Rh, k0 + r, p.rt.v,
                       nullptr, lane, 32);
     for (int i = threadIdx.x; i < nk * DL; i += blockDim.x) {
       const int r = i / DL, d = i - r * DL;
@@ -149,6 +150,8 @@ static int launch_global(GlobalEntParams &p, cudaStream_t st) {
   }
   if (smem > 200 * 1024) return fail(TESM_EUNSUPPORTED, "global_ent: ent_rank too large");
   dim3 grid((unsigned)ceil_div(p.L, 32), (unsigned)p.B, (unsigned)ceil_div(p.D, p.dslice));
+  TESM_REQUIRE(p.R / p.rope_heads <= 256, "global_ent: ent_rank per head above 256");
+  p.rt = rope_table(p.R / p.rope_heads, p.rope_base);
   k_siso_global_ent<<<grid, 256, smem, st>>>(p);
   return check_launch("global_ent");
 }

@@ -49,6 +49,7 @@ struct WinEntParams {
   const float *mimo_o; // MIMO (H, RM, D)
   int B, L, H, D, R, quirk, async16, ntiles_b;
   float thr, es, sqrt_r, rope_base;
+  RopeTab rt;
   void *out_tanh, *out_chg;  // out[(row0 + t) * out_ld + h * D + ch]
   int out_dtype;
   int64_t out_ld;
@@ -272,7 +273,7 @@ __device__ __forceinline__ void win_store2(void *out, int dtype, int64_t o, floa
 // NT threads; NST = 2: one CTA per SM streams the next unit in while computing this one;
 // NST = 1: two CTAs per SM, each loading its next unit after finishing the current one.
 template <int W, int RM, int ES, int MODE, int NT, int NST>
-__global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(WinEntParams p) {
+__global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(const __grid_constant__ WinEntParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const WinGeom g = win_geom(W, p.R, p.D, RM, ES, MODE, NST);
   const WinSmem s = win_carve(smem_raw, g);
@@ -282,7 +283,7 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(WinEntParams p
   const int R4 = (R + 3) & ~3;
   const WinMap mq = win_map<NT>(R * ES / 16), ms = win_map<NT>(RM * (D / 4)), mh = win_map<NT>(half);
 
-  for (int i = tid; i < half; i += NT) s.invf[i] = rope_inv_freq(i, R, p.rope_base);
+  for (int i = tid; i < half; i += NT) s.invf[i] = p.rt.v[i];
   if (R4 > R)  // pad columns read by the 4-wide dot products stay zero
     for (int i = tid; i < (kWinT + g.nk) * (R4 - R); i += NT) {
       const int row = i / (R4 - R), j = i - row * (R4 - R);
@@ -551,6 +552,8 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(WinEntParams p
 template <int W, int RM, int ES, int MODE, int NT, int NST>
 static int win_launch_v(WinEntParams &p, const WinGeom &g, int ctas_per_sm, cudaStream_t st, const char *what) {
   p.async16 = win_async_ok(p, ES, NT);
+  if (p.R > 256) return fail(TESM_EUNSUPPORTED, std::string(what) + ": ent_rank above 256");
+  p.rt = rope_table(p.R, p.rope_base);
   const size_t smem = win_smem_bytes(g);
   static bool attr = false;
   if (!attr) {
