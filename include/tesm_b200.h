@@ -115,13 +115,20 @@ int tesm_b200_gemm_bf16(const void *a, int64_t lda, const void *b, int64_t ldb, 
  * tesm.py:206-209 of state_proj / ent_proj): codes (B x ldc, ldc >= 2*Dp, Dp = D rounded up to
  * 128) hold the tanh codes in [0, D) and the change codes in [Dp, Dp + D), zero padded, ready
  * for tesm_b200_gemm_i8_combine; inv1 / inv2 receive 1/s per token.  The values are rounded to
- * act_dtype before quantisation, like the unfused path. */
+ * act_dtype before quantisation, like the unfused path.
+ * With xstate set (B x D fp32: the previous layer's new state), the step also computes the
+ * cross-layer query bias itself, as cross_layer_q_proj(xstate) (tesm.py:1302-1305 with BitLinear
+ * tesm.py:287-290): per-row int8 codes of the state (eps xq_eps), exact dot products with the
+ * int8 ternary rows xq_tern (ent_rank rows, pitch xq_ld >= D rounded up to 16, 16-byte aligned)
+ * and (float)acc * (1/s) * xq_deq[0] -- the values the separate quantiser + BitLinear GEMM give;
+ * `cross` is then ignored.  xstate = NULL: `cross` (or no bias) as before. */
 int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int64_t ldp, int64_t B, int64_t Dm, int64_t D,
                                      int64_t R, int64_t W, const float *decay_bias, const float *bias,
                                      const float *cross, double *state, float *k_cache, float *v_cache, int *ctl,
                                      float thr, float es, float rope_base, int act_dtype, float eps1, float eps2,
                                      int8_t *codes, int64_t ldc, int64_t Dp, float *inv1, float *inv2,
-                                     float *new_state, tesm_stream_t stream);
+                                     float *new_state, const float *xstate, const int8_t *xq_tern,
+                                     int64_t xq_ld, const float *xq_deq, float xq_eps, tesm_stream_t stream);
 
 /* Tensor-parallel pieces of the row-parallel BitLinear (down_proj / out_proj split along K over
  * ranks; no counterpart in the reference, which runs on one device):

@@ -47,7 +47,8 @@ SIGNATURES = {
                                   c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp],
     "tesm_b200_siso_decode_step_codes": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
                                          c_vp, c_vp, c_vp, c_vp, c_float, c_float, c_float, c_int, c_float,
-                                         c_float, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp],
+                                         c_float, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp,
+                                         c_float, c_vp],
     "tesm_b200_row_absmax": [c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp],
     "tesm_b200_quant_act_amax": [c_vp, c_int, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_i64, c_int, c_vp, c_vp,
                                  c_vp],

@@ -39,7 +39,50 @@ struct DecodeParams {
   int Dp, act_dtype;
   float eps1, eps2;
   float *inv1, *inv2;
+  // fused cross-layer query bias (SISO, one block per row): cross = BitLinear(xstate[row]) with
+  // the fp32 input quantised per row and the int8 ternary weight xq_t (R rows, pitch xq_ld);
+  // replaces `cross` when xstate is set
+  const float *xstate;  // (B, D) fp32: the previous layer's new state
+  const int8_t *xq_t;
+  int64_t xq_ld;
+  const float *xq_deq;
+  float xq_eps;
 };
+
+// Cross-layer query bias of one row, as BitLinear (tesm.py:206-215, 287-290) on the fp32
+// state row: per-row int8 codes (the activation quantiser of quant.cu), exact int32 dot products
+// with the ternary rows (4 threads per output, dp4a over 16-byte groups), dequantised as
+// (float)acc * (1/s) * deq like the BitLinear GEMM / GEMV epilogues.  blockDim >= D.
+__device__ void cross_bias_row(const DecodeParams &p, int64_t row, int8_t *xc, float *out, float *red) {
+  const int tid = threadIdx.x, D = p.D, Dk = (D + 15) & ~15;
+  const float x = tid < D ? p.xstate[row * D + tid] : 0.f;
+  const float amax = block_reduce(fabsf(x), red, [](float a, float b) { return fmaxf(a, b); }, 0.f);
+  const float s = act_scale(amax, p.xq_eps, TESM_F32);
+  if (tid < Dk) xc[tid] = tid < D ? (int8_t)act_code(x, s, TESM_F32) : 0;
+  for (int i = tid + blockDim.x; i < Dk; i += blockDim.x) xc[i] = 0;
+  __syncthreads();
+  const float inv = __frcp_rn(s), wd = p.xq_deq[0];
+  const int groups = Dk / 16;
+  for (int o0 = 0; o0 < p.R; o0 += blockDim.x / 4) {
+    const int o = o0 + tid / 4, part = tid & 3;
+    int acc = 0;
+    if (o < p.R) {
+      const int8_t *wr = p.xq_t + (int64_t)o * p.xq_ld;
+      for (int g = part; g < groups; g += 4) {
+        const int4 w4 = *reinterpret_cast<const int4 *>(wr + g * 16);
+        const int4 c4 = *reinterpret_cast<const int4 *>(xc + g * 16);
+        acc = __dp4a(w4.x, c4.x, acc);
+        acc = __dp4a(w4.y, c4.y, acc);
+        acc = __dp4a(w4.z, c4.z, acc);
+        acc = __dp4a(w4.w, c4.w, acc);
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (o < p.R && part == 0) out[o] = (float)acc * inv * wd;
+  }
+  __syncthreads();
+}
 
 __global__ void k_decode_step(const __grid_constant__ DecodeParams p) {
   extern __shared__ float sm[];
@@ -50,14 +93,20 @@ __global__ void k_decode_step(const __grid_constant__ DecodeParams p) {
   float *k = q + R;          // R
   float *tw = k + R;         // W weights (ternary / norm)
   int *slot = reinterpret_cast<int *>(tw + W);  // W
+  float *xb = reinterpret_cast<float *>(slot + W);          // R: fused cross-layer bias
+  int8_t *xc = reinterpret_cast<int8_t *>(xb + R);          // D rounded up to 16: its input codes
   const int h = blockIdx.x, b = blockIdx.y;
   const int pos = p.ctl[0], idx = p.ctl[1];
   const int valid = min(pos + 1, W);
   const int64_t row = b;
   const int C = H * D;
   const int tid = threadIdx.x;
-  load_rope_row(q, p.pc, p.pc.c_q + h * R, row, R, pos, p.rt.v, p.cross ? p.cross + row * H * R + h * R : nullptr,
-                tid, blockDim.x);
+  if (p.xstate) {
+    __shared__ float xred[32];
+    cross_bias_row(p, row, xc, xb, xred);
+  }
+  load_rope_row(q, p.pc, p.pc.c_q + h * R, row, R, pos, p.rt.v,
+                p.xstate ? xb : (p.cross ? p.cross + row * H * R + h * R : nullptr), tid, blockDim.x);
   load_rope_row(k, p.pc, p.pc.c_k + h * R, row, R, pos, p.rt.v, nullptr, tid, blockDim.x);
   __syncthreads();
   float *kslot = p.kc + (((int64_t)b * W + idx) * H + h) * R;
@@ -164,7 +213,7 @@ extern "C" int tesm_b200_decode_step(const void *proj, int dtype, int64_t ldp, i
   TESM_REQUIRE(B > 0 && H > 0 && D > 0 && D <= 1024 && R > 0 && R % 2 == 0 && W > 0 && W <= 32,
                "decode_step: bad shape (D <= 1024, W <= 32, even R)");
   if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "decode_step: dtype");
-  DecodeParams p;
+  DecodeParams p = {};
   p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)(H * D), (int)(H * R));
   p.decay_bias = decay_bias;
   p.bias = bias;
@@ -201,7 +250,9 @@ extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int
                                                 float *k_cache, float *v_cache, int *ctl, float thr, float es,
                                                 float rope_base, int act_dtype, float eps1, float eps2,
                                                 int8_t *codes, int64_t ldc, int64_t Dp, float *inv1, float *inv2,
-                                                float *new_state, tesm_stream_t stream) {
+                                                float *new_state, const float *xstate, const int8_t *xq_tern,
+                                                int64_t xq_ld, const float *xq_deq, float xq_eps,
+                                                tesm_stream_t stream) {
   TESM_REQUIRE(proj && decay_bias && bias && state && k_cache && v_cache && ctl && codes && inv1 && inv2,
                "decode_step_codes: null pointer");
   TESM_REQUIRE(B > 0 && D > 0 && D <= 1024 && R > 0 && R % 2 == 0 && W > 0 && W <= 32,
@@ -209,7 +260,11 @@ extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int
   TESM_REQUIRE(Dp >= D && Dp % 128 == 0 && ldc >= 2 * Dp, "decode_step_codes: Dp must be D rounded up to 128");
   if (dtype != TESM_F32 && dtype != TESM_BF16) return fail(TESM_EDTYPE, "decode_step_codes: dtype");
   if (act_dtype != TESM_F32 && act_dtype != TESM_BF16) return fail(TESM_EDTYPE, "decode_step_codes: act dtype");
-  DecodeParams p;
+  if (xstate)
+    TESM_REQUIRE(xq_tern && xq_deq && xq_ld >= round_up(D, 16) && xq_ld % 16 == 0 && ((uintptr_t)xq_tern & 15) == 0,
+                 "decode_step_codes: cross-layer weight must be int8 rows of >= D rounded up to 16 bytes, "
+                 "16-byte aligned");
+  DecodeParams p = {};
   p.pc = make_cols(proj, dtype, ldp, (int)Dm, (int)D, (int)R);
   p.decay_bias = decay_bias;
   p.bias = bias;
@@ -240,8 +295,13 @@ extern "C" int tesm_b200_siso_decode_step_codes(const void *proj, int dtype, int
   p.eps2 = eps2;
   p.inv1 = inv1;
   p.inv2 = inv2;
+  p.xstate = xstate;
+  p.xq_t = xq_tern;
+  p.xq_ld = xq_ld;
+  p.xq_deq = xq_deq;
+  p.xq_eps = xq_eps;
   const int threads = (int)round_up(D < 32 ? 32 : D, 32);
-  const size_t smem = sizeof(float) * (2 * R + W) + sizeof(int) * W;
+  const size_t smem = sizeof(float) * (3 * R + W) + sizeof(int) * W + (size_t)round_up(D, 16);
   return launch_k("decode_step_codes", k_decode_step, dim3(1, (unsigned)B), dim3(threads), smem,
                   (cudaStream_t)stream, p);
 }

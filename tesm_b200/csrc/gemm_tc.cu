@@ -12,6 +12,9 @@
 //                reads TMEM lanes 32*(w%4).. and half of the tile's columns.
 // Every mbarrier wait is bounded; a wait that gives up sets the sticky device status
 // (TESM_ETIMEOUT) and the CTA drains and exits instead of hanging.
+#include <algorithm>
+#include <vector>
+#include <cstdio>
 #include "rowio.cuh"
 
 #include <cuda.h>
@@ -63,6 +66,8 @@ struct Params {
   // until every split has counted, adds the other slices to its own chunks (exact integers)
   // and runs the epilogue on them; a second count resets the counter to zero for the next call.
   int splits, n_full;
+  unsigned long long *trace;  // optional per-CTA globaltimer stamps (32 per CTA; TESM_GEMM_TRACE)
+  int pdl_late;  // 1: signal dependents when the epilogue starts the CTA's last unit (else at entry)
   int32_t *ws;      // caller scratch: kCounterInts counters (zero between calls), then the slices
   int64_t ws_bytes;
   int32_t *cnt, *part;
@@ -70,6 +75,15 @@ struct Params {
 };
 
 constexpr int kCounterInts = 4096;  // 16 KB of tile counters at the start of the split-K scratch
+
+// diagnostic phase stamps (globaltimer) of one launch, written only when p.trace is set
+__device__ __forceinline__ void trace_at(const Params &p, int slot) {
+  if (p.trace) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    p.trace[blockIdx.x * 32 + slot] = t;
+  }
+}
 
 // work unit u -> (tile, split, number of splits of that tile)
 __device__ __forceinline__ void unit_info(const Params &p, int u, int &t, int &sp, int &ns) {
@@ -87,6 +101,27 @@ __device__ __forceinline__ void unit_info(const Params &p, int u, int &t, int &s
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// release / acquire at CTA and GPU scope for the split-K meeting
+__device__ __forceinline__ void red_release_cta(int *a, int v) {
+  asm volatile("red.release.cta.shared::cta.add.s32 [%0], %1;\n" ::"r"(smem_u32(a)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta(const int *a) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];\n" : "=r"(v) : "r"(smem_u32(a)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_cta(int *a, int v) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(a)), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_gpu(int *a, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;\n" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int *a) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(a) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
@@ -321,6 +356,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   // split-K meeting words of the epilogue warps (see the split-K branch of the epilogue)
   __shared__ int s_last, s_arrive, s_decided;
+  if (threadIdx.x == 0) trace_at(p, 0);
   if (threadIdx.x == 0) {
     s_last = s_arrive = s_decided = 0;
     for (int i = 0; i < NST; ++i) {
@@ -359,8 +395,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   // programmatic dependent launch: the set-up above overlapped the previous kernel; only the
   // producer's first weight-tile requests (constant data) go out before its completion
-  if (threadIdx.x == 0) pdl_trigger();
+  if (threadIdx.x == 0 && !p.pdl_late) pdl_trigger();
   if (warp != 0) pdl_wait();
+  if (threadIdx.x == 0) trace_at(p, 1);
 
   const int total = p.n_full + (p.num_m_tiles * p.num_n_tiles - p.n_full) * p.splits;
   const int nk_all = p.num_k_blocks;
@@ -407,7 +444,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (crank == 0 && !b_done) mbar_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             tma_load_2d_pair(sA + stage * A_BYTES, &tmA, fb, kb * BK, (mt * 2 + (int)crank) * BM);
-            if (!b_done) tma_load_2d_pair(sB + stage * B_BYTES, &tmB, fb, kb * BK, nt * BN + (int)crank * (BN / 2));
+            if (!b_done)
+              tma_load_2d_pair(sB + stage * B_BYTES, &tmB, fb, kb * BK, nt * BN + (int)crank * (BN / 2));
           } else {
             if (!b_done) mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
             tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM * MT);
@@ -439,6 +477,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
+          if (it == 0) trace_at(p, 2);
           fence_after();
           const uint64_t adesc = smem_desc_sw128(sA + stage * A_BYTES);
           const uint64_t bdesc = smem_desc_sw128(sB + stage * B_BYTES);
@@ -471,6 +510,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mma_commit_pair(&tfull[buf]);
           else
             mma_commit(&tfull[buf]);
+          if (tile_i < 3) trace_at(p, 3 + tile_i);
         }
       }
     }
@@ -499,6 +539,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // byte offset of 16-byte unit j of row r in a 32 x 64 B tile with the 64-byte swizzle
     auto sw64 = [](int r, int j) -> uint32_t { return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); };
     bool epi_ok = true;
+    int nsplit = 0;  // split units this CTA's epilogue has handled (the same count in every warp)
     uint32_t in_phase = 0;  // bit cc: parity of chunk cc's next barrier phase
     // release of a TMEM buffer: to this CTA's barrier, or the pair leader's
     auto release = [&](uint32_t b) {
@@ -508,8 +549,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       else
         mbar_arrive(&tempty[b]);
     };
-    int nsplit = 0;  // split units this CTA's epilogue has handled (the same count in every warp)
     for (int u = ustart; u < total; u += ustride, ++tile_i) {
+      if (warp == 2 && lane == 0 && tile_i > 0 && tile_i < 4) trace_at(p, 9 + tile_i - 1);
       int mt, nt, t_u, sp_u, ns_u;
       unit_info(p, u, t_u, sp_u, ns_u);
       tile_coords(p, t_u, mt, nt);
@@ -518,11 +559,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int cc = 0; cc < DCH; ++cc) issue_in(mt, nt, cc);
       }
-      if (!mbar_wait(&tfull[buf], use & 1)) break;
-      fence_after();
       const int sub = MT == 2 ? half : 0;  // skinny tiles: each warp half owns one M sub-tile
       const int row = (PAIR ? mt * 2 + (int)crank : mt * MT + sub) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
+      // dequantisation factors: loaded before the accumulator wait, so that their latency hides
+      // behind this tile's MMAs (w4[i]: per-row factor of weight row n0 + lane of this warp's
+      // i-th chunk; the SwiGLU tile uses gate rows in w4[0..1] and up rows in w4[2..3])
+      const float xs = BF ? 1.f : (row_ok ? __ldg(p.inv_scale + row) : 0.f);
+      const float wd0 = BF ? 1.f : __ldg(p.w_deq);
+      float w4[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!BF && !DUAL && p.per_row) {
+        if (BN == 256 && MT == 1 && p.swiglu) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ng = nt * BN + (half * 2 + i) * 32 + lane;
+            if (ng < p.N) w4[i] = __ldg(p.w_deq + ng);
+            if (ng + 128 < p.N) w4[2 + i] = __ldg(p.w_deq + ng + 128);
+          }
+        } else {
+          const int c0 = MT == 2 ? 0 : half * (BN / 64);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int n = nt * BN + (c0 + i) * 32 + lane;
+            if (i < (MT == 2 ? BN / 32 : BN / 64) && n < p.N) w4[i] = __ldg(p.w_deq + n);
+          }
+        }
+      }
+      if (!mbar_wait(&tfull[buf], use & 1)) break;
+      if (warp == 2 && lane == 0 && tile_i < 3) trace_at(p, 6 + tile_i);
+      if (p.pdl_late && warp == 2 && lane == 0 && u + ustride >= total) pdl_trigger();
+      fence_after();
       // split-K: the other splits' partial sums of this tile are added to the accumulators read
       // from TMEM (only in the split that arrives last, see Params)
       bool fix = false;
@@ -534,18 +600,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         return reinterpret_cast<int4 *>(p.part) +
                (((int64_t)slice * p.part_rb + rblk) * p.part_cb + (n0 >> 5)) * 256;
       };
+      // the other splits' slices, two per round trip to L2
       auto acc_fix = [&](uint32_t (&r)[32], int n0) {
         if (!fix || n0 >= p.N) return;
-        for (int s2 = 0; s2 < ns_u; ++s2) {
-          if (s2 == sp_u) continue;
-          const int4 *blk = part_blk(s2, n0);
+        for (int k = 0; k < ns_u - 1; k += 2) {
+          const int s_a = k < sp_u ? k : k + 1;
+          const int s_b = k + 1 < sp_u ? k + 1 : k + 2;
+          const bool two = k + 1 < ns_u - 1;
+          const int4 *ba = part_blk(s_a, n0);
+          const int4 *bb = part_blk(two ? s_b : s_a, n0);
+          int4 va[8], vb[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) va[j] = __ldcg(ba + j * 32 + lane);
+          if (two) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vb[j] = __ldcg(bb + j * 32 + lane);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vb[j] = make_int4(0, 0, 0, 0);
+          }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int4 v4 = __ldcg(blk + j * 32 + lane);
-            r[4 * j] += (uint32_t)v4.x;
-            r[4 * j + 1] += (uint32_t)v4.y;
-            r[4 * j + 2] += (uint32_t)v4.z;
-            r[4 * j + 3] += (uint32_t)v4.w;
+            r[4 * j] += (uint32_t)va[j].x + (uint32_t)vb[j].x;
+            r[4 * j + 1] += (uint32_t)va[j].y + (uint32_t)vb[j].y;
+            r[4 * j + 2] += (uint32_t)va[j].z + (uint32_t)vb[j].z;
+            r[4 * j + 3] += (uint32_t)va[j].w + (uint32_t)vb[j].w;
           }
         }
       };
@@ -611,19 +690,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __stcg(blk + j * 32 + lane, make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2],
                                                   (int)r[4 * j + 3]));
         }
-        // the epilogue warps meet through shared-memory words with bounded waits (no named
-        // barrier, so a warp that gave up on an earlier wait cannot leave the others blocked)
+        // Meeting.  Each epilogue warp publishes its partial stores to the CTA (release at CTA
+        // scope on a shared word); warp 0 of the epilogue acquires all eight, counts the CTA in
+        // the tile's counter with one release at GPU scope (cumulative over the stores it has
+        // acquired), waits (bounded) until every split has counted, and hands the outcome to the
+        // other warps through a second shared word.  Shared-memory words with bounded waits
+        // instead of a named barrier: a warp that gave up on an earlier wait cannot leave the
+        // others blocked.
         __syncwarp();
+        if (warp == 2 && lane == 0) trace_at(p, 13);
         ++nsplit;
-        if (lane == 0) {
-          __threadfence();  // this warp's partial stores before the count (cumulative)
-          atomicAdd(&s_arrive, 1);
-        }
         int ok = 0;
+        if (lane == 0) red_release_cta(&s_arrive, 1);
         if (ew == 0 && lane == 0) {
           const long long t0 = clock64();
           bool met = true;
-          while (*(volatile int *)&s_arrive < EPI_WARPS * nsplit) {
+          while (ld_acquire_cta(&s_arrive) < EPI_WARPS * nsplit) {
             if (clock64() - t0 > kWaitCycles) {
               flag_timeout();
               met = false;
@@ -631,14 +713,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
           if (met) {
-            __threadfence();
-            int *c = p.cnt + (int64_t)t_u * 2 + (int)crank;
-            atomicAdd(c, 1);
+            int *cn = p.cnt + (int64_t)t_u * 2 + (int)crank;
+            red_release_gpu(cn, 1);
             const long long t1 = clock64();
-            while (true) {  // every split of the tile has stored its partials
-              int v;
-              asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(c) : "memory");
-              if (v >= ns_u) break;
+            while (ld_acquire_gpu(cn) < ns_u) {  // every split of the tile has stored its partials
               if (clock64() - t1 > kWaitCycles) {
                 flag_timeout();
                 met = false;
@@ -649,22 +727,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               ok = 1;
               // second count: the split that completes it resets the counter for the next call
               // (every split has passed the wait above by then)
-              if (atomicAdd(c, 1) == 2 * ns_u - 1) *c = 0;
+              if (atomicAdd(cn, 1) == 2 * ns_u - 1) *cn = 0;
             }
           }
           s_last = ok;
-          __threadfence_block();
-          *(volatile int *)&s_decided = nsplit;
+          st_release_cta(&s_decided, nsplit);
         } else if (lane == 0) {
           const long long t0 = clock64();
-          while (*(volatile int *)&s_decided < nsplit) {
+          int d;
+          while ((d = ld_acquire_cta(&s_decided)) < nsplit) {
             if (clock64() - t0 > kWaitCycles) {
               flag_timeout();
               break;
             }
           }
-          ok = *(volatile int *)&s_decided >= nsplit ? *(volatile int *)&s_last : 0;
+          ok = d >= nsplit ? *(volatile int *)&s_last : 0;
         }
+        if (warp == 2 && lane == 0) trace_at(p, 14);
         fix = __shfl_sync(0xffffffffu, ok, 0) != 0;
         if (!fix) {
           fence_before();
@@ -674,8 +753,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __threadfence_block();
       }
-      const float xs = BF ? 1.f : (row_ok ? p.inv_scale[row] : 0.f);
-      const float wd0 = BF ? 1.f : p.w_deq[0];
       if (DUAL && dual_tma) {
         const float s1 = xs * wd0, s2 = (row_ok ? p.inv_scale2[row] : 0.f) * p.w_deq2[0];
         int mtn = 0, ntn = 0;
@@ -800,20 +877,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t rg[32], ru[32];
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
           if (fix && c % ns_u != sp_u) continue;  // split-K: another split finalises this chunk
+          if (warp == 2 && lane == 0) trace_at(p, 15);
           tmem_ld32(tbase + c * 32, rg);
           tmem_ld32(tbase + 128 + c * 32, ru);
+          if (warp == 2 && lane == 0) trace_at(p, 16);
           const int ng = nt * BN + c * 32;    // weight row of the first gate column
           const int no = nt * 128 + c * 32;   // output column
           if (ng >= p.N) continue;
           acc_fix(rg, ng);
           acc_fix(ru, ng + 128);
+          if (warp == 2 && lane == 0) trace_at(p, 17);
           float v[32];
           // per-row dequantisation factors of the chunk's 32 gate and 32 up rows: one coalesced
           // load each, handed to the lanes by shuffles
           // (the conversion and transcendental unit is the epilogue's bottleneck: accumulators
           // are converted with integer adds when |acc| < 2^22, and silu takes one exp2 and one
           // reciprocal, relative error a few ulp)
-          const float dg = p.w_deq[ng + lane], du = p.w_deq[ng + 128 + lane];
+          const float dg = (c & 1) ? w4[1] : w4[0], du = (c & 1) ? w4[3] : w4[2];
           const bool small_acc = p.K < 32768;  // |acc| <= 128 K < 2^22
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -823,9 +903,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const float u = au * xs * __shfl_sync(0xffffffffu, du, j);
             v[j] = __fdividef(g, 1.f + __expf(-g)) * u;
           }
+          if (warp == 2 && lane == 0) trace_at(p, 18);
           const int nout = p.N / 2;
           if (p.vec_store && no + 32 <= nout) {
             stage_store(v, row - lane, no);
+            if (warp == 2 && lane == 0) trace_at(p, 19);
             continue;
           }
           if (!row_ok) continue;
@@ -843,20 +925,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (fix && c % ns_u != sp_u) continue;  // split-K: another split finalises this chunk
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + sub * BN + c * 32;
+        if (warp == 2 && lane == 0) trace_at(p, 15);
         tmem_ld32(taddr, r);
+        if (warp == 2 && lane == 0) trace_at(p, 16);
         const int n0 = nt * BN + c * 32;
         if (n0 >= p.N) continue;
         acc_fix(r, n0);
+        if (warp == 2 && lane == 0) trace_at(p, 17);
         float v[32];
-        const float wdl = p.per_row ? (n0 + lane < p.N ? p.w_deq[n0 + lane] : 0.f) : wd0;
+        const int ci = c - c_lo;
+        const float wdl = p.per_row ? (ci == 0 ? w4[0] : ci == 1 ? w4[1] : ci == 2 ? w4[2] : w4[3]) : wd0;
         const bool small_acc = p.K < 32768;  // |acc| <= 128 K < 2^22: convert without the XU pipe
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float wd = p.per_row ? __shfl_sync(0xffffffffu, wdl, j) : wd0;
           v[j] = BF ? __uint_as_float(r[j]) : (small_acc ? acc_to_f(r[j]) : (float)(int32_t)r[j]) * xs * wd;
         }
+        if (warp == 2 && lane == 0) trace_at(p, 18);
         if (p.out && p.vec_store && n0 + 32 <= p.N && !p.acc_out) {
           stage_store(v, row - lane, n0);
+          if (warp == 2 && lane == 0) trace_at(p, 19);
           continue;
         }
         if (!row_ok) continue;
@@ -892,6 +980,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     // TMA stores still reading this warp's output slots must finish before the CTA exits
     if (dual_tma && lane == 0) bulk_wait_all();
+    if (warp == 2 && lane == 0) trace_at(p, 12);
   }
 
   fence_before();
@@ -987,11 +1076,39 @@ static int make_map_bf16_32(CUtensorMap *map, const void *ptr, int64_t inner, in
   return TESM_OK;
 }
 
+// prints, per stamp slot, the min / median / max over CTAs in microseconds after the first CTA start
+static void dump_trace(unsigned long long *tr, int ctas, cudaStream_t st, int M, int N, int K, int total,
+                       int splits, int n_full) {
+  std::vector<unsigned long long> h((size_t)ctas * 32);
+  cudaStreamSynchronize(st);
+  cudaMemcpy(h.data(), tr, h.size() * 8, cudaMemcpyDeviceToHost);
+  cudaFree(tr);
+  unsigned long long t0 = ~0ull;
+  for (int c = 0; c < ctas; ++c)
+    if (h[c * 32] && h[c * 32] < t0) t0 = h[c * 32];
+  fprintf(stderr, "gemm trace M=%d N=%d K=%d ctas=%d units=%d splits=%d n_full=%d\n", M, N, K, ctas, total, splits,
+          n_full);
+  for (int s = 0; s < 32; ++s) {
+    std::vector<double> v;
+    for (int c = 0; c < ctas; ++c)
+      if (h[c * 32 + s]) v.push_back((h[c * 32 + s] - t0) * 1e-3);
+    if (v.empty()) continue;
+    std::sort(v.begin(), v.end());
+    fprintf(stderr, "  slot %2d n=%3zu min %7.2f med %7.2f max %7.2f us\n", s, v.size(), v[0], v[v.size() / 2],
+            v.back());
+  }
+}
+
 template <int BN, bool DUAL = false, int MT = 1, bool PAIR = false, bool BF = false>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
   CUtensorMap ma, mb, ml, mg, mo;
   int rc = make_map(&ma, A, p.K, p.M, lda, BM * MT);
   if (rc) return rc;
+  static const int pdl_late_env = [] {
+    const char *e = getenv("TESM_PDL_GEMM_LATE");
+    return e ? atoi(e) : 1;
+  }();
+  p.pdl_late = pdl_late_env;
   rc = make_map(&mb, B, p.K, p.N, ldb, PAIR ? BN / 2 : BN);
   if (rc) return rc;
   ml = mg = mo = ma;  // unused unless dual_tma
@@ -1089,7 +1206,19 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     const int clusters = total < max_clusters ? total : max_clusters;
     cfg.gridDim = dim3(2 * clusters);
+    static const int trace_at_call = [] {
+      const char *e = getenv("TESM_GEMM_TRACE");
+      return e ? atoi(e) : 0;
+    }();
+    static int calls = 0;
+    unsigned long long *tr = nullptr;
+    if (trace_at_call && ++calls == trace_at_call) {
+      cudaMalloc(&tr, (size_t)cfg.gridDim.x * 32 * 8);
+      cudaMemsetAsync(tr, 0, (size_t)cfg.gridDim.x * 32 * 8, st);
+      p.trace = tr;
+    }
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, ml, mg, mo, p);
+    if (tr) dump_trace(tr, cfg.gridDim.x, st, p.M, p.N, p.K, total, p.splits, p.n_full);
     if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemm_i8 (CTA pairs): ") + cudaGetErrorString(e));
     return check_launch("gemm_i8 (CTA pairs)");
   }

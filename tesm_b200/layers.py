@@ -291,17 +291,22 @@ def siso_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     snapshot_if_due(cache)
     W = cache["ent_k_cache"].shape[1]
     proj = linear_q(mod.in_proj, q, act_dtype)
-    cross_bias = None
+    # the cross-layer query bias is computed inside the step kernel (cross_layer_q_proj on the
+    # previous layer's fp32 state row)
+    xstate = xq = None
     if cross_layer_state is not None:
-        cross_bias = linear(mod.cross_layer_q_proj, cross_layer_state.reshape(B, D).float(), torch.float32)
+        xstate = cross_layer_state.reshape(B, D)
+        if xstate.dtype != torch.float32 or not xstate.is_contiguous():
+            xstate = xstate.float().contiguous()
+        xq = packed_weight(mod.cross_layer_q_proj, need_tern=True)
     new_state = torch.empty(B, D, device=dev, dtype=torch.float32)
     # the step emits the int8 codes of tanh(ent) | ent - s; state_proj, ent_proj and the combine
     # then run as one dual-accumulator GEMM, as in prefill
     codes, inv1, inv2, Dp = ops.siso_decode_step_codes(
         proj, B, Dm, D, R, W, _param_cache(mod, "decay_bias"), _param_cache(mod, "local_entanglement_bias"),
-        cross_bias, cache["state"], cache["ent_k_cache"], cache["ent_v_cache"], cache["_ctl"],
+        None, cache["state"], cache["ent_k_cache"], cache["ent_v_cache"], cache["_ctl"],
         mod.entanglement_threshold, mod.entanglement_scale, mod.rope_base, act_dtype, mod.state_proj.bit_eps,
-        mod.ent_proj.bit_eps, new_state)
+        mod.ent_proj.bit_eps, new_state, xstate, xq, mod.cross_layer_q_proj.bit_eps if xq is not None else 0.0)
     _advance_host(cache, W)
     tern, deq1, deq2, _ = combine_weight(mod)
     y = torch.empty(B, Dm, device=dev, dtype=act_dtype)

@@ -390,8 +390,11 @@ def decode_step(proj, B, Dm, H, D, R, W, decay_bias, bias, cross, state, kc, vc,
 
 
 def siso_decode_step_codes(proj, B, Dm, D, R, W, decay_bias, bias, cross, state, kc, vc, ctl, thr, es, base,
-                           act_dtype, eps1, eps2, new_state):
-    """One-token SISO step emitting the int8 codes of tanh(ent) | ent - s for the combine GEMM."""
+                           act_dtype, eps1, eps2, new_state, xstate=None, xq: Optional[PackedWeight] = None,
+                           xq_eps=0.0):
+    """One-token SISO step emitting the int8 codes of tanh(ent) | ent - s for the combine GEMM.
+    With ``xstate`` (the previous layer's fp32 state, (B, D)) and ``xq`` (cross_layer_q_proj's
+    packed weight) the step computes the cross-layer query bias itself."""
     Dp = round_up(D, 128)
     codes = torch.empty(B, 2 * Dp, device=proj.device, dtype=torch.int8)
     inv1 = torch.empty(B, device=proj.device, dtype=torch.float32)
@@ -400,7 +403,8 @@ def siso_decode_step_codes(proj, B, Dm, D, R, W, decay_bias, bias, cross, state,
               R, W, decay_bias.data_ptr(), bias.data_ptr(), _ptr(cross), state.data_ptr(), kc.data_ptr(),
               vc.data_ptr(), ctl.data_ptr(), float(thr), float(es), float(base), dtype_code(act_dtype), float(eps1),
               float(eps2), codes.data_ptr(), codes.stride(0), Dp, inv1.data_ptr(), inv2.data_ptr(), _ptr(new_state),
-              _stream())
+              _ptr(xstate), _ptr(xq.tern) if xq is not None else None, xq.tern.stride(0) if xq is not None else 0,
+              _ptr(xq.deq) if xq is not None else None, float(xq_eps), _stream())
     return codes, inv1, inv2, Dp
 
 

@@ -335,3 +335,36 @@ def test_generate_graph_matches_eager(lib, temperature, top_k):
     assert outs[0].shape == (4, 22)
     assert torch.equal(outs[0][:, :10], ids)
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("B,D,R,W,pos", [(3, 256, 64, 16, 20), (256, 256, 64, 16, 5), (5, 40, 16, 4, 9), (70, 96, 32, 8, 0)])
+def test_decode_fused_cross_bias_matches_bitlinear(ops, B, D, R, W, pos):
+    """The decode step's in-kernel cross-layer query bias (cross_layer_q_proj on the previous
+    layer's fp32 state, tesm.py:1302-1305) against the separate quantiser + BitLinear GEMM/GEMV
+    bias it replaces: codes, scales, state and caches bit-identical."""
+    Dm, eps = 64, 1e-5
+    dev = torch.device("cuda")
+    proj = randn((B, 2 * Dm + 3 * D + 2 * R), 11).to(dev).to(torch.bfloat16)
+    xstate = (randn((B, D), 12) * 0.7).to(dev)
+    pw = ops.pack_weight((randn((R, D), 13) * 0.05).to(dev), eps, with_tern=True)
+    decay_bias = (randn((D,), 14) * 0.3 + 2.0).to(dev)
+    bias = (randn((W,), 15) * 0.3).to(dev)
+    state0 = randn((B, D), 16).double().to(dev)
+    kc0, vc0 = randn((B, W, R), 17).to(dev), randn((B, W, D), 18).to(dev)
+    ctl0 = torch.tensor([pos, pos % W, 0], dtype=torch.int32, device=dev)
+
+    def run(fused):
+        state, kc, vc, ctl = state0.clone(), kc0.clone(), vc0.clone(), ctl0.clone()
+        ns = torch.empty(B, D, device=dev, dtype=torch.float32)
+        if fused:
+            cross, xs, xq = None, xstate, pw
+        else:
+            cross, xs, xq = ops.matmul_q(ops.quantize(xstate, eps), pw, torch.float32), None, None
+        codes, inv1, inv2, _ = ops.siso_decode_step_codes(
+            proj, B, Dm, D, R, W, decay_bias, bias, cross, state, kc, vc, ctl, 0.1, 0.2, 1e4, torch.bfloat16,
+            eps, eps, ns, xs, xq, eps)
+        torch.cuda.synchronize()
+        return [codes, inv1, inv2, ns, state, kc, vc, ctl]
+
+    for a, b in zip(run(False), run(True)):
+        assert torch.equal(a, b)
