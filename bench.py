@@ -524,6 +524,36 @@ def run_combine_case(args):
     return 0
 
 
+def run_quant_case(args):
+    """The activation quantisers at prefill and decode shapes of config 5, graph-timed, for
+    ncu captures and their HBM fractions: k_quant_act on the SwiGLU output h (M x 11008 bf16 in,
+    int8 codes out) and k_add_rmsnorm_quant on a block boundary (M x 4096 bf16 hidden + fp32
+    residual in, fp32 residual + int8 codes out).  Prefill M = 16384 (inputs > L2); decode M = 256."""
+    import torch
+    from tesm_b200 import ops
+    torch.manual_seed(0)
+    peaks, _ = load_peaks()
+    F, Dm = CFG["d_intermediate"], CFG["d_model"]
+    for M in (16384, 256):
+        h = torch.randn(M, F, device="cuda").to(torch.bfloat16)
+        t = _graph_time(lambda i: ops.quant_act(h, 1e-5, ops.LAYOUT_ROWMAJOR), inner=4)
+        byts = M * F * 3
+        print(json.dumps({"kernel": "k_quant_act", "M": M, "K": F, "us": t * 1e6, "GB_s": byts / t / 1e9,
+                          "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"]}), flush=True)
+        del h
+        x = torch.randn(M, Dm, device="cuda").to(torch.bfloat16)
+        res = torch.randn(M, Dm, device="cuda")
+        res_out = torch.empty_like(res)
+        w = torch.rand(Dm, device="cuda") + 0.5
+        q = ops.alloc_quant(M, Dm, x.device, ops.LAYOUT_ROWMAJOR)
+        t = _graph_time(lambda i: ops.add_rmsnorm_quant(x, res, res_out, w, 1e-5, 1e-5, q), inner=4)
+        byts = M * Dm * (2 + 4 + 4 + 1)
+        print(json.dumps({"kernel": "k_add_rmsnorm_quant", "M": M, "K": Dm, "us": t * 1e6, "GB_s": byts / t / 1e9,
+                          "hbm_frac": byts / t / 1e9 / peaks["hbm_gbs"]}), flush=True)
+        del x, res, res_out
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone case of the dominant kernel for ncu captures: one int8 tcgen05 GEMM
     of in_proj-like shape M=16384, N=11008, K=4096 (operands 109 MB + 360 MB output > L2)."""
@@ -857,7 +887,7 @@ def main():
     ap.add_argument("--workload", default=None, choices=["cfg2", "cfg3", "cfg4"],
                     help="supplementary measurements of BASELINE configs 2-4 (one JSON line per measurement)")
     ap.add_argument("--decode-steps", type=int, default=512, help="config-5 decode steps at batch 256 (0: skip)")
-    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine", "skinny", "prefill_gemms"],
+    ap.add_argument("--kernel", default=None, choices=["gemm", "decode", "combine", "skinny", "prefill_gemms", "quant"],
                     help="run a small ncu case")
     args = ap.parse_args()
     if args.workload:
@@ -866,6 +896,8 @@ def main():
         return run_decode_case(args)
     if args.kernel == "combine":
         return run_combine_case(args)
+    if args.kernel == "quant":
+        return run_quant_case(args)
     if args.kernel == "skinny":
         return run_skinny_case(args)
     if args.kernel == "prefill_gemms":

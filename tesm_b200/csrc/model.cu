@@ -85,6 +85,16 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
   for (int j = 0; j < GPT; ++j) {
     const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
     if (g >= groups_out) continue;
+    if (layout == TESM_LAYOUT_ROWMAJOR && !rowsum) {  // act_code via act_code_bits (FMA pipe only)
+      uint32_t wv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        wv[q] = pack_code_bytes(act_code_bits(__fmul_rn(v[j][4 * q], s)), act_code_bits(__fmul_rn(v[j][4 * q + 1], s)),
+                                act_code_bits(__fmul_rn(v[j][4 * q + 2], s)),
+                                act_code_bits(__fmul_rn(v[j][4 * q + 3], s)));
+      reinterpret_cast<uint4 *>(crow)[g] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      continue;
+    }
     int c[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
@@ -187,11 +197,17 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
                   (!residual_out || (uintptr_t)residual_out % 16 == 0) && ((uintptr_t)weight % 16 == 0) &&
                   (!y_out || (uintptr_t)y_out % 16 == 0);
   // few rows (decode): one 16-element group per thread, so each row's latency chain is short
-  const int gpt = M < 1024 && groups_out <= 1024 ? 1 : 4;
+  static const int gpt_big = [] {
+    const char *e = getenv("TESM_ARQ_GPT");  // tuning override: 16-element groups per thread, many rows
+    const int v = e ? atoi(e) : 2;  // 2: 56 registers, 0.76 of HBM at 16384 x 4096 (4: 96, 0.70)
+    return v == 4 ? 4 : 2;
+  }();
+  const int gpt = M < 1024 && groups_out <= 1024 ? 1 : gpt_big;
   int64_t threads = round_up(ceil_div(groups_out, gpt), 32);
   if (threads < 32) threads = 32;
   TESM_REQUIRE(threads <= 1024, "add_rmsnorm_quant: K too large");
-  return launch_k("add_rmsnorm_quant", gpt == 1 ? k_add_rmsnorm_quant<1> : k_add_rmsnorm_quant<4>,
+  return launch_k("add_rmsnorm_quant",
+                  gpt == 1 ? k_add_rmsnorm_quant<1> : gpt == 2 ? k_add_rmsnorm_quant<2> : k_add_rmsnorm_quant<4>,
                   dim3((unsigned)M), dim3((unsigned)threads), 0, (cudaStream_t)stream, x, xdtype, residual,
                   residual_out, weight, eps, (int)K, qeps, codes, ld_codes, layout, groups_out, inv_scale, rowsum,
                   y_out, ydtype, vec);

@@ -111,6 +111,69 @@ __global__ void k_unpack(const uint8_t *__restrict__ packed, int64_t ld_packed, 
 // (16-byte vector loads when the row is aligned).
 constexpr int kQuantGPT = 4;
 
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// bf16 rows with row-major codes.  A group's 16 values stay packed as 8 bf16x2 words.  Row maximum
+// of |x| on the bit patterns (non-negative bf16 values order like their 16-bit patterns).  Codes:
+// the exact product x * s of two bf16 values rounded once to bf16 (mul.rn.bf16x2) is the fp32
+// __fmul_rn followed by act_code's round to bf16; then act_code_bits.  Same codes as act_code.
+template <int GPT>
+__device__ __forceinline__ void quant_row_bf16(const __nv_bfloat16 *xrow, float eps, int8_t *crow, int64_t groups,
+                                               float *inv_scale, const float *amax_in, int64_t row, float *redf) {
+  uint32_t w[GPT][8];
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+    if (g < groups) {
+      const uint4 *p = reinterpret_cast<const uint4 *>(xrow + g * 16);
+      const uint4 a = p[0], b = p[1];
+      w[j][0] = a.x, w[j][1] = a.y, w[j][2] = a.z, w[j][3] = a.w;
+      w[j][4] = b.x, w[j][5] = b.y, w[j][6] = b.z, w[j][7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[j][i] = 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = __vmaxu2(m, w[j][i] & 0x7fff7fffu);
+  }
+  float amax = __uint_as_float(max(m & 0xffffu, m >> 16) << 16);
+  amax = block_reduce(amax, redf, [](float a, float b) { return fmaxf(a, b); }, 0.f);
+  if (amax_in) amax = amax_in[row];
+  const float s = act_scale(amax, eps, TESM_BF16);
+  if (threadIdx.x == 0) inv_scale[row] = __frcp_rn(s);
+  const uint32_t sb = __float_as_uint(s) >> 16, s2 = sb | (sb << 16);
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
+    if (g >= groups) continue;
+    uint32_t wv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t p0 = mul_bf16x2(w[j][2 * q], s2), p1 = mul_bf16x2(w[j][2 * q + 1], s2);
+      wv[q] = pack_code_bytes(act_code_bits(__uint_as_float(p0 << 16)), act_code_bits(__uint_as_float(p0 & 0xffff0000u)),
+                              act_code_bits(__uint_as_float(p1 << 16)), act_code_bits(__uint_as_float(p1 & 0xffff0000u)));
+    }
+    reinterpret_cast<uint4 *>(crow)[g] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
+// bf16 rows, 16-byte aligned, row-major codes (the GEMM operand): quant_row_bf16, one block per row
+template <int GPT>
+__global__ void k_quant_act_bf16(const __nv_bfloat16 *__restrict__ x, int64_t K, int64_t ldx, float eps,
+                                 int8_t *__restrict__ codes, int64_t ld_codes, float *__restrict__ inv_scale,
+                                 const float *__restrict__ amax_in) {
+  __shared__ float redf[32];
+  pdl_trigger();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  quant_row_bf16<GPT>(x + row * ldx, eps, codes + row * ld_codes, (K + 15) / 16, inv_scale, amax_in, row, redf);
+}
+
 template <int GPT>
 __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, int64_t ldx, float eps,
                             int8_t *__restrict__ codes, int64_t ld_codes, int layout, int64_t groups_out,
@@ -243,6 +306,10 @@ static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_
   TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
   const int esz = dtype == TESM_BF16 ? 2 : 4;
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
+  if (dtype == TESM_BF16 && vec && layout == TESM_LAYOUT_ROWMAJOR)
+    return launch_k("quant_act", gpt == 1 ? k_quant_act_bf16<1> : k_quant_act_bf16<kQuantGPT>, dim3((unsigned)M),
+                    dim3((unsigned)threads), 0, (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16 *>(x), K,
+                    ldx, eps, codes, ld_codes, inv_scale, amax);
   return launch_k("quant_act", gpt == 1 ? k_quant_act<1> : k_quant_act<kQuantGPT>, dim3((unsigned)M),
                   dim3((unsigned)threads), 0, (cudaStream_t)stream, x, dtype, K, ldx, eps, codes, ld_codes, layout,
                   groups_out, inv_scale, rowsum, vec, amax);

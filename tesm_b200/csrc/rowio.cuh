@@ -137,4 +137,19 @@ __device__ __forceinline__ int act_code(float x, float s, int dtype) {
   return (int)fminf(fmaxf(p, -128.f), 127.f);
 }
 
+// act_code on a value already rounded to the quantiser dtype (p = round_to(dtype, x * s)), as the
+// low byte of a float: clamping to [-128, 127] before rounding to an integer gives the same code as
+// rounding first, and adding 1.5 * 2^23 rounds a value of magnitude <= 128 to the nearest integer
+// (ties to even, like rintf) in the low mantissa bits, two's complement in the low byte.  FMA-pipe
+// arithmetic only (no rintf / float-to-int conversion).
+__device__ __forceinline__ uint32_t act_code_bits(float p) {
+  return __float_as_uint(fminf(fmaxf(p, -128.f), 127.f) + 12582912.f);
+}
+// low bytes of four act_code_bits words -> one packed word (first argument in the low byte)
+__device__ __forceinline__ uint32_t pack_code_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+// the signed code held in the low byte of an act_code_bits word
+__device__ __forceinline__ int code_of_bits(uint32_t bits) { return (int)(bits << 24) >> 24; }
+
 }  // namespace tesm
