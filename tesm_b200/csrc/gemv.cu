@@ -159,7 +159,13 @@ static int launch_gemv_rows(const GemvParams &p, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddepcontrol.wait
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  // the GEMV follows its activation quantiser: launched programmatically it requests every weight
+  // byte of its rows while the quantiser runs (TESM_GEMV_PDL=0 turns this off)
+  static const int gemv_pdl = [] {
+    const char *e = getenv("TESM_GEMV_PDL");
+    return e ? atoi(e) : 1;
+  }();
+  cfg.numAttrs = (gemv_pdl || pdl_enabled()) ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_rows<NT, WPC, PF>, p);
   if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemv_int2 launch: ") + cudaGetErrorString(e));
   return TESM_OK;
