@@ -48,6 +48,7 @@ struct WinEntParams {
   const float *bias;   // window bias of head h at bias + h * W, read at [W-1-o]
   const float *mimo_o; // MIMO (H, RM, D)
   int B, L, H, D, R, quirk, async16, ntiles_b;
+  int stage_out;  // bf16 outputs with 16-byte aligned 8-channel groups: staged 16-byte row stores
   float thr, es, sqrt_r, rope_base;
   RopeTab rt;
   void *out_tanh, *out_chg;  // out[(row0 + t) * out_ld + h * D + ch]
@@ -106,7 +107,12 @@ struct WinSmem {
   float *twr;      // T x W ternary
   float *inv;      // T     1 / max(sum |tern|, 1)
   float *oT, *oC;  // kWinSisoCodes: T x (D + 1) staged outputs
+  int *amT, *amC;  // kWinSisoCodes: per-row max |value| (non-negative float bits)
+  uint32_t *stg;   // other modes: per warp 16 rows x 20 words (32 bf16 + 16 bytes of padding)
 };
+
+// warps of the CTA: one staging buffer (nst = 1) runs 256 threads, two run 512
+__host__ __device__ inline int win_warps(const WinGeom &g) { return g.nst == 1 ? 8 : 16; }
 
 __host__ __device__ inline size_t win_smem_bytes(const WinGeom &g) {
   const size_t stage = win_r16((int64_t)g.NROWS * g.SRR * 4) + win_r16((int64_t)kWinT * g.QRS) +
@@ -114,7 +120,10 @@ __host__ __device__ inline size_t win_smem_bytes(const WinGeom &g) {
   size_t b = g.nst * stage + win_r16((int64_t)g.nk * g.half * 8) + win_r16((int64_t)g.half * 4) +
              win_r16((int64_t)kWinT * g.RP * 4) + win_r16((int64_t)g.nk * g.RP * 4) +
              win_r16((int64_t)kWinT * g.W * 4) + win_r16((int64_t)kWinT * 4);
-  if (g.mode == kWinSisoCodes) b += 2 * win_r16((int64_t)kWinT * (g.D + 1) * 4);
+  if (g.mode == kWinSisoCodes)
+    b += 2 * win_r16((int64_t)kWinT * (g.D + 1) * 4) + 2 * win_r16((int64_t)kWinT * 4);
+  else
+    b += win_r16((int64_t)win_warps(g) * 16 * 20 * 4);
   return b;
 }
 
@@ -138,9 +147,15 @@ __device__ __forceinline__ WinSmem win_carve(uint8_t *p, const WinGeom &g) {
   s.twr = reinterpret_cast<float *>(take((int64_t)kWinT * g.W * 4));
   s.inv = reinterpret_cast<float *>(take((int64_t)kWinT * 4));
   s.oT = s.oC = nullptr;
+  s.amT = s.amC = nullptr;
+  s.stg = nullptr;
   if (g.mode == kWinSisoCodes) {
     s.oT = reinterpret_cast<float *>(take((int64_t)kWinT * (g.D + 1) * 4));
     s.oC = reinterpret_cast<float *>(take((int64_t)kWinT * (g.D + 1) * 4));
+    s.amT = reinterpret_cast<int *>(take((int64_t)kWinT * 4));
+    s.amC = reinterpret_cast<int *>(take((int64_t)kWinT * 4));
+  } else {
+    s.stg = reinterpret_cast<uint32_t *>(take((int64_t)win_warps(g) * 16 * 20 * 4));
   }
   return s;
 }
@@ -366,6 +381,7 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(const __grid_c
       }
     }
     __syncthreads();
+    if (MODE == kWinSisoCodes && tid < 2 * kWinT) (tid < kWinT ? s.amT : s.amC)[tid & (kWinT - 1)] = 0;
     // scores: lane = (row t, lag group og) with lags og + j * OG, j < LPT, so one q load feeds
     // LPT independent dot products; the row's OG lanes are adjacent (shuffle-summed count)
     {
@@ -413,7 +429,10 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(const __grid_c
       }
     }
     __syncthreads();
-    // banded window product on the tensor cores + epilogue
+    // banded window product on the tensor cores + epilogue.  A warp pair owns a contiguous range
+    // of 8-channel groups and walks it in batches of 4 groups; with staged bf16 outputs each
+    // batch's 16 rows x 32 channels are transposed through the warp's shared block (tanh rows,
+    // then change rows) and leave as 16-byte row segments.
     {
       constexpr int KS = (15 + W + 7) / 8;
       const int SRR = g.SRR, SR = g.SR;
@@ -430,103 +449,173 @@ __global__ void __launch_bounds__(NT, NST == 1 ? 2 : 1) k_win_ent(const __grid_c
       }
       const int ngroups = (D + 7) / 8;
       const float *st = sg.st;
-      for (int cg = warp >> 1; cg < ngroups; cg += NT / 64) {
-        float acc[RM][4];
+      constexpr int NWP = NT / 64;
+      const int gpw = (ngroups + NWP - 1) / NWP;
+      const int g_lo = min(ngroups, (warp >> 1) * gpw), g_hi = min(ngroups, g_lo + gpw);
+      const bool staged = MODE != kWinSisoCodes && p.stage_out;
+      uint32_t *stg = MODE != kWinSisoCodes ? s.stg + warp * 320 : nullptr;
+      float rmT[2] = {0.f, 0.f}, rmC[2] = {0.f, 0.f};  // codes: max |value| of rows gq, gq + 8
+      for (int cb = g_lo; cb < g_hi; cb += 4) {
+        float2 keepC[4][2];  // staged: the batch's change values, transposed after the tanh rows
 #pragma unroll
-        for (int k = 0; k < RM; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
-        const float *bcol = st + (size_t)(tb + tig) * SRR + cg * 8 + gq;
+        for (int j = 0; j < 4; ++j) {
+          keepC[j][0] = keepC[j][1] = make_float2(0.f, 0.f);
+          const int cg = cb + j;
+          if (cg >= g_hi) continue;
+          float acc[RM][4];
 #pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
+          for (int k = 0; k < RM; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
+          const float *bcol = st + (size_t)(tb + tig) * SRR + cg * 8 + gq;
 #pragma unroll
-          for (int k = 0; k < RM; ++k) {
-            const float x0 = bcol[(size_t)(ks * 8) * SRR + k * SR], x1 = bcol[(size_t)(ks * 8 + 4) * SRR + k * SR];
-            const uint32_t h0 = f32_to_tf32(x0), h1 = f32_to_tf32(x1);
-            mma_tf32(acc[k], a[ks], h0, h1);
-            mma_tf32(acc[k], a[ks], __float_as_uint(x0 - __uint_as_float(h0)),
-                     __float_as_uint(x1 - __uint_as_float(h1)));
+          for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+            for (int k = 0; k < RM; ++k) {
+              const float x0 = bcol[(size_t)(ks * 8) * SRR + k * SR], x1 = bcol[(size_t)(ks * 8 + 4) * SRR + k * SR];
+              const uint32_t h0 = f32_to_tf32(x0), h1 = f32_to_tf32(x1);
+              mma_tf32(acc[k], a[ks], h0, h1);
+              mma_tf32(acc[k], a[ks], __float_as_uint(x0 - __uint_as_float(h0)),
+                       __float_as_uint(x1 - __uint_as_float(h1)));
+            }
+          }
+          // epilogue: the lane holds rows tb+gq, tb+gq+8 x channels ch, ch+1 of every rank
+          const int ch = cg * 8 + 2 * tig;
+          const bool has_x = ch < D, has_y = ch + 1 < D;
+          float2 mo[RM];
+          if (MODE == kWinMimo) {
+#pragma unroll
+            for (int k = 0; k < RM; ++k) {
+              const float *m = p.mimo_o + ((int64_t)h * RM + k) * D + ch;
+              mo[k] = make_float2(has_x ? m[0] : 0.f, has_y ? m[1] : 0.f);
+            }
+          }
+#pragma unroll
+          for (int hr = 0; hr < 2; ++hr) {
+            const int t = tb + gq + 8 * hr;
+            if (t >= nt || !has_x) continue;
+            const float iv = s.inv[t];
+            const float *srow = st + (size_t)(t + W - 1) * SRR + ch;
+            // the two channels ch, ch+1 in packed fp32 (FFMA2): e = s + es (acc / norm - s)
+            const float2 iv2 = make_float2(iv, iv), es2 = make_float2(es, es);
+            float2 E = make_float2(0.f, 0.f), Cg = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < RM; ++k) {
+              float2 sv;
+              if (has_y) {
+                sv = *reinterpret_cast<const float2 *>(srow + k * SR);  // ch even, SR % 4 == 0
+              } else {
+                sv = make_float2(srow[k * SR], 0.f);
+              }
+              const float2 nsv = make_float2(-sv.x, -sv.y);
+              const float2 dlt = __ffma2_rn(make_float2(acc[k][2 * hr], acc[k][2 * hr + 1]), iv2, nsv);
+              const float2 e = __ffma2_rn(es2, dlt, sv);
+              const float2 chg = __fadd2_rn(e, nsv);
+              if (MODE == kWinMimo) {
+                E = __ffma2_rn(mo[k], e, E);
+                Cg = __ffma2_rn(mo[k], chg, Cg);
+              } else {
+                E = e;
+                Cg = chg;
+              }
+            }
+            const float ex = E.x, ey = E.y, cx = Cg.x, cy = Cg.y;
+            if (MODE == kWinSisoCodes) {
+              float *rt = s.oT + t * (D + 1) + ch, *rc = s.oC + t * (D + 1) + ch;
+              const float vt = round_to(p.act_dtype, win_tanh(ex)), vc = round_to(p.act_dtype, cx);
+              rt[0] = vt;
+              rc[0] = vc;
+              rmT[hr] = fmaxf(rmT[hr], fabsf(vt));
+              rmC[hr] = fmaxf(rmC[hr], fabsf(vc));
+              if (has_y) {
+                const float wt = round_to(p.act_dtype, win_tanh(ey)), wc = round_to(p.act_dtype, cy);
+                rt[1] = wt;
+                rc[1] = wc;
+                rmT[hr] = fmaxf(rmT[hr], fabsf(wt));
+                rmC[hr] = fmaxf(rmC[hr], fabsf(wc));
+              }
+            } else if (staged) {
+              const __nv_bfloat162 tv = __floats2bfloat162_rn(win_tanh(ex), win_tanh(ey));
+              stg[(gq + 8 * hr) * 20 + j * 4 + tig] = *reinterpret_cast<const uint32_t *>(&tv);
+              keepC[j][hr] = make_float2(cx, cy);
+            } else {
+              const int64_t o = (row0 + t0 + t) * p.out_ld + (int64_t)h * D + ch;
+              const bool pair = has_y && (o & 1) == 0;
+              win_store2(p.out_tanh, p.out_dtype, o, win_tanh(ex), has_y ? win_tanh(ey) : 0.f, pair, has_y);
+              win_store2(p.out_chg, p.out_dtype, o, cx, cy, pair, has_y);
+            }
           }
         }
-        // epilogue: the lane holds rows tb+gq, tb+gq+8 x channels ch, ch+1 of every rank
-        const int ch = cg * 8 + 2 * tig;
-        const bool has_x = ch < D, has_y = ch + 1 < D;
-        float2 mo[RM];
-        if (MODE == kWinMimo) {
+        if (MODE != kWinSisoCodes && staged) {
 #pragma unroll
-          for (int k = 0; k < RM; ++k) {
-            const float *m = p.mimo_o + ((int64_t)h * RM + k) * D + ch;
-            mo[k] = make_float2(has_x ? m[0] : 0.f, has_y ? m[1] : 0.f);
+          for (int arr = 0; arr < 2; ++arr) {
+            if (arr == 1) {
+              __syncwarp();  // the tanh rows have been read
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                  const __nv_bfloat162 cv = __floats2bfloat162_rn(keepC[j][hr].x, keepC[j][hr].y);
+                  stg[(gq + 8 * hr) * 20 + j * 4 + tig] = *reinterpret_cast<const uint32_t *>(&cv);
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+              const int row = ps * 8 + (lane >> 2), chunk = lane & 3, t = tb + row;
+              if (t < nt && cb + chunk < g_hi) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(stg + row * 20 + chunk * 4);
+                const int64_t o = (row0 + t0 + t) * p.out_ld + (int64_t)h * D + (cb + chunk) * 8;
+                *reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(arr ? p.out_chg : p.out_tanh) + o) = v;
+              }
+            }
           }
+          __syncwarp();  // the block is rewritten by the next batch
         }
+      }
+      if (MODE == kWinSisoCodes) {
+        // row maxima: the row's 4 lanes, then the warps of the CTA (shared atomics on the bits
+        // of non-negative floats, which order like their values)
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
-          const int t = tb + gq + 8 * hr;
-          if (t >= nt || !has_x) continue;
-          const float iv = s.inv[t];
-          const float *srow = st + (size_t)(t + W - 1) * SRR + ch;
-          // the two channels ch, ch+1 in packed fp32 (FFMA2): e = s + es (acc / norm - s)
-          const float2 iv2 = make_float2(iv, iv), es2 = make_float2(es, es);
-          float2 E = make_float2(0.f, 0.f), Cg = make_float2(0.f, 0.f);
+          float mt = rmT[hr], mc = rmC[hr];
 #pragma unroll
-          for (int k = 0; k < RM; ++k) {
-            float2 sv;
-            if (has_y) {
-              sv = *reinterpret_cast<const float2 *>(srow + k * SR);  // ch even, SR % 4 == 0
-            } else {
-              sv = make_float2(srow[k * SR], 0.f);
-            }
-            const float2 nsv = make_float2(-sv.x, -sv.y);
-            const float2 dlt = __ffma2_rn(make_float2(acc[k][2 * hr], acc[k][2 * hr + 1]), iv2, nsv);
-            const float2 e = __ffma2_rn(es2, dlt, sv);
-            const float2 chg = __fadd2_rn(e, nsv);
-            if (MODE == kWinMimo) {
-              E = __ffma2_rn(mo[k], e, E);
-              Cg = __ffma2_rn(mo[k], chg, Cg);
-            } else {
-              E = e;
-              Cg = chg;
-            }
+          for (int o = 1; o <= 2; o <<= 1) {
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
           }
-          const float ex = E.x, ey = E.y, cx = Cg.x, cy = Cg.y;
-          if (MODE == kWinSisoCodes) {
-            float *rt = s.oT + t * (D + 1) + ch, *rc = s.oC + t * (D + 1) + ch;
-            rt[0] = round_to(p.act_dtype, win_tanh(ex));
-            rc[0] = round_to(p.act_dtype, cx);
-            if (has_y) {
-              rt[1] = round_to(p.act_dtype, win_tanh(ey));
-              rc[1] = round_to(p.act_dtype, cy);
-            }
-          } else {
-            const int64_t o = (row0 + t0 + t) * p.out_ld + (int64_t)h * D + ch;
-            const bool pair = has_y && (o & 1) == 0;
-            win_store2(p.out_tanh, p.out_dtype, o, win_tanh(ex), has_y ? win_tanh(ey) : 0.f, pair, has_y);
-            win_store2(p.out_chg, p.out_dtype, o, cx, cy, pair, has_y);
+          const int t = tb + gq + 8 * hr;
+          if (tig == 0 && t < nt && g_lo < g_hi) {
+            atomicMax(s.amT + t, __float_as_int(mt));
+            atomicMax(s.amC + t, __float_as_int(mc));
           }
         }
       }
     }
     if (MODE == kWinSisoCodes) {
-      // per-token int8 codes of both staged outputs (exactly as tesm_b200_quant_act)
+      // per-token int8 codes of both staged outputs (the codes of tesm_b200_quant_act): lane =
+      // row (conflict-free on the D + 1 row pitch), 16 channels per item, 16-byte stores
       __syncthreads();
-      for (int item = warp; item < 2 * nt; item += NT / 32) {
-        const int t = item >> 1, which = item & 1;
-        const float *src = (which ? s.oC : s.oT) + t * (D + 1);
-        float amax = 0.f;
-        for (int d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(src[d]));
-        amax = warp_max(amax);
+      const int gpr = p.Dp / 16;
+      for (int item = tid; item < 2 * kWinT * gpr; item += NT) {
+        const int t = item & (kWinT - 1), which = (item / kWinT) & 1, g16 = item / (2 * kWinT);
+        if (t >= nt) continue;
+        const float amax = __int_as_float(which ? s.amC[t] : s.amT[t]);
         const float sc = act_scale(amax, which ? p.eps2 : p.eps1, p.act_dtype);
-        const int64_t row = row0 + t0 + t;
-        int8_t *crow = p.codes + row * p.ldc + (which ? p.Dp : 0);
-        for (int d4 = lane * 4; d4 < p.Dp; d4 += 128) {
-          uint32_t wv = 0;
+        const float *src = (which ? s.oC : s.oT) + t * (D + 1);
+        uint32_t wv[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t bts[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int d = d4 + i;
-            const int c = d < D ? act_code(src[d], sc, p.act_dtype) : 0;
-            wv |= (uint32_t)(uint8_t)c << (8 * i);
+            const int d = g16 * 16 + 4 * q + i;
+            bts[i] = d < D ? act_code_bits(round_to(p.act_dtype, __fmul_rn(src[d], sc))) : act_code_bits(0.f);
           }
-          *reinterpret_cast<uint32_t *>(crow + d4) = wv;
+          wv[q] = pack_code_bytes(bts[0], bts[1], bts[2], bts[3]);
         }
-        if (lane == 0) (which ? p.inv2 : p.inv1)[row] = __frcp_rn(sc);
+        const int64_t row = row0 + t0 + t;
+        *reinterpret_cast<uint4 *>(p.codes + row * p.ldc + (which ? p.Dp : 0) + g16 * 16) =
+            make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        if (g16 == 0) (which ? p.inv2 : p.inv1)[row] = __frcp_rn(sc);
       }
     }
     __syncthreads();  // this stage, qs/ks, twr and the staged outputs are free again
@@ -554,6 +643,10 @@ static int win_launch_v(WinEntParams &p, const WinGeom &g, int ctas_per_sm, cuda
   p.async16 = win_async_ok(p, ES, NT);
   if (p.R > 256) return fail(TESM_EUNSUPPORTED, std::string(what) + ": ent_rank above 256");
   p.rt = rope_table(p.R, p.rope_base);
+  p.stage_out = MODE != kWinSisoCodes && p.out_dtype == TESM_BF16 && p.D % 8 == 0 && p.out_ld % 8 == 0 &&
+                (uintptr_t)p.out_tanh % 16 == 0 && (uintptr_t)p.out_chg % 16 == 0;
+  if (MODE == kWinSisoCodes && ((uintptr_t)p.codes % 16 != 0 || p.ldc % 16 != 0 || p.Dp % 16 != 0))
+    return fail(TESM_EINVAL, std::string(what) + ": codes rows must be 16-byte aligned");
   const size_t smem = win_smem_bytes(g);
   static bool attr = false;
   if (!attr) {
