@@ -300,7 +300,9 @@ static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_
   } else {
     return fail(TESM_EINVAL, "quant_act: unknown layout");
   }
-  const int gpt = M < 1024 && groups_out <= 1024 ? 1 : kQuantGPT;  // few rows: short per-row chains
+  // few rows: short per-row chains; short rows (K < 2048): one group per thread, else most of
+  // a 32-thread block would sit idle
+  const int gpt = (M < 1024 && groups_out <= 1024) || groups_out < 128 ? 1 : kQuantGPT;
   int64_t threads = round_up(ceil_div(groups_out, gpt), 32);
   if (threads < 32) threads = 32;
   TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
