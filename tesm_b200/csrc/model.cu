@@ -40,6 +40,10 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
   const void *xrow = reinterpret_cast<const uint8_t *>(x) + row * K * xsz;
   float v[GPT][16];
   float ss = 0.f;
+  // one group per thread (decode rows): the norm weight is requested with the inputs instead of
+  // after the sum-of-squares reduction (one dependent round trip fewer)
+  float wpre[16];
+  if (GPT == 1 && (int64_t)threadIdx.x < groups_in) load16(w, TESM_F32, (int64_t)threadIdx.x * 16, K, vec, wpre);
 #pragma unroll
   for (int j = 0; j < GPT; ++j) {
     const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
@@ -67,7 +71,12 @@ __global__ void k_add_rmsnorm_quant(const void *x, int xdtype, const float *resi
     const int64_t g = threadIdx.x + (int64_t)j * blockDim.x;
     if (g < groups_in) {
       float wv[16];
-      load16(w, TESM_F32, g * 16, K, vec, wv);
+      if (GPT == 1) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) wv[e] = wpre[e];
+      } else {
+        load16(w, TESM_F32, g * 16, K, vec, wv);
+      }
 #pragma unroll
       for (int e = 0; e < 16; ++e) v[j][e] = (v[j][e] * rs) * wv[e];
       if (y_out) store16(reinterpret_cast<uint8_t *>(y_out) + row * K * ysz, ydtype, g * 16, K, vec, v[j]);
