@@ -148,6 +148,17 @@ int tesm_b200_quant_act_amax(const void *x, int dtype, int64_t M, int64_t K, int
 int tesm_b200_acc_scale(const int32_t *acc, int64_t M, int64_t N, const float *inv_scale, const float *w_deq,
                         int per_row, void *out, int out_dtype, int64_t ldo, tesm_stream_t stream);
 
+/* Tensor-parallel MIMO output combine (no reference counterpart; the single-device operation is
+ * tesm_b200_gemm_i8_combine, tesm.py:1255-1261 / tesm_mimo.py:1044-1049): the combine epilogue
+ * of the dual-accumulator GEMM applied to int32 accumulators of state_proj (acc1) and ent_proj
+ * (acc2) summed over the ranks' head shards: out = local + sigmoid(gate) * acc1 * inv1 * deq1
+ * + acc2 * inv2 * deq2 with the GEMM epilogue's float operations (bit-identical to one device);
+ * local / gate are columns c_local / c_gate of proj. */
+int tesm_b200_combine_acc(const int32_t *acc1, const int32_t *acc2, int64_t ld_acc, int64_t M, int64_t N,
+                          const float *inv1, const float *inv2, const float *deq1, const float *deq2, const void *proj,
+                          int proj_dtype, int64_t ldp, int64_t c_local, int64_t c_gate, void *out, int out_dtype,
+                          int64_t ldo, tesm_stream_t stream);
+
 /* state_proj + ent_proj + output combine in one tcgen05 GEMM (tesm.py:1256-1260): two TMEM
  * accumulators, acc1 over the first Kh columns (codes of tanh(ent) x state_proj ternary weights),
  * acc2 over the next Kh (codes of ent - s x ent_proj weights); the epilogue writes

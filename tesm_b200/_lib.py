@@ -53,6 +53,8 @@ SIGNATURES = {
     "tesm_b200_quant_act_amax": [c_vp, c_int, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_i64, c_int, c_vp, c_vp,
                                  c_vp],
     "tesm_b200_acc_scale": [c_vp, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_int, c_i64, c_vp],
+    "tesm_b200_combine_acc": [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64,
+                              c_vp, c_int, c_i64, c_vp],
     "tesm_b200_global_ent_tc_workspace": [c_i64, c_i64, c_i64, c_i64, c_vp],
     "tesm_b200_siso_global_ent_tc": [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
                                      c_float, c_float, c_float, c_vp, c_vp, c_int, c_vp, c_i64, c_vp],

@@ -301,6 +301,13 @@ __device__ __forceinline__ float acc_to_f(uint32_t a) {
 // Sigmoid for the combine epilogue: two transcendental-unit ops (exp2, approximate reciprocal),
 // relative error a few ulp; exp overflow gives 1/inf = 0, the correct limit.
 __device__ __forceinline__ float epi_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+// The output combine of the dual-accumulator epilogue, local + sigmoid(gate) * sp + ep with
+// sp = acc1 * s1 and ep = acc2 * s2, as explicit fused multiply-adds so that every kernel that
+// applies it (both epilogue variants, k_combine_acc) rounds identically.
+__device__ __forceinline__ float combine_first(float loc, float gate, float a1, float s1) {
+  return __fmaf_rn(epi_sigmoid(gate), __fmul_rn(a1, s1), loc);
+}
+__device__ __forceinline__ float combine_second(float v, float a2, float s2) { return __fmaf_rn(a2, s2, v); }
 
 __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
   const int per_group = p.group_m * p.num_n_tiles;
@@ -790,8 +797,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int e = 0; e < 4; ++e) {
               const float2 fl = __bfloat1622float2(hl[e]), fg = __bfloat1622float2(hg[e]);
               const int jj = 8 * j + 2 * e;
-              v[jj] = fl.x + epi_sigmoid(fg.x) * (acc_to_f(r[jj]) * s1);
-              v[jj + 1] = fl.y + epi_sigmoid(fg.y) * (acc_to_f(r[jj + 1]) * s1);
+              v[jj] = combine_first(fl.x, fg.x, acc_to_f(r[jj]), s1);
+              v[jj + 1] = combine_first(fl.y, fg.y, acc_to_f(r[jj + 1]), s1);
             }
           }
           // every lane has consumed its slot values (register dependencies above): refill the
@@ -800,7 +807,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (un < total && epi_ok) issue_in(mtn, ntn, cc);
           tmem_ld32(tbase + BN, r);  // acc2 (ent_proj)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += acc_to_f(r[j]) * s2;
+          for (int j = 0; j < 32; ++j) v[j] = combine_second(v[j], acc_to_f(r[j]), s2);
           // the output slot of this chunk was last used DCH store groups ago
           if (lane == 0) bulk_wait_read<DCH - 1>();
           __syncwarp();
@@ -851,7 +858,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int jj = 16 * h + j;
-                v[jj] = loc[j] + epi_sigmoid(gt[j]) * (acc_to_f(r1[jj]) * s1) + acc_to_f(r2[jj]) * s2;
+                v[jj] = combine_second(combine_first(loc[j], gt[j], acc_to_f(r1[jj]), s1), acc_to_f(r2[jj]), s2);
               }
             }
           }
@@ -1028,6 +1035,24 @@ __global__ void k_splitk_finalize(const int32_t *ws, int splits, int M, int N, c
     if (out) store_f(out, out_dtype, (int64_t)m * ldo + n, (float)a * xs * wd);
     if (acc_out) acc_out[(int64_t)m * ld_acc + n] = a;
   }
+}
+
+// The dual-accumulator combine epilogue on int32 accumulators summed elsewhere (tensor-parallel
+// row splits of state_proj / ent_proj): out = local + sigmoid(gate) * acc1 * (inv1 * deq1)
+// + acc2 * (inv2 * deq2), the arithmetic of the GEMM's epilogue.
+__global__ void k_combine_acc(const int32_t *acc1, const int32_t *acc2, int64_t lda, int M, int N,
+                              const float *inv1, const float *inv2, const float *deq1, const float *deq2,
+                              const void *proj, int proj_dtype, int64_t ldp, int c_local, int c_gate, void *out,
+                              int out_dtype, int64_t ldo) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)M * N) return;
+  const int m = (int)(i / N), n = (int)(i - (int64_t)m * N);
+  const float s1 = inv1[m] * deq1[0], s2 = inv2[m] * deq2[0];
+  const float loc = load_f(proj, proj_dtype, (int64_t)m * ldp + c_local + n);
+  const float gate = load_f(proj, proj_dtype, (int64_t)m * ldp + c_gate + n);
+  const float v = combine_second(combine_first(loc, gate, acc_to_f((uint32_t)acc1[(int64_t)m * lda + n]), s1),
+                                 acc_to_f((uint32_t)acc2[(int64_t)m * lda + n]), s2);
+  store_f(out, out_dtype, (int64_t)m * ldo + n, v);
 }
 
 // ------------------------------------------------------------ host side
@@ -1428,4 +1453,20 @@ extern "C" int tesm_b200_gemm_bf16(const void *a, int64_t lda, const void *b, in
   if (M > 128)  // 256-row tiles on CTA pairs
     return tc::launch<256, false, 1, true, true>(A, lda * 2, B, ldb * 2, p, st);
   return tc::launch<256, false, 1, false, true>(A, lda * 2, B, ldb * 2, p, st);
+}
+
+extern "C" int tesm_b200_combine_acc(const int32_t *acc1, const int32_t *acc2, int64_t ld_acc, int64_t M, int64_t N,
+                                     const float *inv1, const float *inv2, const float *deq1, const float *deq2,
+                                     const void *proj, int proj_dtype, int64_t ldp, int64_t c_local, int64_t c_gate,
+                                     void *out, int out_dtype, int64_t ldo, tesm_stream_t stream) {
+  if (M == 0) return TESM_OK;
+  TESM_REQUIRE(acc1 && acc2 && inv1 && inv2 && deq1 && deq2 && proj && out, "combine_acc: null pointer");
+  TESM_REQUIRE(M > 0 && N > 0 && ld_acc >= N && ldo >= N && M * N < (1ll << 40), "combine_acc: bad shape");
+  if (proj_dtype != TESM_F32 && proj_dtype != TESM_BF16) return fail(TESM_EDTYPE, "combine_acc: proj dtype");
+  if (out_dtype != TESM_F32 && out_dtype != TESM_BF16) return fail(TESM_EDTYPE, "combine_acc: out dtype");
+  const int64_t n = M * N;
+  tc::k_combine_acc<<<(unsigned)ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      acc1, acc2, ld_acc, (int)M, (int)N, inv1, inv2, deq1, deq2, proj, proj_dtype, ldp, (int)c_local, (int)c_gate,
+      out, out_dtype, ldo);
+  return check_launch("combine_acc");
 }

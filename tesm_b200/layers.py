@@ -192,12 +192,19 @@ def _out_proj(mod, y, act_dtype):
 
 
 def _tail(mod, proj, M, C, Rc, tanh_e, chg, act_dtype):
-    """state_proj / ent_proj, output combine and out_proj (tesm.py:1255-1261)."""
+    """state_proj / ent_proj, output combine and out_proj (tesm.py:1255-1261; MIMO
+    tesm_mimo.py:1040-1052): the int8 codes of tanh(ent) and ent - s side by side, then one
+    dual-accumulator GEMM with the combine epilogue (as the SISO window path does)."""
     Dm = mod.d_model
-    sp = linear(mod.state_proj, tanh_e, act_dtype)
-    ep = linear(mod.ent_proj, chg, act_dtype)
-    y = torch.empty(M, Dm, device=proj.device, dtype=act_dtype)
-    ops.combine(proj, M, Dm, C, Rc, sp, ep, y)
+    dev = proj.device
+    tern, deq1, deq2, Dp = combine_weight(mod)
+    codes = torch.empty(M, 2 * Dp, device=dev, dtype=torch.int8)
+    inv1 = torch.empty(M, device=dev, dtype=torch.float32)
+    inv2 = torch.empty(M, device=dev, dtype=torch.float32)
+    ops.quant_act_into(tanh_e.reshape(M, C), mod.state_proj.bit_eps, codes, 0, inv1)
+    ops.quant_act_into(chg.reshape(M, C), mod.ent_proj.bit_eps, codes, Dp, inv2)
+    y = torch.empty(M, Dm, device=dev, dtype=act_dtype)
+    ops.gemm_combine(codes, Dp, inv1, inv2, tern, deq1, deq2, proj, 0, Dm + 3 * C, M, Dm, y)
     return _out_proj(mod, y, act_dtype)
 
 

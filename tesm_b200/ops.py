@@ -135,6 +135,15 @@ def quant_act(x2d: torch.Tensor, eps: float, layout: int):
     return codes, inv, rowsum
 
 
+def quant_act_into(x2d: torch.Tensor, eps: float, codes: torch.Tensor, col0: int, inv: torch.Tensor):
+    """Row-major int8 codes of x written into columns [col0, col0 + K) of ``codes`` (16-byte
+    aligned rows and col0), 1/s into ``inv``."""
+    assert x2d.is_cuda and x2d.dim() == 2 and x2d.stride(1) == 1 and col0 % 16 == 0
+    M, K = x2d.shape
+    _lib.call("tesm_b200_quant_act", x2d.data_ptr(), dtype_code(x2d.dtype), M, K, x2d.stride(0), float(eps),
+              codes.data_ptr() + col0, codes.stride(0), LAYOUT_ROWMAJOR, inv.data_ptr(), None, _stream())
+
+
 def gemv(codes, inv, rowsum, pw: PackedWeight, M: int, out_dtype: torch.dtype, out=None, acc=False):
     dev = codes.device
     out = out if out is not None else torch.empty(M, pw.N, device=dev, dtype=out_dtype)
@@ -206,6 +215,15 @@ def acc_scale(acc, inv, pw: PackedWeight, out_dtype, out=None):
     out = out if out is not None else torch.empty(M, N, device=acc.device, dtype=out_dtype)
     _lib.call("tesm_b200_acc_scale", acc.data_ptr(), M, N, inv.data_ptr(), pw.deq.data_ptr(), int(pw.per_row),
               out.data_ptr(), dtype_code(out.dtype), out.stride(0), _stream())
+    return out
+
+
+def combine_acc(acc1, acc2, inv1, inv2, deq1, deq2, proj, c_local, c_gate, out):
+    """The dual-accumulator combine epilogue on summed int32 accumulators (bit for bit)."""
+    M, N = out.shape
+    _lib.call("tesm_b200_combine_acc", acc1.data_ptr(), acc2.data_ptr(), acc1.stride(0), M, N, inv1.data_ptr(),
+              inv2.data_ptr(), deq1.data_ptr(), deq2.data_ptr(), proj.data_ptr(), dtype_code(proj.dtype),
+              proj.stride(0), c_local, c_gate, out.data_ptr(), dtype_code(out.dtype), out.stride(0), _stream())
     return out
 
 

@@ -399,25 +399,28 @@ def mimo_shards(mixer, tp: TPGroup):
     return sh
 
 
-def _row_parallel_linear(x_r, pw, eps, act_dtype, tp: TPGroup):
-    """A BitLinear whose input columns are split over the ranks: global row maxima, local codes,
-    int32 partials summed, scaled once."""
+def _row_parallel_acc(x_r, pw, eps, tp: TPGroup):
+    """int32 accumulators of a BitLinear whose input columns are split over the ranks (global row
+    maxima, local codes, partials summed) and the per-row 1/s."""
     amax = _all_reduce(ops.row_absmax(x_r), "max", tp)
     q = ops.quant_act_amax(x_r, eps, amax)
     acc = torch.empty(x_r.shape[0], pw.N, device=x_r.device, dtype=torch.int32)
     ops.gemm_acc(q.codes, q.inv, pw, x_r.shape[0], acc)
     _all_reduce(acc, "sum", tp)
-    return ops.acc_scale(acc, q.inv, pw, act_dtype)
+    return acc, q.inv
 
 
 def _mimo_tail(mod, sh, proj_r, tanh_r, chg_r, M, act_dtype, tp: TPGroup):
+    """state_proj / ent_proj row-parallel over the rank's heads, then the combine epilogue of
+    the one-device dual-accumulator GEMM on the summed accumulators (bit-identical to it)."""
     from . import layers
-    sp = _row_parallel_linear(tanh_r, sh["sp_pw"], mod.state_proj.bit_eps, act_dtype, tp)
-    ep = _row_parallel_linear(chg_r, sh["ep_pw"], mod.ent_proj.bit_eps, act_dtype, tp)
+    acc1, inv1 = _row_parallel_acc(tanh_r, sh["sp_pw"], mod.state_proj.bit_eps, tp)
+    acc2, inv2 = _row_parallel_acc(chg_r, sh["ep_pw"], mod.ent_proj.bit_eps, tp)
     h0, h1 = sh["h"]
     Dm = mod.d_model
     y = torch.empty(M, Dm, device=proj_r.device, dtype=act_dtype)
-    ops.combine(proj_r, M, Dm, (h1 - h0) * mod.d_state, (h1 - h0) * mod.ent_rank, sp, ep, y)
+    ops.combine_acc(acc1, acc2, inv1, inv2, sh["sp_pw"].deq, sh["ep_pw"].deq, proj_r, 0,
+                    Dm + 3 * (h1 - h0) * mod.d_state, y)
     return layers.linear(mod.out_proj, y, act_dtype)
 
 

@@ -218,6 +218,11 @@ def test_gemm_combine_epilogue(ops, dtype, MNK):
     tol = 1e-5 if dtype == "float32" else 8e-3
     err = ((got - ref).abs() / (ref.abs() + 1.0)).max().item()
     assert err <= tol, err
+    # the same epilogue on accumulators summed elsewhere (tensor-parallel MIMO tail): bit for bit
+    out2 = torch.empty_like(out)
+    ops.combine_acc(a1.to(torch.int32).cuda(), a2.to(torch.int32).cuda(), inv1.cuda(), inv2.cuda(), deq1.cuda(),
+                    deq2.cuda(), proj.cuda(), c_local, c_gate, out2)
+    assert torch.equal(out2, out)
 
 
 @pytest.mark.parametrize("MNK", [(1, 32000, 4096), (32, 32000, 4096), (256, 32000, 4096), (300, 1000, 520),
