@@ -1339,6 +1339,13 @@ extern "C" int tesm_b200_gemm_i8_combine(const int8_t *codes, int64_t ld_codes, 
   p.proj_vec = ((uintptr_t)proj % 16 == 0) && ((ldp * psz) % 16 == 0) && ((c_local * psz) % 16 == 0) &&
                ((c_gate * psz) % 16 == 0);
   p.dual_tma = p.proj_vec && p.vec_store && proj_dtype == TESM_BF16 && out_dtype == TESM_BF16;
+  // decode batches: 64-column tiles double the CTAs when 128-column tiles leave SMs idle
+  static const int narrow = [] {
+    const char *e = getenv("TESM_COMBINE_NARROW");  // tuning override: 0 = always 128 columns
+    return e ? atoi(e) : 1;
+  }();
+  if (narrow && ceil_div(M, 128) * ceil_div(N, 128) < sm_count())
+    return tc::launch<64, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
   return tc::launch<128, true>(codes, ld_codes, tern, ld_tern, p, (cudaStream_t)stream);
 }
 
