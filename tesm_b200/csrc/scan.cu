@@ -412,15 +412,24 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
   }
   float a0[TT], a1[TT], u0[TT], u1[TT];
   float A0 = 1.f, A1 = 1.f, U0 = 0.f, U1 = 0.f;
-  float P0 = 1.f, P1 = 1.f;  // running products since the last reference chunk start (TT % cs == 0)
-  const int cs = p.cs;
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     a0[t] = decay_gate(bf16lo(rd[t]), nb0);
     a1[t] = decay_gate(bf16hi(rd[t]), nb1);
+    A0 *= a0[t];
+    A1 *= a1[t];
+  }
+  // The reference's chunk clamp u_t * min(1, P_t / 1e-12), P_t the running decay product since
+  // the last multiple of cs (TT % cs == 0).  P_t >= A (the thread's whole product: factors <= 1),
+  // so when A >= 2e-12 every factor min(1, P_t * 1e12) is exactly 1 and the clamp is skipped.
+  const int cs = p.cs;
+  const bool clamp = cs > 0 && __any_sync(0xffffffffu, A0 < 2e-12f || A1 < 2e-12f);
+  float P0 = 1.f, P1 = 1.f;
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
     u0[t] = write_value(bf16lo(rw[t]), bf16lo(rv[t]));
     u1[t] = write_value(bf16hi(rw[t]), bf16hi(rv[t]));
-    if (cs > 0) {
+    if (clamp) {
       if (t % cs == 0) P0 = P1 = 1.f;
       P0 *= fmaxf(a0[t], 1e-12f);
       P1 *= fmaxf(a1[t], 1e-12f);
@@ -429,8 +438,6 @@ __global__ void __launch_bounds__(128 * G) k_scan_siso_reg(ScanParams p) {
     }
     U0 = fmaf(a0[t], U0, u0[t]);
     U1 = fmaf(a1[t], U1, u1[t]);
-    A0 *= a0[t];
-    A1 *= a1[t];
   }
   // combine the time groups: exclusive map E of groups 0..g-1, total map of the chunk
   s_map[g][cp] = make_float4(A0, A1, U0, U1);
