@@ -12,9 +12,6 @@
 //                reads TMEM lanes 32*(w%4).. and half of the tile's columns.
 // Every mbarrier wait is bounded; a wait that gives up sets the sticky device status
 // (TESM_ETIMEOUT) and the CTA drains and exits instead of hanging.
-#include <algorithm>
-#include <vector>
-#include <cstdio>
 #include "rowio.cuh"
 
 #include <cuda.h>
@@ -66,7 +63,6 @@ struct Params {
   // until every split has counted, adds the other slices to its own chunks (exact integers)
   // and runs the epilogue on them; a second count resets the counter to zero for the next call.
   int splits, n_full;
-  unsigned long long *trace;  // optional per-CTA globaltimer stamps (32 per CTA; TESM_GEMM_TRACE)
   int pdl_late;  // 1: signal dependents when the epilogue starts the CTA's last unit (else at entry)
   int32_t *ws;      // caller scratch: kCounterInts counters (zero between calls), then the slices
   int64_t ws_bytes;
@@ -76,14 +72,6 @@ struct Params {
 
 constexpr int kCounterInts = 4096;  // 16 KB of tile counters at the start of the split-K scratch
 
-// diagnostic phase stamps (globaltimer) of one launch, written only when p.trace is set
-__device__ __forceinline__ void trace_at(const Params &p, int slot) {
-  if (p.trace) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    p.trace[blockIdx.x * 32 + slot] = t;
-  }
-}
 
 // work unit u -> (tile, split, number of splits of that tile)
 __device__ __forceinline__ void unit_info(const Params &p, int u, int &t, int &sp, int &ns) {
@@ -363,7 +351,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   // split-K meeting words of the epilogue warps (see the split-K branch of the epilogue)
   __shared__ int s_last, s_arrive, s_decided;
-  if (threadIdx.x == 0) trace_at(p, 0);
   if (threadIdx.x == 0) {
     s_last = s_arrive = s_decided = 0;
     for (int i = 0; i < NST; ++i) {
@@ -404,7 +391,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // producer's first weight-tile requests (constant data) go out before its completion
   if (threadIdx.x == 0 && !p.pdl_late) pdl_trigger();
   if (warp != 0) pdl_wait();
-  if (threadIdx.x == 0) trace_at(p, 1);
 
   const int total = p.n_full + (p.num_m_tiles * p.num_n_tiles - p.n_full) * p.splits;
   const int nk_all = p.num_k_blocks;
@@ -484,7 +470,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          if (it == 0) trace_at(p, 2);
           fence_after();
           const uint64_t adesc = smem_desc_sw128(sA + stage * A_BYTES);
           const uint64_t bdesc = smem_desc_sw128(sB + stage * B_BYTES);
@@ -517,7 +502,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mma_commit_pair(&tfull[buf]);
           else
             mma_commit(&tfull[buf]);
-          if (tile_i < 3) trace_at(p, 3 + tile_i);
         }
       }
     }
@@ -557,7 +541,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&tempty[b]);
     };
     for (int u = ustart; u < total; u += ustride, ++tile_i) {
-      if (warp == 2 && lane == 0 && tile_i > 0 && tile_i < 4) trace_at(p, 9 + tile_i - 1);
       int mt, nt, t_u, sp_u, ns_u;
       unit_info(p, u, t_u, sp_u, ns_u);
       tile_coords(p, t_u, mt, nt);
@@ -593,7 +576,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!mbar_wait(&tfull[buf], use & 1)) break;
-      if (warp == 2 && lane == 0 && tile_i < 3) trace_at(p, 6 + tile_i);
       if (p.pdl_late && warp == 2 && lane == 0 && u + ustride >= total) pdl_trigger();
       fence_after();
       // split-K: the other splits' partial sums of this tile are added to the accumulators read
@@ -705,7 +687,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // instead of a named barrier: a warp that gave up on an earlier wait cannot leave the
         // others blocked.
         __syncwarp();
-        if (warp == 2 && lane == 0) trace_at(p, 13);
         ++nsplit;
         int ok = 0;
         if (lane == 0) red_release_cta(&s_arrive, 1);
@@ -750,7 +731,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           ok = d >= nsplit ? *(volatile int *)&s_last : 0;
         }
-        if (warp == 2 && lane == 0) trace_at(p, 14);
         fix = __shfl_sync(0xffffffffu, ok, 0) != 0;
         if (!fix) {
           fence_before();
@@ -884,16 +864,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t rg[32], ru[32];
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
           if (fix && c % ns_u != sp_u) continue;  // split-K: another split finalises this chunk
-          if (warp == 2 && lane == 0) trace_at(p, 15);
           tmem_ld32(tbase + c * 32, rg);
           tmem_ld32(tbase + 128 + c * 32, ru);
-          if (warp == 2 && lane == 0) trace_at(p, 16);
           const int ng = nt * BN + c * 32;    // weight row of the first gate column
           const int no = nt * 128 + c * 32;   // output column
           if (ng >= p.N) continue;
           acc_fix(rg, ng);
           acc_fix(ru, ng + 128);
-          if (warp == 2 && lane == 0) trace_at(p, 17);
           float v[32];
           // per-row dequantisation factors of the chunk's 32 gate and 32 up rows: one coalesced
           // load each, handed to the lanes by shuffles
@@ -910,11 +887,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const float u = au * xs * __shfl_sync(0xffffffffu, du, j);
             v[j] = __fdividef(g, 1.f + __expf(-g)) * u;
           }
-          if (warp == 2 && lane == 0) trace_at(p, 18);
           const int nout = p.N / 2;
           if (p.vec_store && no + 32 <= nout) {
             stage_store(v, row - lane, no);
-            if (warp == 2 && lane == 0) trace_at(p, 19);
             continue;
           }
           if (!row_ok) continue;
@@ -932,13 +907,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (fix && c % ns_u != sp_u) continue;  // split-K: another split finalises this chunk
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + sub * BN + c * 32;
-        if (warp == 2 && lane == 0) trace_at(p, 15);
         tmem_ld32(taddr, r);
-        if (warp == 2 && lane == 0) trace_at(p, 16);
         const int n0 = nt * BN + c * 32;
         if (n0 >= p.N) continue;
         acc_fix(r, n0);
-        if (warp == 2 && lane == 0) trace_at(p, 17);
         float v[32];
         const int ci = c - c_lo;
         const float wdl = p.per_row ? (ci == 0 ? w4[0] : ci == 1 ? w4[1] : ci == 2 ? w4[2] : w4[3]) : wd0;
@@ -948,10 +920,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const float wd = p.per_row ? __shfl_sync(0xffffffffu, wdl, j) : wd0;
           v[j] = BF ? __uint_as_float(r[j]) : (small_acc ? acc_to_f(r[j]) : (float)(int32_t)r[j]) * xs * wd;
         }
-        if (warp == 2 && lane == 0) trace_at(p, 18);
         if (p.out && p.vec_store && n0 + 32 <= p.N && !p.acc_out) {
           stage_store(v, row - lane, n0);
-          if (warp == 2 && lane == 0) trace_at(p, 19);
           continue;
         }
         if (!row_ok) continue;
@@ -987,7 +957,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     // TMA stores still reading this warp's output slots must finish before the CTA exits
     if (dual_tma && lane == 0) bulk_wait_all();
-    if (warp == 2 && lane == 0) trace_at(p, 12);
   }
 
   fence_before();
@@ -1101,29 +1070,6 @@ static int make_map_bf16_32(CUtensorMap *map, const void *ptr, int64_t inner, in
   return TESM_OK;
 }
 
-// prints, per stamp slot, the min / median / max over CTAs in microseconds after the first CTA start
-static void dump_trace(unsigned long long *tr, int ctas, cudaStream_t st, int M, int N, int K, int total,
-                       int splits, int n_full) {
-  std::vector<unsigned long long> h((size_t)ctas * 32);
-  cudaStreamSynchronize(st);
-  cudaMemcpy(h.data(), tr, h.size() * 8, cudaMemcpyDeviceToHost);
-  cudaFree(tr);
-  unsigned long long t0 = ~0ull;
-  for (int c = 0; c < ctas; ++c)
-    if (h[c * 32] && h[c * 32] < t0) t0 = h[c * 32];
-  fprintf(stderr, "gemm trace M=%d N=%d K=%d ctas=%d units=%d splits=%d n_full=%d\n", M, N, K, ctas, total, splits,
-          n_full);
-  for (int s = 0; s < 32; ++s) {
-    std::vector<double> v;
-    for (int c = 0; c < ctas; ++c)
-      if (h[c * 32 + s]) v.push_back((h[c * 32 + s] - t0) * 1e-3);
-    if (v.empty()) continue;
-    std::sort(v.begin(), v.end());
-    fprintf(stderr, "  slot %2d n=%3zu min %7.2f med %7.2f max %7.2f us\n", s, v.size(), v[0], v[v.size() / 2],
-            v.back());
-  }
-}
-
 template <int BN, bool DUAL = false, int MT = 1, bool PAIR = false, bool BF = false>
 static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Params p, cudaStream_t st) {
   CUtensorMap ma, mb, ml, mg, mo;
@@ -1231,19 +1177,7 @@ static int launch(const int8_t *A, int64_t lda, const int8_t *B, int64_t ldb, Pa
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     const int clusters = total < max_clusters ? total : max_clusters;
     cfg.gridDim = dim3(2 * clusters);
-    static const int trace_at_call = [] {
-      const char *e = getenv("TESM_GEMM_TRACE");
-      return e ? atoi(e) : 0;
-    }();
-    static int calls = 0;
-    unsigned long long *tr = nullptr;
-    if (trace_at_call && ++calls == trace_at_call) {
-      cudaMalloc(&tr, (size_t)cfg.gridDim.x * 32 * 8);
-      cudaMemsetAsync(tr, 0, (size_t)cfg.gridDim.x * 32 * 8, st);
-      p.trace = tr;
-    }
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, ml, mg, mo, p);
-    if (tr) dump_trace(tr, cfg.gridDim.x, st, p.M, p.N, p.K, total, p.splits, p.n_full);
     if (e != cudaSuccess) return fail(TESM_ELAUNCH, std::string("gemm_i8 (CTA pairs): ") + cudaGetErrorString(e));
     return check_launch("gemm_i8 (CTA pairs)");
   }
