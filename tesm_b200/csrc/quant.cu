@@ -227,6 +227,58 @@ __global__ void k_quant_act(const void *__restrict__ x, int dtype, int64_t K, in
   }
 }
 
+// Short rows (K <= 1024): one warp per row, 8 rows per block, warp-shuffle reductions (a
+// 32-thread block per row of a few hundred elements is bound by block scheduling).
+__global__ void k_quant_act_warp(const void *__restrict__ x, int dtype, int64_t M, int64_t K, int64_t ldx, float eps,
+                                 int8_t *__restrict__ codes, int64_t ld_codes, int layout, int64_t groups_out,
+                                 float *__restrict__ inv_scale, int32_t *__restrict__ rowsum, int vec,
+                                 const float *__restrict__ amax_in) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int64_t groups_in = (K + 15) / 16;
+  const int esz = dtype == TESM_BF16 ? 2 : 4;
+  const void *xrow = reinterpret_cast<const uint8_t *>(x) + row * ldx * esz;
+  float v[2][16];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int64_t g = lane + 32 * j;
+    if (g < groups_in) {
+      load16(xrow, dtype, g * 16, K, vec, v[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[j][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[j][e]));
+  }
+  amax = warp_max(amax);
+  if (amax_in) amax = amax_in[row];
+  const float s = act_scale(amax, eps, dtype);
+  if (lane == 0) inv_scale[row] = __frcp_rn(s);
+  int csum = 0;
+  int8_t *crow = codes + row * ld_codes;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int64_t g = lane + 32 * j;
+    if (g >= groups_out) continue;
+    int c[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      c[e] = act_code(v[j][e], s, dtype);
+      csum += c[e];
+    }
+    store_codes16(crow, g, layout, c);
+  }
+  if (rowsum) {
+    csum = warp_sum_i(csum);
+    if (lane == 0) rowsum[row] = csum;
+  }
+}
+
 // max |x| of each row (tensor-parallel shards: reduced across ranks, then quantised with it).
 __global__ void k_row_absmax(const void *__restrict__ x, int dtype, int64_t K, int64_t ldx, int vec,
                              float *__restrict__ amax_out) {
@@ -308,6 +360,9 @@ static int quant_act_impl(const void *x, int dtype, int64_t M, int64_t K, int64_
   TESM_REQUIRE(threads <= 1024, "quant_act: K too large (max 65536)");
   const int esz = dtype == TESM_BF16 ? 2 : 4;
   const int vec = (K % 16 == 0) && ((uintptr_t)x % 16 == 0) && ((ldx * esz) % 16 == 0);
+  if (M >= 1024 && groups_out <= 64)  // many short rows: one warp per row
+    return launch_k("quant_act", k_quant_act_warp, dim3((unsigned)ceil_div(M, 8)), dim3(256), 0, (cudaStream_t)stream,
+                    x, dtype, M, K, ldx, eps, codes, ld_codes, layout, groups_out, inv_scale, rowsum, vec, amax);
   if (dtype == TESM_BF16 && vec && layout == TESM_LAYOUT_ROWMAJOR)
     return launch_k("quant_act", gpt == 1 ? k_quant_act_bf16<1> : k_quant_act_bf16<kQuantGPT>, dim3((unsigned)M),
                     dim3((unsigned)threads), 0, (cudaStream_t)stream, reinterpret_cast<const __nv_bfloat16 *>(x), K,

@@ -66,7 +66,7 @@ def test_golden_codes(ops, c):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
-@pytest.mark.parametrize("MK", [(1, 4096), (7, 37), (33, 11008), (300, 96)])
+@pytest.mark.parametrize("MK", [(1, 4096), (7, 37), (33, 11008), (300, 96), (2048, 256), (1500, 1000)])
 def test_quant_codes_bit_exact(ops, dtype, MK):
     M, K = MK
     x = (randn((M, K), 7) * 3).to(DT[dtype])
