@@ -208,8 +208,8 @@ extern "C" int tesm_b200_add_rmsnorm_quant(const void *x, int xdtype, const floa
   // few rows (decode): one 16-element group per thread, so each row's latency chain is short
   static const int gpt_big = [] {
     const char *e = getenv("TESM_ARQ_GPT");  // tuning override: 16-element groups per thread, many rows
-    const int v = e ? atoi(e) : 2;  // 2: 56 registers, 0.76 of HBM at 16384 x 4096 (4: 96, 0.70)
-    return v == 4 ? 4 : 2;
+    const int v = e ? atoi(e) : 2;  // 2: 56 registers, 0.76 of HBM at 16384 x 4096 (4: 0.70, 1: 0.74)
+    return v == 4 ? 4 : v == 1 ? 1 : 2;
   }();
   const int gpt = M < 1024 && groups_out <= 1024 ? 1 : gpt_big;
   int64_t threads = round_up(ceil_div(groups_out, gpt), 32);
