@@ -284,6 +284,13 @@ def siso_prefill(mod, u, cross_layer_state=None, prev_state=None, cache=None, ac
     return out.view(B, L, Dm), fin64
 
 
+def _state_out(cache):
+    """The state a decode step returns: a snapshot (the reference returns each step's new fp64
+    state as its own tensor, tesm.py:1385-1400, while the cache here is updated in place), or
+    None for callers that discard it (decode graphs, generate)."""
+    return None if cache.get("_b200_no_state_out") else cache["state"].clone()
+
+
 def siso_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=None):
     """``TESM_SISO._forward_incremental`` (tesm.py:1274-1400): one token per sequence."""
     B = shape[0] if shape is not None else u.shape[0]
@@ -320,7 +327,7 @@ def siso_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     ops.gemm_combine(codes, Dp, inv1, inv2, tern, deq1, deq2, proj, 0, Dm + 3 * D, B, Dm, y)
     out = _out_proj(mod, y, act_dtype)
     mod._last_cross_layer_state = new_state
-    return out.view(B, 1, Dm), cache["state"].clone()
+    return out.view(B, 1, Dm), _state_out(cache)
 
 
 # ------------------------------------------------------------------ MIMO layer
@@ -396,7 +403,7 @@ def mimo_decode(mod, u, cache, cross_layer_state=None, act_dtype=None, shape=Non
     _advance_host(cache, W)
     out = _tail(mod, proj, B, C, H * R, tanh_e, chg, act_dtype)
     mod._last_cross_layer_state = new_state.view(B, H, D)
-    return out.view(B, 1, Dm), cache["state"].clone()
+    return out.view(B, 1, Dm), _state_out(cache)
 
 
 def _is_mimo(mixer):
@@ -659,11 +666,17 @@ class DecodeGraph:
         torch.cuda.synchronize()
         hosts = [(c["seq_pos"], c["cache_idx"], c["_ctl_host"]) for c in self.caches.values()]
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            out, _ = self.lm(self.ids, inference_params=self.ip)
-            self.logits = out.logits
-            if greedy:
-                self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1, keepdim=True))
+        for c in self.caches.values():  # the replayed steps return no per-layer state snapshots
+            c["_b200_no_state_out"] = True
+        try:
+            with torch.cuda.graph(self.graph):
+                out, _ = self.lm(self.ids, inference_params=self.ip)
+                self.logits = out.logits
+                if greedy:
+                    self.ids.copy_(out.logits[:, -1, :].argmax(dim=-1, keepdim=True))
+        finally:
+            for c in self.caches.values():
+                c.pop("_b200_no_state_out", None)
         for c, h in zip(self.caches.values(), hosts):  # capture ran no kernel; restore the mirrors
             c["seq_pos"], c["cache_idx"], c["_ctl_host"] = h
 
@@ -731,6 +744,8 @@ def generate(lm, input_ids, max_new_tokens=64, temperature=1.0, top_k=0, use_cac
                 graph = DecodeGraph(lm, ip, nxt, greedy=False)
             logits = graph.step_logits(nxt)
         elif use_cache:
+            for c in ip["state_cache"].values():  # generate discards the per-layer states
+                c["_b200_no_state_out"] = True
             out, _ = lm(nxt, inference_params=ip)
             logits = out.logits[:, -1, :]
         else:

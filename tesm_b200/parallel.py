@@ -343,6 +343,8 @@ def siso_decode_tp(mod, q: ops.QuantAct, B, cache, cross_layer_state, act_dtype,
     layers._advance_host(cache, W)
     out = _combine_out(mod, sh, proj, tanh_e, chg, B, act_dtype, tp)
     mod._last_cross_layer_state = _gather_cols(new_state, tp)
+    if cache.get("_b200_no_state_out"):
+        return out.view(B, 1, Dm), None
     return out.view(B, 1, Dm), _gather_cols(tc["state"], tp)
 
 
@@ -497,4 +499,6 @@ def mimo_decode_tp(mod, q: ops.QuantAct, B, cache, cross_layer_state, act_dtype,
     layers._advance_host(cache, W)
     out = _mimo_tail(mod, sh, proj, tanh_e, chg, B, act_dtype, tp)
     mod._last_cross_layer_state = _gather_cols(new_state, tp).view(B, mod.n_heads, D)
+    if cache.get("_b200_no_state_out"):
+        return out.view(B, 1, Dm), None
     return out.view(B, 1, Dm), _gather_cols(tc["state"].view(B, -1), tp).view(B, mod.n_heads, D)
