@@ -140,3 +140,57 @@ def _mixer_worker(rank, world, port, out_dir):
 def test_channel_parallel_mixer_decomposition(tmp_path):
     mp.spawn(_mixer_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
     assert [open(tmp_path / f"m{r}").read() for r in range(2)] == ["1", "1"]
+
+
+def _mimo_head_worker(rank, world, port, out_dir):
+    """The head-parallel MIMO layer tail on the oracle (config 4's (b, h) split): each rank owns
+    a range of heads, state_proj / ent_proj run row-parallel over those heads' channels (MAX of
+    row maxima, SUM of int32 partials), then the combine and out_proj -- against the oracle's
+    whole layer (tesm_mimo.py:914-1062), exactly."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rng = np.random.default_rng(13)
+    B, L, Dm, H, D, R, RM, W = 2, 24, 48, 4, 8, 8, 2, 4
+    C = H * D
+    eps = 1e-5
+    x = rng.standard_normal((B, L, Dm)).astype(np.float32)
+    P = {"in_proj.weight": (rng.standard_normal((2 * Dm + 3 * C + 2 * H * R, Dm)) * 0.05).astype(np.float32),
+         "state_proj.weight": (rng.standard_normal((Dm, C)) * 0.05).astype(np.float32),
+         "ent_proj.weight": (rng.standard_normal((Dm, C)) * 0.05).astype(np.float32),
+         "out_proj.weight": (rng.standard_normal((Dm, Dm)) * 0.05).astype(np.float32),
+         "decay_bias": (np.full((H, D), 2.0) + rng.standard_normal((H, D)) * 0.3).astype(np.float32),
+         "mimo_x": (1.0 / RM + rng.standard_normal((H, RM, D)) * 0.05).astype(np.float32),
+         "mimo_o": (1.0 / RM + rng.standard_normal((H, RM, D)) * 0.05).astype(np.float32),
+         "local_entanglement_bias": (rng.standard_normal((H, W)) * 0.3).astype(np.float32)}
+    cfg = dict(d_model=Dm, d_state=D, ent_rank=R, n_heads=H, mimo_rank=RM, entanglement_window=W,
+               entanglement_threshold=0.1, entanglement_scale=0.2, bit_eps=eps, rope_base=1e4)
+    out_ref, _, _, det = O.mimo_forward(P, cfg, x, details=True)
+    h0, h1 = shard_range(H, world, rank, 1)
+    c0, c1 = h0 * D, h1 * D
+
+    def row_parallel(xfull, w):
+        xr = np.ascontiguousarray(xfull[..., c0:c1])
+        amax = torch.from_numpy(np.abs(xr).max(-1))
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+        c, s = O.quant_act(xr, eps, amax=amax.numpy())
+        t, _, deq = O.ternary_weight(w, eps)
+        acc = torch.from_numpy(O.int_gemm(c, t[:, c0:c1]).astype(np.int64))
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+        return (acc.numpy().astype(np.float64) * (1.0 / s.astype(np.float64))[..., None]
+                * np.float64(deq.reshape(-1)[0])).astype(np.float32)
+
+    sp = row_parallel(np.tanh(det["ent"].reshape(B, L, C)), P["state_proj.weight"])
+    ep = row_parallel(det["chg"].reshape(B, L, C), P["ent_proj.weight"])
+    proj = O.bitlinear(x, P["in_proj.weight"], eps)
+    local, gate = proj[..., :Dm], O.sigmoid(proj[..., Dm + 3 * C:2 * Dm + 3 * C])
+    y = (local + gate * sp + ep).astype(np.float32)
+    out = O.bitlinear(y, P["out_proj.weight"], eps)
+    ok = np.array_equal(out, out_ref)
+    with open(os.path.join(out_dir, f"h{rank}"), "w") as f:
+        f.write("1" if ok else f"0 {np.abs(out - out_ref).max()}")
+    dist.destroy_process_group()
+
+
+def test_head_parallel_mimo_tail_decomposition(tmp_path):
+    mp.spawn(_mimo_head_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    assert [open(tmp_path / f"h{r}").read() for r in range(2)] == ["1", "1"]
